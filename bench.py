@@ -1,0 +1,436 @@
+"""Benchmark: seconds per CFG denoising step of the Qwen-Image MMDiT at 1328x1328.
+
+Workload ("C4"): 166x166 latent -> 6889 image
+tokens + 256 text tokens, 60 double-stream blocks, W8A8 INT8 weights in
+quantize.cu's format produced from seeded N(0, 0.02^2) BF16 weights, CFG
+scale 4.0, flow-matching Euler with fixed shift 3.0 over 50 sigmas.  One step
+= the cond and uncond forwards (batched: nb = 2 in one pass) + the
+norm-preserving CFG combine and Euler update.  Synthetic inputs (no
+checkpoint or dataset is available): latents and text states ~ N(0, 1).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+N > 1 (torchrun, one process per GPU): ranks form CFG pairs; rank 2p runs the
+cond half and rank 2p+1 the uncond half of one denoising job with one NCCL
+all-gather of the velocities per step; pairs are independent jobs.
+
+Prints one JSON line (rank 0).  `value` is seconds per step on the device
+with inputs resident in HBM (CUDA events, max over ranks); `e2e` is the same
+step through the C ABI with host buffers (H2D of the step's inputs and D2H of
+the velocity inside the timed region).  The 20.4 GB of INT8 weights streamed
+every step exceed the 126 MB L2, so no flush is needed between steps.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "qwen-image.cu_b200"))
+sys.path.insert(0, os.path.join(ROOT, "oracle"))
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+H_LAT = W_LAT = 166
+N_TXT = 256
+BLOCKS = 60
+CFG_SCALE = 4.0
+SHIFT = 3.0
+SCHED_STEPS = 50
+N_IMG = (H_LAT // 2) * (W_LAT // 2)
+S_JOINT = N_IMG + N_TXT
+DIM, MLP = 3072, 12288
+METRIC = "MMDiT sec/denoise-step at 1328^2 @1/2/4/8 B200; % of tensor-core peak"
+
+
+def sigmas_fixed_shift(n, shift):
+    """FlowMatchScheduler.get_sigmas, fixed-shift branch (scheduler.h:62-101)."""
+    s = [1.0 + (1.0 / n - 1.0) * i / (n - 1) for i in range(n)]
+    s = [shift * t / (1.0 + (shift - 1.0) * t) for t in s]
+    return s + [0.0]
+
+
+def flops_per_forward(n_img, n_txt, blocks=BLOCKS):
+    """Algorithmic FLOPs of one forward: INT8 linears + attention (QK + PV)."""
+    toks = n_img + n_txt
+    lin = 2.0 * toks * (4 * DIM * DIM + 2 * DIM * MLP) * blocks
+    attn = 4.0 * toks * toks * DIM * blocks
+    return lin, attn
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons, sampled every 200 ms."""
+
+    def __init__(self, index):
+        self.index = index
+        self.rows = []
+        self.proc = None
+
+    def __enter__(self):
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([v.strip() for v in line.split(",")])
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in self.rows:
+            try:
+                sm.append(float(r[1]))
+                mx = float(r[2])
+                for n, v in zip(names, r[5:9]):
+                    if v.lower().startswith("active"):
+                        reasons.add(n)
+            except (ValueError, IndexError):
+                continue
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def measured_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return json.load(f), "measured"
+    except Exception:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+def init_dist(world, local):
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                             device_id=torch.device("cuda", local))
+
+
+def barrier(world):
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+
+
+def max_over_ranks(v, world):
+    if world == 1:
+        return v
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ------------------------------------------------------------------ our arm
+def run_ours(args):
+    import qib200 as Q
+
+    rank, world, local = dist_env()
+    init_dist(world, local)
+    pair = world > 1
+    half = rank % 2 if pair else None  # CFG half of this rank
+    nb = 1 if pair else 2
+    g, blocks = Q.make_weight_table(BLOCKS, base_seed=0)
+    ctx = Q.Context(local)
+    model = Q.Model(ctx, g, blocks)
+    del g, blocks
+    torch.cuda.empty_cache()
+
+    sig = sigmas_fixed_shift(SCHED_STEPS, SHIFT)
+    job = rank // 2 if pair else rank
+    latent = Q.synth((1, 16, H_LAT, W_LAT), Q.seed_for(100 + job, "noise"), sig[0])
+    lat_bf = latent.to(torch.bfloat16)
+    ctxs = torch.stack([Q.synth((N_TXT, 3584), Q.seed_for(100 + job, f"context_{b}"), 1.0, dtype=torch.bfloat16)
+                        for b in range(2)])
+    pe1 = torch.from_numpy(Q.rope_table(H_LAT, W_LAT, N_TXT)).cuda()
+    pe = torch.stack([pe1, pe1]) if nb == 2 else pe1[None]
+    my_ctx = ctxs if nb == 2 else ctxs[half:half + 1].contiguous()
+    vel = torch.empty(nb, 16, H_LAT, W_LAT, dtype=torch.bfloat16, device="cuda")
+    gathered = torch.empty(2, 16, H_LAT, W_LAT, dtype=torch.bfloat16, device="cuda")
+    group = None
+    if pair:
+        pairs = [torch.distributed.new_group([2 * p, 2 * p + 1]) for p in range(world // 2)]
+        group = pairs[rank // 2]
+    stream = torch.cuda.current_stream()
+
+    def step(i):
+        s, s_next = sig[i % SCHED_STEPS], sig[i % SCHED_STEPS + 1]
+        x = lat_bf.expand(nb, -1, -1, -1).contiguous() if nb == 2 else lat_bf
+        Q.forward(ctx, model, x, s * 1000.0, my_ctx, pe, out=vel)
+        if pair:
+            torch.distributed.all_gather_into_tensor(gathered, vel, group=group)
+            v = gathered
+        else:
+            v = vel
+        Q.check(Q.lib().qi_cfg_euler_step(Q._p(latent), Q._p(v[0]), Q._p(v[1]), CFG_SCALE, s, s_next, H_LAT, W_LAT,
+                                          Q._p(lat_bf), Q._stream()))
+
+    for i in range(args.warmup):
+        step(i)
+    ctx.check()
+    Q.lib().qi_ctx_set_profiling(ctx.h, 1)
+    Q.lib().qi_ctx_profile(ctx.h, None, None, 1)
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        e0.record(stream)
+        for i in range(args.steps):
+            step(args.warmup + i)
+        e1.record(stream)
+        barrier(world)
+    ms = e0.elapsed_time(e1) / args.steps
+    ms = max_over_ranks(ms, world)
+    nprof = 12
+    import ctypes
+    pl = (ctypes.c_int * nprof)()
+    pm = (ctypes.c_float * nprof)()
+    Q.check(Q.lib().qi_ctx_profile(ctx.h, pl, pm, 1))
+    Q.lib().qi_ctx_set_profiling(ctx.h, 0)
+    launches_per_forward = ctx.launches()
+    ctx.check()
+
+    # e2e: the same step through the C ABI from pinned host buffers
+    h_x = torch.empty(nb, 16, H_LAT, W_LAT, dtype=torch.bfloat16).pin_memory()
+    h_ctx = my_ctx.cpu().pin_memory()
+    h_pe = pe.cpu().pin_memory()
+    h_out = torch.empty(nb, 16, H_LAT, W_LAT, dtype=torch.bfloat16).pin_memory()
+    d_x = torch.empty_like(vel)
+    d_ctx = torch.empty_like(my_ctx)
+    d_pe = torch.empty_like(pe)
+    h_x.copy_(lat_bf.expand(nb, -1, -1, -1).cpu())
+    barrier(world)
+    e0.record(stream)
+    for i in range(args.steps):
+        s = sig[i % SCHED_STEPS]
+        d_x.copy_(h_x, non_blocking=True)
+        d_ctx.copy_(h_ctx, non_blocking=True)
+        d_pe.copy_(h_pe, non_blocking=True)
+        Q.forward(ctx, model, d_x, s * 1000.0, d_ctx, d_pe, out=vel)
+        if pair:
+            torch.distributed.all_gather_into_tensor(gathered, vel, group=group)
+        h_out.copy_(vel, non_blocking=True)
+    e1.record(stream)
+    barrier(world)
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, world)
+    bi = h_x.numel() * 2 + h_ctx.numel() * 2 + h_pe.numel() * 4
+    bo = h_out.numel() * 2
+
+    if rank != 0:
+        model.close()
+        ctx.close()
+        if world > 1:
+            torch.distributed.destroy_process_group()
+        return
+
+    peaks, psrc = measured_peaks()
+    int8_peak = 2.0 * peaks["bf16_tflops"]  # INT8 dense = 2 x BF16 dense on B200 (kind::i8)
+    lin_f, attn_f = flops_per_forward(N_IMG, N_TXT)
+    gemm_stages = [2, 7, 8, 10]  # QI_PROF_GEMM_QKV, _OUT, _FC1, _FC2
+    gemm_ms = sum(pm[i] for i in gemm_stages)
+    gemm_n = sum(pl[i] for i in gemm_stages)
+    gemm_flops_total = lin_f * nb * args.steps  # every INT8 linear of the blocks runs in these launches
+    avg_launch_ms = gemm_ms / max(gemm_n, 1)
+    achieved = gemm_flops_total / gemm_n / (avg_launch_ms * 1e-3) / 1e12 if gemm_n else None
+    attn_ms = pm[5]
+    attn_tflops = attn_f * nb * args.steps / (attn_ms * 1e-3) / 1e12 if attn_ms > 0 else None
+    stage_names = ["pre", "quant_ln", "gemm_qkv", "qkv_post", "sage_quant", "attention", "quant_o", "gemm_out",
+                   "gemm_fc1", "quant_h", "gemm_fc2", "post"]
+    stages = {n: {"launches": int(pl[i]), "ms_per_step": round(pm[i] / args.steps, 3)}
+              for i, n in enumerate(stage_names)}
+
+    cpu = cpu_baseline(args) if (world == 1 and not args.no_cpu) else None
+    traffic = None
+    tpath = os.path.join(ROOT, "profiles", "gemm_i8_traffic.json")
+    if os.path.exists(tpath):
+        with open(tpath) as f:
+            traffic = json.load(f).get("bytes_per_launch")
+    line = {
+        "metric": METRIC,
+        "value": round(ms / 1000.0, 5),
+        "unit": "s/step",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms, 3),
+        "higher_is_better": False,
+        "scaling": "strong" if world <= 2 else "weak",
+        "vs_baseline": None,
+        "dtype": "int8",
+        "data": "synthetic (seeded N(0,1) latents/text states; random-init N(0,0.02^2) weights quantized to INT8)",
+        "config": {"workload": "C4: 1328x1328, 6889 img + 256 txt tokens, CFG cond+uncond, 60 blocks, W8A8 + "
+                               "SageAttention (INT8 QK, FP16 PV)",
+                   "latent": [16, H_LAT, W_LAT], "n_img": N_IMG, "n_txt": N_TXT, "blocks": BLOCKS,
+                   "cfg": "batched (nb=2) on 1 GPU" if world == 1 else "cond/uncond split over rank pairs",
+                   "parallelism": "single" if world == 1 else f"cfg2 x {world // 2} jobs",
+                   "l2": "no flush: 20.4 GB of INT8 weights streamed per step >> 126 MB L2"},
+        "e2e": {"value": round(e2e_ms / 1000.0, 5), "unit": "s/step", "h2d_bytes_per_step": bi,
+                "d2h_bytes_per_step": bo},
+        "gpu_launches": (launches_per_forward + 1) * args.steps,
+        "roofline": {"kernel": "gemm_kernel<false> (tcgen05 kind::i8 W8A8 GEMM)", "bound": "tensor",
+                     "achieved": round(achieved, 1) if achieved else None, "peak": round(int8_peak, 1),
+                     "unit": "TFLOP/s", "frac": round(achieved / int8_peak, 4) if achieved else None,
+                     "traffic": traffic,
+                     "peak_source": f"2 x bf16_tflops {psrc} (MEASURED_PEAKS.json); INT8 dense = 2x BF16 dense",
+                     "flops_per_launch": gemm_flops_total / max(gemm_n, 1), "avg_launch_ms": avg_launch_ms},
+        "attention": {"tflops": round(attn_tflops, 1) if attn_tflops else None,
+                      "ms_per_step": round(attn_ms / args.steps, 3)},
+        "stages": stages,
+        "clocks": clk.summary(),
+    }
+    if cpu:
+        line["cpu_baseline"] = cpu
+    print(json.dumps(line), flush=True)
+    model.close()
+    ctx.close()
+    if world > 1:
+        torch.distributed.destroy_process_group()
+
+
+def cpu_baseline(args):
+    """The FP32 CPU evaluation (CPU oracle, unquantized) of one double-stream
+    block at the C1 size (1024 image + 64 text tokens, the reference's
+    block-verify configuration), timed on the host cores and scaled by the
+    algorithmic FLOP ratio to one C4 denoising step (2 x 60 blocks at 7145
+    tokens)."""
+    import qi_oracle as O
+    threads = os.cpu_count() or 1
+    O.set_threads(threads)
+    W = O.Weights(1)
+    n_img, n_txt = 1024, 64
+    img = O.gen_f32(1, (n_img, DIM))
+    txt = O.gen_f32(2, (n_txt, DIM))
+    mi = O.gen_f32(3, (6 * DIM,), 0.1)
+    mt = O.gen_f32(4, (6 * DIM,), 0.1)
+    pe = O.rope_table(64, 64, n_txt)
+    O.block_fp32(W, img[:8], txt[:8], mi, mt, pe)  # materialise the weights
+    best = None
+    for _ in range(2):
+        t0 = time.time()
+        O.block_fp32(W, img, txt, mi, mt, pe)
+        dt = time.time() - t0
+        best = dt if best is None else min(best, dt)
+    lin_b, attn_b = flops_per_forward(n_img, n_txt, blocks=1)
+    lin_s, attn_s = flops_per_forward(N_IMG, N_TXT)
+    scale = 2.0 * (lin_s + attn_s) / (lin_b + attn_b)
+    return {"value": round(best * scale, 2), "unit": "s/step", "cores": threads, "kind": "port",
+            "sample": f"one FP32 block at C1 (1024+64 tokens, {best:.2f} s, best of 2) x {scale:.0f} "
+                      f"(FLOP ratio to one C4 CFG step)"}
+
+
+# ------------------------------------------------------------------ reference arm
+def run_reference(args):
+    rank, world, local = dist_env()
+    if rank != 0:
+        return
+    torch.cuda.set_device(local)
+    import qi_ref as R
+    if not R.available():
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libqiref.so (reference build) missing"}))
+        return
+    g, blocks = R.make_table(BLOCKS, distinct=BLOCKS)
+    garr, barrs, bt = R.table_pointers(g, blocks)
+    sig = sigmas_fixed_shift(SCHED_STEPS, SHIFT)
+    latent = R.synth((1, 16, H_LAT, W_LAT), R.seed_for(100, "noise"), sig[0])
+    ctxs = [R.synth((1, N_TXT, 3584), R.seed_for(100, f"context_{b}"), 1.0, dtype=torch.bfloat16) for b in range(2)]
+    import numpy as _np  # noqa: F401
+    pe = torch.from_numpy(R.rope_table(H_LAT, W_LAT, N_TXT)).cuda()
+    stream = torch.cuda.current_stream()
+
+    def step(i):
+        s, s_next = sig[i % SCHED_STEPS], sig[i % SCHED_STEPS + 1]
+        x = latent.to(torch.bfloat16)
+        vc = R.transformer_forward(garr, bt, x, s * 1000.0, ctxs[0], pe, H_LAT, W_LAT, sage=True).float()
+        vu = R.transformer_forward(garr, bt, x, s * 1000.0, ctxs[1], pe, H_LAT, W_LAT, sage=True).float()
+        # the caller's norm-preserving CFG + Euler (main.cu:817-868) as plain torch ops
+        comb = vu + CFG_SCALE * (vc - vu)
+        grp = lambda t: t.reshape(16, H_LAT // 2, 2, W_LAT // 2, 2).permute(1, 3, 0, 2, 4).reshape(-1, 64)
+        r = grp(vc).norm(dim=1) / grp(comb).norm(dim=1).clamp_min(1e-30)
+        v = (grp(comb) * r[:, None]).reshape(H_LAT // 2, W_LAT // 2, 16, 2, 2).permute(2, 0, 3, 1, 4)
+        v = v.reshape(1, 16, H_LAT, W_LAT)
+        den = latent - s * v
+        latent.copy_(latent + (latent - den) / s * (s_next - s))
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        e0.record(stream)
+        for i in range(args.steps):
+            step(args.warmup + i)
+        e1.record(stream)
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    line = {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": round(ms / 1000.0, 5),
+        "unit": "s/step",
+        "n_gpus": 1,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms, 3),
+        "higher_is_better": False,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "int8",
+        "data": "synthetic (same seeds as the product arm)",
+        "config": {"workload": "C4: 1328x1328, 6889 img + 256 txt tokens, CFG cond+uncond, 60 blocks, W8A8 + "
+                               "SageAttention sm80 (reference build, transformer_forward x2 per step)",
+                   "latent": [16, H_LAT, W_LAT], "n_img": N_IMG, "n_txt": N_TXT, "blocks": BLOCKS},
+        "cpu_baseline": {"value": round(ms / 1000.0, 5), "unit": "s/step", "cores": 0, "kind": "reference",
+                         "sample": "the reference's own CUDA build (it has no CPU path) timed on one GPU"},
+        "e2e": {"value": round(ms / 1000.0, 5), "unit": "s/step", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "clocks": clk.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        print("warmup < 3 is not a valid measurement; using 3", file=sys.stderr)
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,203 @@
+/*
+ * qwen_image_b200.h -- C ABI of the B200-native Qwen-Image MMDiT denoising path.
+ *
+ * Plain pointers and sizes only.  Every entry point returns an int status
+ * (QI_OK == 0) instead of exiting; qi_status_string() names it.  Device
+ * pointers are CUDA device addresses on the context's device; `stream` is a
+ * cudaStream_t passed as void* (NULL = legacy default stream).  All calls are
+ * asynchronous on `stream` unless stated otherwise.
+ *
+ * Reference interfaces each entry replaces are cited as file:line of the
+ * reference project (TheLegendOfKitty/qwen-image.cu).
+ */
+#ifndef QWEN_IMAGE_B200_H
+#define QWEN_IMAGE_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ------------------------------------------------------------ status codes */
+enum {
+  QI_OK = 0,
+  QI_ERR_ARG = 1,         /* bad size / null pointer / unsupported shape        */
+  QI_ERR_ALIGN = 2,       /* pointer or leading dimension not 16-byte aligned    */
+  QI_ERR_CUDA = 3,        /* a CUDA runtime/driver call failed                   */
+  QI_ERR_OOM = 4,         /* device allocation failed                            */
+  QI_ERR_UNSUPPORTED = 5, /* shape outside what the kernels implement            */
+  QI_ERR_IO = 6,          /* file missing or malformed (safetensors)             */
+  QI_ERR_DEVICE = 7,      /* a kernel reported a bounded-wait timeout            */
+  QI_ERR_NCCL = 8         /* a collective failed or timed out                    */
+};
+
+const char* qi_status_string(int status);
+int qi_version(void);
+
+/* ------------------------------------------------------------ op level
+ * Each op mirrors one reference function; the tests call these through the
+ * ABI and compare with the reference's own build on the same inputs.        */
+
+/* Load-time weight quantizer: BF16 [N,K] -> block-FWHT rows (block K & -K)
+ * -> per-row INT8 codes [N,K] + FP32 scales [N].
+ * Replaces quantize_weight_tensor (cuda_kernels.cuh:308, cuda_kernels.cu:2830)
+ * and produces quantize.cu's "<name>" / "<name>.__scales__" pair
+ * (quantize.cu:121-137).  Codes and scales are bit-exact with the reference. */
+int qi_quantize_weight(const void* w_bf16, int N, int K, int8_t* codes, float* scales, void* stream);
+
+/* Activation quantizer: FP32 [M,K] -> block-FWHT (block `had_block`) ->
+ * per-token INT8 codes + FP32 scales.  had_block <= 1 skips the transform.
+ * Replaces quantize_activation_int8_hadamard_fp32 (cuda_kernels.cuh:277,
+ * cuda_kernels.cu:2603).  Bit-exact with the reference.                      */
+int qi_fwht_quantize(const float* x, int M, int K, int had_block, int8_t* codes, float* scales, void* stream);
+
+/* W8A8 linear on prequantized activations:
+ *   out[m,n] = acc[m,n] * act_scales[m] * w_scales[n] + bias[n]   (epilogue 0)
+ *   out[m,n] = gelu_tanh(...)                                     (epilogue 1)
+ *   out[m,n] += gate[n] * (...)                                   (epilogue 2)
+ * acc = sum_k act[m,k] * w[n,k] in INT32 (exact).  bias is BF16 [N] or NULL.
+ * Requires K % 16 == 0, N % 32 == 0, ldo % 4 == 0, 16-byte aligned pointers.
+ * Replaces linear_forward_int8_prequantized (cuda_kernels.cuh:297,
+ * cuda_kernels.cu:2735) and, for epilogue 2, the following gate_add_fp32f
+ * (cuda_kernels.cuh:567).                                                    */
+int qi_linear_i8(const int8_t* act, const float* act_scales, int M, int K, const int8_t* w, const float* w_scales,
+                 int N, const void* bias_bf16, int epilogue, const float* gate, float* out, int ldo, void* stream);
+
+/* Full W8A8 linear from FP32 activations (FWHT + quantize + GEMM + dequant),
+ * M == 1 included.  Replaces linear_forward_int8 (cuda_kernels.cuh:290,
+ * cuda_kernels.cu:2674) / linear_forward_quantized for INT8 weights
+ * (cuda_kernels.cuh:420).                                                    */
+int qi_linear_i8_f32in(const float* x, int M, int K, const int8_t* w, const float* w_scales, int N,
+                       const void* bias_bf16, int apply_gelu, float* out, void* stream);
+
+/* SageAttention on FP16 Q, K, V laid out [BH, S, 128] (head-major):
+ * K mean smoothing, per-thread INT8 Q/K quantisation, INT8 QK^T, FP16 P.V,
+ * online base-2 softmax; output FP32 [BH, S, 128] (each value an FP16
+ * rounding, as the reference's FP16 output converted to FP32).
+ * Replaces attention_forward_sage_sm80_fp16io (cuda_kernels.cuh:560,
+ * sageattention_sm80.cu:965-1027).  head_dim must be 128.                    */
+int qi_sage_attention(const void* q_f16, const void* k_f16, const void* v_f16, float* out, float scale, int BH,
+                      int S, int D, void* stream);
+
+/* The Sage quantizers alone, for bit-exact checks against the reference:
+ * k_mean [BH,128]; Q codes [BH,S,128] + scales [BH, ceil(S/128)*32];
+ * K codes [BH,S,128] + scales [BH, ceil(S/64)*4]
+ * (sageattention_sm80.cu:759-886).                                           */
+int qi_sage_quantize(const void* q_f16, const void* k_f16, int BH, int S, float* k_mean, int8_t* q_codes,
+                     float* q_scales, int8_t* k_codes, float* k_scales, void* stream);
+
+/* LayerNorm (no affine, eps) + modulate: out = norm(x) * (1 + scale) + shift.
+ * Replaces layer_norm_modulate_fp32 (cuda_kernels.cuh:524).                  */
+int qi_layer_norm_modulate(const float* x, const float* shift, const float* scale, float* out, int rows, int dim,
+                           float eps, void* stream);
+
+/* Per-row RMSNorm, FP32 in/out, BF16 weight.  Replaces rms_norm_fp32
+ * (cuda_kernels.cuh:510).                                                    */
+int qi_rms_norm(const float* x, const void* w_bf16, float* out, int rows, int dim, float eps, void* stream);
+
+/* ------------------------------------------------------------ model level */
+typedef struct qi_ctx qi_ctx;
+typedef struct qi_model qi_model;
+
+/* Device context: device ordinal, scratch workspace (grows on demand, like
+ * the reference's static workspace, transformer.cu:134-215), error slot.    */
+int qi_ctx_create(int device, qi_ctx** out);
+int qi_ctx_destroy(qi_ctx* ctx);
+/* Reads (and clears) the device error word a kernel raised; QI_ERR_DEVICE if
+ * any kernel gave up a bounded wait since the last call.  Synchronous.      */
+int qi_ctx_check(qi_ctx* ctx);
+
+/* Weight table in quantize.cu's format, one device pointer per tensor,
+ * indexed by the enums below.  INT8 linears: codes I8 [N,K], scales F32 [N],
+ * bias BF16 [N].  Boundary linears (img_in, txt_in, norm_out, proj_out):
+ * BF16 weight [N,K] + BF16 bias (quantize.cu:467-477).  Norm weights BF16.
+ * Names: transformer.h:407-563.                                              */
+enum {
+  QI_G_T1_W, QI_G_T1_S, QI_G_T1_B, /* time_text_embed.timestep_embedder.linear_1 [3072,256] */
+  QI_G_T2_W, QI_G_T2_S, QI_G_T2_B, /* ...linear_2 [3072,3072] */
+  QI_G_TXT_NORM,                   /* txt_norm.weight [3584] */
+  QI_G_IMG_IN_W, QI_G_IMG_IN_B,    /* img_in [3072,64] BF16 */
+  QI_G_TXT_IN_W, QI_G_TXT_IN_B,    /* txt_in [3072,3584] BF16 */
+  QI_G_NORM_OUT_W, QI_G_NORM_OUT_B, /* norm_out.linear [6144,3072] BF16 */
+  QI_G_PROJ_OUT_W, QI_G_PROJ_OUT_B, /* proj_out [64,3072] BF16 */
+  QI_G_COUNT
+};
+/* Per block: 14 INT8 linears x (codes, scales, bias) then 4 norm weights. */
+enum {
+  QI_L_IMG_MOD, QI_L_TXT_MOD, QI_L_TO_Q, QI_L_TO_K, QI_L_TO_V, QI_L_ADD_Q, QI_L_ADD_K, QI_L_ADD_V,
+  QI_L_TO_OUT, QI_L_TO_ADD_OUT, QI_L_IMG_FC1, QI_L_IMG_FC2, QI_L_TXT_FC1, QI_L_TXT_FC2, QI_L_COUNT
+};
+enum {
+  QI_B_NORM_Q = 3 * QI_L_COUNT, QI_B_NORM_K, QI_B_NORM_ADDED_Q, QI_B_NORM_ADDED_K, QI_B_COUNT
+};
+
+/* Builds the kernels' weight layout (fused QKV, stacked modulation) from a
+ * device table.  Copies; the caller may free its tensors afterwards.
+ * Replaces TransformerWeights::load's INT8 path (transformer.h:144-200,
+ * 515-563).  block_tables[i] points to QI_B_COUNT device pointers.           */
+int qi_model_create(qi_ctx* ctx, int num_blocks, const void* const* global_table,
+                    const void* const* const* block_tables, qi_model** out);
+/* Reads a quantize.cu INT8 safetensors file (or a sharded index .json).
+ * Replaces SafeTensorsLoader + TransformerWeights::load (safetensors.h:36-212,
+ * transformer.h:144).                                                        */
+int qi_model_load_safetensors(qi_ctx* ctx, const char* path, qi_model** out);
+int qi_model_destroy(qi_model* model);
+int qi_model_num_blocks(const qi_model* model);
+
+/* One MMDiT forward for `nb` independent batch elements that share the
+ * latent shape and timestep (nb = 2: CFG cond/uncond in one pass).
+ *   x:   nb x [16, H, W] BF16 latents (contiguous)
+ *   ctx: nb x [n_txt, 3584] BF16 text states (contiguous)
+ *   pe:  nb x [n_txt + n_img, 64, 2, 2] FP32 RoPE tables (contiguous; the
+ *        table of rope.h gen_qwen_image_pe)
+ *   out: nb x [16, H, W] BF16 velocities
+ * Replaces transformer_forward (transformer.h:613-621, transformer.cu:234-931)
+ * with use_sage_attention = true.  H and W must be even.                     */
+int qi_forward(qi_ctx* ctx, const qi_model* model, int nb, const void* x_bf16, float timestep,
+               const void* ctx_bf16, int n_txt, const float* pe, int H, int W, void* out_bf16, void* stream);
+
+/* RoPE table of rope.h gen_qwen_image_pe (h, w = latent size): host memory,
+ * [n_txt + n_img, 64, 2, 2] FP32.                                            */
+int qi_rope_table(int h, int w, int n_txt, float* pe_host);
+
+/* Number of kernel launches issued by the last qi_forward on this context. */
+int qi_ctx_last_launch_count(const qi_ctx* ctx);
+
+/* Per-stage timing of qi_forward with CUDA events (the reference's
+ * PROFILE_BLOCK hook, transformer.cu:486-495 / 838-860).  While enabled each
+ * forward records an event pair around every launch; qi_ctx_profile then
+ * returns, per stage (QI_PROF_*), the number of launches and the summed
+ * device milliseconds since the last reset.  Synchronous.                    */
+enum {
+  QI_PROF_PRE = 0,       /* patchify, timestep MLP, modulation, img_in, txt_in */
+  QI_PROF_QUANT_LN,      /* LayerNorm + modulate + FWHT + INT8 (2 per block)    */
+  QI_PROF_GEMM_QKV,      /* fused Q/K/V INT8 GEMM                               */
+  QI_PROF_QKV_POST,      /* q/k RMSNorm + RoPE + FP16 head-major                */
+  QI_PROF_SAGE_QUANT,    /* K mean + Q/K per-thread INT8                         */
+  QI_PROF_ATTENTION,     /* SageAttention                                       */
+  QI_PROF_QUANT_O,       /* attention output FWHT + INT8                        */
+  QI_PROF_GEMM_OUT,      /* out-projection INT8 GEMM + gated residual           */
+  QI_PROF_GEMM_FC1,      /* fc1 INT8 GEMM + GELU                                */
+  QI_PROF_QUANT_H,       /* fc2 input FWHT(4096) + INT8                         */
+  QI_PROF_GEMM_FC2,      /* fc2 INT8 GEMM + gated residual                      */
+  QI_PROF_POST,          /* output AdaLN, proj_out, unpatchify                  */
+  QI_PROF_COUNT
+};
+int qi_ctx_set_profiling(qi_ctx* ctx, int enable);
+int qi_ctx_profile(qi_ctx* ctx, int* launches, float* ms, int reset);
+
+/* One flow-matching Euler step with norm-preserving CFG on the device
+ * (main.cu:228-288 cfg_combine_and_norms + cfg_norm_scale, :221
+ * denoiser_scaling_fp32, :210 euler_step_fp32, then fp32_to_bf16 for the next
+ * forward): v = uncond + s*(cond - uncond), rescaled per 2x2 patch group so its
+ * norm matches cond's; x += (x - (x - sigma*v)) / sigma * (sigma_next - sigma).
+ * latent: FP32 [16,H,W] updated in place; latent_bf16 receives its BF16 copy. */
+int qi_cfg_euler_step(float* latent, const void* cond_bf16, const void* uncond_bf16, float cfg_scale, float sigma,
+                      float sigma_next, int H, int W, void* latent_bf16, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* QWEN_IMAGE_B200_H */

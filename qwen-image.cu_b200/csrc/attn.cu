@@ -1,0 +1,525 @@
+// attn.cu -- SageAttention (INT8 QK^T, FP16 P.V) on the 5th-gen tensor cores.
+//
+// Algorithm of the reference's launched instantiation
+// qk_int_sv_f16_attn_kernel<CTA_Q=128, CTA_K=64, per-thread Q/K scales, FP32
+// accumulation, tensor-core row sums> (sageattention_sm80.cu:47-674, launch
+// :896-961), re-tiled for tcgen05:
+//   * Q and K are INT8 codes with "per-thread" scales (32 per 128-query block,
+//     4 per 64-key block, after K mean smoothing); S = Qc . Kc^T is an exact
+//     INT32 tile produced by tcgen05.mma.kind::i8 into TMEM;
+//   * the scales are rank-1 (row x column) so they are applied to the INT32
+//     tile after the TMEM load: s = float(acc) * q_scale[row] * k_scale[col]
+//     * sm_scale * log2(e);
+//   * online softmax in base 2 (ex2.approx, m initialised to -5e6, the
+//     reference's update_mdo, sageattention_attn_utils.cuh:352-456);
+//   * P is rounded to FP16 and the row sum is accumulated from the rounded
+//     values; O += P.V runs as tcgen05.mma.kind::f16 with FP32 accumulation in
+//     TMEM; the running output is rescaled in TMEM when the row max grows;
+//   * the result is O * rcp(l) rounded to FP16 (normalize_d, :719-760).
+//
+// Tiling: one CTA per (128 queries, batch-head); keys in blocks of 128 (two
+// of the reference's 64-key scale blocks).  Warp 0 issues TMA (Q once, K/V in
+// a two-stage ring), warp 1 issues the MMAs (QK^T of block j+1 is issued
+// before P.V of block j so the tensor core works while softmax runs), warps
+// 2-5 own one query row per thread (TMEM lane = row).
+// TMEM: S double buffer (2 x 128 columns) + O (128 columns).
+#include "qi_internal.h"
+#include "sm100.cuh"
+
+namespace qi {
+
+namespace attn {
+constexpr int BQ = 128, BKV = 128, D = 128;
+constexpr int Q_BYTES = BQ * D;        // int8
+constexpr int K_BYTES = BKV * D;       // int8
+constexpr int V_BYTES = BKV * D * 2;   // fp16
+constexpr int P_BYTES = BQ * BKV * 2;  // fp16
+constexpr int OFF_Q = 0;
+constexpr int OFF_K = OFF_Q + Q_BYTES;
+constexpr int OFF_V = OFF_K + 2 * K_BYTES;
+constexpr int OFF_P = OFF_V + 2 * V_BYTES;
+constexpr int OFF_BAR = OFF_P + P_BYTES;
+constexpr int SMEM_BYTES = OFF_BAR + 256 + 1024;
+constexpr int THREADS = 192;
+constexpr int TMEM_COLS = 512;
+constexpr int TM_S0 = 0, TM_S1 = 128, TM_O = 256;
+}  // namespace attn
+
+struct alignas(64) AttnArgsDev {
+  CUtensorMap tmQ, tmK, tmV;
+  const float* qs;
+  const float* ks;
+  void* out;
+  int BH, S, heads, out_mode, nb, n_img, n_txt, ngq, ngk;
+  float qk_scale;  // sm_scale * log2(e)
+  int* err;
+};
+
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm volatile("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float rcp_approx(float x) {
+  float y;
+  asm volatile("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__global__ void __launch_bounds__(attn::THREADS, 1) sage_attn_kernel(const __grid_constant__ AttnArgsDev args) {
+  using namespace attn;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem + OFF_Q;
+  uint8_t* sK = smem + OFF_K;
+  uint8_t* sV = smem + OFF_V;
+  uint8_t* sP = smem + OFF_P;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
+  uint64_t* q_full = bars + 0;
+  uint64_t* k_full = bars + 1;   // [2]
+  uint64_t* k_empty = bars + 3;  // [2]
+  uint64_t* v_full = bars + 5;   // [2]
+  uint64_t* v_empty = bars + 7;  // [2]
+  uint64_t* s_full = bars + 9;   // [2]
+  uint64_t* s_free = bars + 11;  // [2]
+  uint64_t* p_full = bars + 13;
+  uint64_t* o_done = bars + 14;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 17);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int q0 = blockIdx.x * BQ;
+  const int bh = blockIdx.y;
+  const int S = args.S;
+  const int nkb = (S + BKV - 1) / BKV;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], 1);
+      mbar_init(&v_full[i], 1);
+      mbar_init(&v_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_free[i], 4);
+    }
+    mbar_init(p_full, 4);
+    mbar_init(o_done, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&args.tmQ);
+    tma_prefetch_desc(&args.tmK);
+    tma_prefetch_desc(&args.tmV);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      bool ok = true;
+      uint32_t kmask = 0, kpar = 0, vmask = 0, vpar = 0;
+      mbar_expect_tx(q_full, Q_BYTES);
+      tma_load_3d(sQ, &args.tmQ, 0, q0, bh, q_full);
+      for (int j = 0; j < nkb && ok; ++j) {
+        const int st = j & 1;
+        const uint32_t ph = (j >> 1) & 1;
+        if (!mbar_wait(&k_empty[st], ph ^ 1u, abort_flag)) { ok = false; break; }
+        mbar_expect_tx(&k_full[st], K_BYTES);
+        tma_load_3d(sK + st * K_BYTES, &args.tmK, 0, j * BKV, bh, &k_full[st]);
+        kmask |= 1u << st;
+        kpar = (kpar & ~(1u << st)) | (ph << st);
+        if (!mbar_wait(&v_empty[st], ph ^ 1u, abort_flag)) { ok = false; break; }
+        mbar_expect_tx(&v_full[st], V_BYTES);
+        tma_load_3d(sV + st * V_BYTES, &args.tmV, 0, j * BKV, bh, &v_full[st]);
+        tma_load_3d(sV + st * V_BYTES + V_BYTES / 2, &args.tmV, 64, j * BKV, bh, &v_full[st]);
+        vmask |= 1u << st;
+        vpar = (vpar & ~(1u << st)) | (ph << st);
+      }
+      if (!ok) {
+        *abort_flag = 1;
+        atomicCAS(args.err, 0, kErrTimeoutProducer);
+        uint64_t t0 = global_timer_ns();
+        while (!mbar_try_wait(q_full, 0) && global_timer_ns() - t0 < kWaitLimitNs / 4) {
+        }
+        for (int s = 0; s < 2; ++s) {
+          t0 = global_timer_ns();
+          if (kmask & (1u << s))
+            while (!mbar_try_wait(&k_full[s], (kpar >> s) & 1u) && global_timer_ns() - t0 < kWaitLimitNs / 4) {
+            }
+          t0 = global_timer_ns();
+          if (vmask & (1u << s))
+            while (!mbar_try_wait(&v_full[s], (vpar >> s) & 1u) && global_timer_ns() - t0 < kWaitLimitNs / 4) {
+            }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      bool ok = mbar_wait(q_full, 0, abort_flag);
+      const uint32_t id_qk = idesc_i8(BQ, BKV);
+      const uint32_t id_pv = idesc_f16(BQ, D, false, true);
+      const uint32_t q_addr = smem_u32(sQ);
+      for (int j = 0; j <= nkb && ok; ++j) {
+        if (j < nkb) {
+          const int st = j & 1;
+          const uint32_t ph = (j >> 1) & 1;
+          if (!mbar_wait(&k_full[st], ph, abort_flag)) { ok = false; break; }
+          if (!mbar_wait(&s_free[st], ph ^ 1u, abort_flag)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t k_addr = smem_u32(sK + st * K_BYTES);
+          const uint32_t d_s = tmem + (st ? TM_S1 : TM_S0);
+#pragma unroll
+          for (int k = 0; k < D / 32; ++k)
+            mma_i8_ss(d_s, umma_desc_sw128(q_addr + k * 32, 16, 1024), umma_desc_sw128(k_addr + k * 32, 16, 1024),
+                      id_qk, k > 0 ? 1u : 0u);
+          mma_commit(&s_full[st]);
+          mma_commit(&k_empty[st]);
+        }
+        if (j >= 1) {
+          const int jj = j - 1;
+          const int st = jj & 1;
+          if (!mbar_wait(p_full, jj & 1, abort_flag)) { ok = false; break; }
+          if (!mbar_wait(&v_full[st], (jj >> 1) & 1, abort_flag)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t v_addr = smem_u32(sV + st * V_BYTES);
+          const uint32_t p_addr = smem_u32(sP);
+#pragma unroll
+          for (int kk = 0; kk < BKV / 16; ++kk) {
+            const uint64_t ad = umma_desc_sw128(p_addr + (kk >> 2) * (P_BYTES / 2) + (kk & 3) * 32, 16, 1024);
+            const uint64_t bd = umma_desc_sw128(v_addr + kk * 16 * 128, V_BYTES / 2, 1024);
+            mma_f16_ss(tmem + TM_O, ad, bd, id_pv, (jj > 0 || kk > 0) ? 1u : 0u);
+          }
+          mma_commit(o_done);
+          mma_commit(&v_empty[st]);
+        }
+      }
+      if (!ok) {
+        *abort_flag = 1;
+        atomicCAS(args.err, 0, kErrTimeoutMma);
+      }
+    }
+  } else {
+    // -------------------------------------------------------------- softmax
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const int qrow = q0 + row;
+    const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
+    const int gq = (qrow / 128) * 32 + ((qrow % 128) / 32) * 8 + (qrow % 8);
+    const float qsm = (qrow < S) ? args.qs[static_cast<size_t>(bh) * args.ngq + gq] * args.qk_scale : 0.0f;
+    float m = -5000000.0f, l = 0.0f;
+    bool ok = true;
+    for (int j = 0; j < nkb; ++j) {
+      const int sb = j & 1;
+      bool w = mbar_wait(&s_full[sb], (j >> 1) & 1, abort_flag);
+      if (!__all_sync(0xffffffffu, w)) { ok = false; break; }
+      tc_fence_after();
+      // column factors: k_scale[(2j + c/64)*4 + (c%8)/2] * q_scale * sm_scale * log2e
+      float kf[8];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int kb64 = 2 * j + h;
+#pragma unroll
+        for (int g = 0; g < 4; ++g)
+          kf[h * 4 + g] = (kb64 * 64 < S) ? args.ks[static_cast<size_t>(bh) * args.ngk + kb64 * 4 + g] * qsm : 0.0f;
+      }
+      float s[BKV];
+      const uint32_t s_addr = tmem + lane_off + (sb ? TM_S1 : TM_S0);
+#pragma unroll
+      for (int c = 0; c < BKV; c += 32) {
+        uint32_t r[32];
+        tmem_ld32(s_addr + c, r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int col = c + i;
+          s[col] = static_cast<float>(static_cast<int32_t>(r[i])) * kf[(col >> 6) * 4 + ((col & 7) >> 1)];
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s_free[sb]);
+      if (j == nkb - 1 && (j + 1) * BKV > S) {
+#pragma unroll
+        for (int i = 0; i < BKV; ++i)
+          if (j * BKV + i >= S) s[i] = -5000000.0f;
+      }
+      float mloc = s[0];
+#pragma unroll
+      for (int i = 1; i < BKV; ++i) mloc = fmaxf(mloc, s[i]);
+      const float m_new = fmaxf(m, mloc);
+      const float alpha = ex2_approx(m - m_new);
+      if (j > 0) {
+        w = mbar_wait(o_done, (j - 1) & 1, abort_flag);
+        if (!__all_sync(0xffffffffu, w)) { ok = false; break; }
+        tc_fence_after();
+        if (__any_sync(0xffffffffu, alpha != 1.0f)) {
+#pragma unroll 1
+          for (int c = 0; c < D; c += 32) {
+            uint32_t r[32];
+            tmem_ld32(tmem + lane_off + TM_O + c, r);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
+            tmem_st32(tmem + lane_off + TM_O + c, r);
+          }
+          tmem_st_wait();
+        }
+      }
+      l *= alpha;
+      // P = exp2(s - m_new) -> FP16, row sum from the rounded values, store
+      // into the K-major 128-byte-swizzled A-operand tile.
+      uint8_t* prow = sP + row * 128;
+#pragma unroll
+      for (int c = 0; c < BKV / 8; ++c) {
+        uint32_t pk[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float p0 = ex2_approx(s[c * 8 + 2 * e] - m_new);
+          const float p1 = ex2_approx(s[c * 8 + 2 * e + 1] - m_new);
+          __half2 h2 = __floats2half2_rn(p0, p1);
+          const float2 back = __half22float2(h2);
+          l += back.x + back.y;
+          pk[e] = *reinterpret_cast<uint32_t*>(&h2);
+        }
+        const int region = c >> 3, cc = c & 7;
+        uint8_t* dst = prow + region * (P_BYTES / 2) + ((cc ^ (row & 7)) << 4);
+        *reinterpret_cast<uint4*>(dst) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_full);
+      m = m_new;
+    }
+    if (ok) {
+      bool w = mbar_wait(o_done, (nkb - 1) & 1, abort_flag);
+      ok = __all_sync(0xffffffffu, w);
+    }
+    if (!ok) {
+      if (lane == 0) {
+        *abort_flag = 1;
+        atomicCAS(args.err, 0, kErrTimeoutSoftmax);
+      }
+    } else {
+      tc_fence_after();
+      const float rl = rcp_approx(l);
+      const bool valid = qrow < S;
+      const int b = bh / args.heads, h = bh % args.heads;
+#pragma unroll 1
+      for (int c = 0; c < D; c += 32) {
+        uint32_t r[32];
+        tmem_ld32(tmem + lane_off + TM_O + c, r);
+        tmem_ld_wait();
+        if (!valid) continue;
+        if (args.out_mode == 0) {
+          float* dst = reinterpret_cast<float*>(args.out) + (static_cast<size_t>(bh) * S + qrow) * D + c;
+#pragma unroll
+          for (int i = 0; i < 32; i += 4) {
+            float4 o;
+            o.x = __half2float(__float2half_rn(__uint_as_float(r[i + 0]) * rl));
+            o.y = __half2float(__float2half_rn(__uint_as_float(r[i + 1]) * rl));
+            o.z = __half2float(__float2half_rn(__uint_as_float(r[i + 2]) * rl));
+            o.w = __half2float(__float2half_rn(__uint_as_float(r[i + 3]) * rl));
+            *reinterpret_cast<float4*>(dst + i) = o;
+          }
+        } else {
+          const long long orow = (qrow < args.n_txt)
+                                     ? static_cast<long long>(args.nb) * args.n_img + static_cast<long long>(b) * args.n_txt + qrow
+                                     : static_cast<long long>(b) * args.n_img + (qrow - args.n_txt);
+          __half* dst = reinterpret_cast<__half*>(args.out) + orow * kDim + h * D + c;
+#pragma unroll
+          for (int i = 0; i < 32; i += 8) {
+            uint32_t pk[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              __half2 h2 = __floats2half2_rn(__uint_as_float(r[i + 2 * e]) * rl, __uint_as_float(r[i + 2 * e + 1]) * rl);
+              pk[e] = *reinterpret_cast<uint32_t*>(&h2);
+            }
+            *reinterpret_cast<uint4*>(dst + i) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, TMEM_COLS);
+  }
+}
+
+// ------------------------------------------------------------- quantizers
+// Restated from sageattention_sm80.cu:759-886 with the same expressions so
+// that, compiled with the same fast-math flags, the codes and scales match
+// the reference bit for bit.
+
+__device__ __forceinline__ int8_t cvt_rni_sat_s8(float x) {
+  uint32_t d;
+  asm volatile("cvt.rni.sat.s8.f32 %0, %1;" : "=r"(d) : "f"(x));
+  return static_cast<int8_t>(d & 0xff);
+}
+
+// Per (head, dim): serial sum over tokens in order (the reference's order),
+// 32 dims per warp so each token read is one 64-byte segment.
+__global__ void sage_kmean_kernel(const __half* __restrict__ k, float* __restrict__ kmean, int S) {
+  const int bh = blockIdx.x;
+  const int d = blockIdx.y * 32 + threadIdx.x;
+  const __half* p = k + static_cast<size_t>(bh) * S * 128 + d;
+  float sum = 0.0f;
+  int s = 0;
+  for (; s + 8 <= S; s += 8) {
+    __half h[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) h[i] = p[static_cast<size_t>(s + i) * 128];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) sum += __half2float(h[i]);
+  }
+  for (; s < S; ++s) sum += __half2float(p[static_cast<size_t>(s) * 128]);
+  kmean[bh * 128 + d] = sum / fmaxf(static_cast<float>(S), 1.0f);
+}
+
+__device__ __forceinline__ float block128_max(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  return fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+}
+
+__global__ void sage_quant_q_kernel(const __half* __restrict__ q, int8_t* __restrict__ qc, float* __restrict__ qs,
+                                    int S) {
+  __shared__ float red[4];
+  __shared__ float block_scale;
+  const int group = blockIdx.x, bh = blockIdx.y, d = threadIdx.x;
+  const int token_base = (group / 32) * 128 + ((group % 32) / 8) * 32 + (group % 8);
+  const __half* hp = q + static_cast<size_t>(bh) * S * 128;
+  float vals[4];
+  float amax = 1e-7f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int t = token_base + i * 8;
+    float v = 0.0f;
+    if (t < S) v = __half2float(hp[static_cast<size_t>(t) * 128 + d]);
+    vals[i] = v;
+    amax = fmaxf(amax, fabsf(v));
+  }
+  const float block_amax = block128_max(amax, red);
+  if (threadIdx.x == 0) {
+    block_scale = block_amax / 127.0f + 1e-7f;
+    qs[static_cast<size_t>(bh) * (((S + 127) / 128) * 32) + group] = block_scale;
+  }
+  __syncthreads();
+  const float inv_scale = 1.0f / block_scale;
+  int8_t* out = qc + static_cast<size_t>(bh) * S * 128;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int t = token_base + i * 8;
+    if (t < S) out[static_cast<size_t>(t) * 128 + d] = cvt_rni_sat_s8(vals[i] * inv_scale);
+  }
+}
+
+__global__ void sage_quant_k_kernel(const __half* __restrict__ k, const float* __restrict__ kmean,
+                                    int8_t* __restrict__ kc, float* __restrict__ ks, int S) {
+  __shared__ float red[4];
+  __shared__ float block_scale;
+  const int group = blockIdx.x, bh = blockIdx.y, d = threadIdx.x;
+  const int token_base = (group / 4) * 64 + (group % 4) * 2;
+  const __half* hp = k + static_cast<size_t>(bh) * S * 128;
+  const float mean = kmean[bh * 128 + d];
+  float vals[16];
+  float amax = 1e-7f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int t0 = token_base + i * 8, t1 = t0 + 1;
+    float v0 = 0.0f, v1 = 0.0f;
+    if (t0 < S) v0 = __half2float(hp[static_cast<size_t>(t0) * 128 + d]) - mean;
+    if (t1 < S) v1 = __half2float(hp[static_cast<size_t>(t1) * 128 + d]) - mean;
+    vals[2 * i] = v0;
+    vals[2 * i + 1] = v1;
+    amax = fmaxf(amax, fabsf(v0));
+    amax = fmaxf(amax, fabsf(v1));
+  }
+  const float block_amax = block128_max(amax, red);
+  if (threadIdx.x == 0) {
+    block_scale = block_amax / 127.0f + 1e-7f;
+    ks[static_cast<size_t>(bh) * (((S + 63) / 64) * 4) + group] = block_scale;
+  }
+  __syncthreads();
+  const float inv_scale = 1.0f / block_scale;
+  int8_t* out = kc + static_cast<size_t>(bh) * S * 128;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int t0 = token_base + i * 8, t1 = t0 + 1;
+    if (t0 < S) out[static_cast<size_t>(t0) * 128 + d] = cvt_rni_sat_s8(vals[2 * i] * inv_scale);
+    if (t1 < S) out[static_cast<size_t>(t1) * 128 + d] = cvt_rni_sat_s8(vals[2 * i + 1] * inv_scale);
+  }
+}
+
+int sage_quantize_launch(const void* q, const void* k, int BH, int S, float* kmean, int8_t* qc, float* qs, int8_t* kc,
+                         float* ks, cudaStream_t stream) {
+  if (BH <= 0 || S <= 0) return QI_ERR_ARG;
+  sage_kmean_kernel<<<dim3(BH, 4), 32, 0, stream>>>(reinterpret_cast<const __half*>(k), kmean, S);
+  sage_quant_q_kernel<<<dim3(((S + 127) / 128) * 32, BH), 128, 0, stream>>>(reinterpret_cast<const __half*>(q), qc,
+                                                                           qs, S);
+  sage_quant_k_kernel<<<dim3(((S + 63) / 64) * 4, BH), 128, 0, stream>>>(reinterpret_cast<const __half*>(k), kmean,
+                                                                         kc, ks, S);
+  return cudaGetLastError() == cudaSuccess ? QI_OK : QI_ERR_CUDA;
+}
+
+static int encode_3d(CUtensorMap* tm, CUtensorMapDataType dt, int esize, const void* base, int S, int BH,
+                     int box_d) {
+  cuuint64_t dims[3] = {128, static_cast<cuuint64_t>(S), static_cast<cuuint64_t>(BH)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(128 * esize), static_cast<cuuint64_t>(S) * 128 * esize};
+  cuuint32_t box[3] = {static_cast<cuuint32_t>(box_d), 128, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = qi_encode_tiled(tm, dt, 3, const_cast<void*>(base), dims, strides, box, estr,
+                                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? QI_OK : QI_ERR_CUDA;
+}
+
+int attention_launch(const AttnArgs& a, cudaStream_t stream, int* err_dev) {
+  if (a.BH <= 0 || a.S <= 0) return QI_ERR_ARG;
+  if ((reinterpret_cast<uintptr_t>(a.qc) & 15) || (reinterpret_cast<uintptr_t>(a.kc) & 15) ||
+      (reinterpret_cast<uintptr_t>(a.v) & 15) || (reinterpret_cast<uintptr_t>(a.out) & 15))
+    return QI_ERR_ALIGN;
+  static bool attr = false;
+  if (!attr) {
+    if (cudaFuncSetAttribute(sage_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, attn::SMEM_BYTES) !=
+        cudaSuccess)
+      return QI_ERR_CUDA;
+    attr = true;
+  }
+  AttnArgsDev d;
+  memset(&d, 0, sizeof(d));
+  if (encode_3d(&d.tmQ, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a.qc, a.S, a.BH, 128) != QI_OK) return QI_ERR_CUDA;
+  if (encode_3d(&d.tmK, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a.kc, a.S, a.BH, 128) != QI_OK) return QI_ERR_CUDA;
+  if (encode_3d(&d.tmV, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, a.v, a.S, a.BH, 64) != QI_OK) return QI_ERR_CUDA;
+  d.qs = a.qs;
+  d.ks = a.ks;
+  d.out = a.out;
+  d.BH = a.BH;
+  d.S = a.S;
+  d.heads = a.heads;
+  d.out_mode = a.out_mode;
+  d.nb = a.nb;
+  d.n_img = a.n_img;
+  d.n_txt = a.n_txt;
+  d.ngq = ((a.S + 127) / 128) * 32;
+  d.ngk = ((a.S + 63) / 64) * 4;
+  d.qk_scale = a.sm_scale * 1.44269504088896340736f;
+  d.err = err_dev;
+  dim3 grid((a.S + attn::BQ - 1) / attn::BQ, a.BH);
+  sage_attn_kernel<<<grid, attn::THREADS, attn::SMEM_BYTES, stream>>>(d);
+  return cudaGetLastError() == cudaSuccess ? QI_OK : QI_ERR_CUDA;
+}
+
+}  // namespace qi

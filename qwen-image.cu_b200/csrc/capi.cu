@@ -1,0 +1,639 @@
+// capi.cu -- the C ABI (include/qwen_image_b200.h) and the MMDiT forward.
+//
+// The forward follows transformer_forward (transformer.cu:234-931) step for
+// step, with the reference's per-op launches fused:
+//   reference (per block, per stream)               here (per block, both streams)
+//   LN+mod; FWHT+quant                        ->    rowquant<LnMod>        (1 launch)
+//   3 x (cuBLAS INT8 + dequant)               ->    fused-QKV tcgen05 GEMM  (1, img+txt grouped)
+//   4 x RMSNorm; 3 x concat/transpose; 2 x RoPE ->  qkv_post               (1)
+//   k_mean; Q quant; K quant; attention; h->f  ->   sage quant (3) + tcgen05 attention (1)
+//   transpose/split; FWHT+quant                ->   rowquant<F16>          (1)
+//   cuBLAS + dequant; gate_add                 ->   GEMM, residual epilogue (1)
+//   LN+mod; FWHT+quant                         ->   rowquant<LnMod>        (1)
+//   fc1 cuBLAS + dequant+GELU; FWHT+quant      ->   GEMM GELU epilogue (1) + rowquant (1)
+//   fc2 cuBLAS + dequant; gate_add             ->   GEMM, residual epilogue (1)
+// The 120 modulation linears of a forward depend only on the timestep
+// (transformer.cu:506-515) and run as one GEMV over the stacked weights.
+// `nb` batch elements (CFG cond/uncond) share every launch.
+#include "qi_internal.h"
+#include "sm100.cuh"
+
+#include <cuda_bf16.h>
+
+#include <map>
+#include <mutex>
+#include <string>
+#include <vector>
+
+namespace qi {
+int synth_launch(uint64_t seed, long long n, float scale, float offset, void* out, int bf16, cudaStream_t stream);
+uint64_t synth_seed_for(uint64_t base, const char* name);
+int rope_table_host(int h, int w, int n_txt, float* pe);
+
+CUresult qi_encode_tiled(CUtensorMap* tm, CUtensorMapDataType dt, cuuint32_t rank, void* base, const cuuint64_t* dims,
+                         const cuuint64_t* strides, const cuuint32_t* box, const cuuint32_t* estr,
+                         CUtensorMapInterleave il, CUtensorMapSwizzle sw, CUtensorMapL2promotion l2,
+                         CUtensorMapFloatOOBfill oob) {
+  using Fn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*, const cuuint64_t*,
+                          const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                          CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+  static Fn fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess || !p)
+      return CUDA_ERROR_NOT_FOUND;
+    fn = reinterpret_cast<Fn>(p);
+  }
+  return fn(tm, dt, rank, base, dims, strides, box, estr, il, sw, l2, oob);
+}
+
+int device_num_sms() {
+  int dev = 0, n = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n;
+}
+}  // namespace qi
+
+using namespace qi;
+
+#define QI_TRY(expr)              \
+  do {                            \
+    int _st = (expr);             \
+    if (_st != QI_OK) return _st; \
+  } while (0)
+
+static inline cudaStream_t S_(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+// ------------------------------------------------------------------ context
+enum BufId {
+  B_PATCH, B_TEMB256, B_TACT, B_TACT_S, B_T1, B_TEMB, B_TSILU, B_MODS, B_ADA, B_X, B_TXTN, B_ACT, B_ACT_S, B_QKV,
+  B_QH, B_KH, B_VH, B_QC, B_KC, B_QS, B_KS, B_KMEAN, B_O, B_H, B_FIN, B_PROJ, B_COUNT
+};
+
+struct qi_ctx {
+  int device = 0;
+  int num_sms = 148;
+  int* err = nullptr;  // device error word
+  void* buf[B_COUNT] = {};
+  size_t cap[B_COUNT] = {};
+  int launches = 0;
+  // stage profiler (qi_ctx_set_profiling): event pairs recorded around each
+  // launch of a forward, resolved lazily in qi_ctx_profile
+  bool profiling = false;
+  std::vector<std::pair<int, std::pair<cudaEvent_t, cudaEvent_t>>> pending;
+  std::vector<cudaEvent_t> pool;
+  int prof_launches[QI_PROF_COUNT] = {};
+  double prof_ms[QI_PROF_COUNT] = {};
+
+  cudaEvent_t ev() {
+    if (!pool.empty()) {
+      cudaEvent_t e = pool.back();
+      pool.pop_back();
+      return e;
+    }
+    cudaEvent_t e;
+    cudaEventCreate(&e);
+    return e;
+  }
+
+  int ensure(int id, size_t bytes) {
+    bytes = (bytes + 255) & ~size_t(255);
+    if (cap[id] >= bytes) return QI_OK;
+    if (buf[id]) cudaFree(buf[id]);
+    buf[id] = nullptr;
+    cap[id] = 0;
+    if (cudaMalloc(&buf[id], bytes) != cudaSuccess) return QI_ERR_OOM;
+    cap[id] = bytes;
+    return QI_OK;
+  }
+  template <typename T>
+  T* p(int id) const {
+    return reinterpret_cast<T*>(buf[id]);
+  }
+};
+
+// ------------------------------------------------------------------ model
+struct Lin {  // INT8 linear in kernel layout
+  int8_t* w = nullptr;
+  float* s = nullptr;
+  __nv_bfloat16* b = nullptr;
+  int N = 0, K = 0;
+};
+struct BlockW {
+  Lin qkv[2], out[2], fc1[2], fc2[2];  // [0] image stream, [1] text stream
+  __nv_bfloat16* norms = nullptr;       // [4][128]: q, k, added_q, added_k
+};
+struct qi_model {
+  int nblocks = 0;
+  Lin t1, t2;
+  Lin mod;  // stacked [nblocks][2][18432][3072]
+  __nv_bfloat16 *txt_norm = nullptr, *img_in_w = nullptr, *img_in_b = nullptr, *txt_in_w = nullptr,
+                *txt_in_b = nullptr, *norm_out_w = nullptr, *norm_out_b = nullptr, *proj_out_w = nullptr,
+                *proj_out_b = nullptr;
+  std::vector<BlockW> blocks;
+  std::vector<void*> allocs;
+
+  template <typename T>
+  T* alloc(size_t n) {
+    void* p = nullptr;
+    if (cudaMalloc(&p, n * sizeof(T)) != cudaSuccess) return nullptr;
+    allocs.push_back(p);
+    return reinterpret_cast<T*>(p);
+  }
+  ~qi_model() {
+    for (void* p : allocs) cudaFree(p);
+  }
+};
+
+extern "C" {
+
+const char* qi_status_string(int st) {
+  switch (st) {
+    case QI_OK: return "ok";
+    case QI_ERR_ARG: return "invalid argument";
+    case QI_ERR_ALIGN: return "pointer or leading dimension not 16-byte aligned";
+    case QI_ERR_CUDA: return "CUDA call failed";
+    case QI_ERR_OOM: return "device allocation failed";
+    case QI_ERR_UNSUPPORTED: return "shape not supported by the kernels";
+    case QI_ERR_IO: return "file missing or malformed";
+    case QI_ERR_DEVICE: return "kernel bounded wait timed out";
+    case QI_ERR_NCCL: return "collective failed";
+    default: return "unknown status";
+  }
+}
+
+int qi_version(void) { return 1; }
+
+int qi_ctx_create(int device, qi_ctx** out) {
+  if (!out) return QI_ERR_ARG;
+  if (cudaSetDevice(device) != cudaSuccess) return QI_ERR_CUDA;
+  qi_ctx* c = new qi_ctx();
+  c->device = device;
+  c->num_sms = device_num_sms();
+  if (cudaMalloc(&c->err, sizeof(int)) != cudaSuccess) {
+    delete c;
+    return QI_ERR_OOM;
+  }
+  cudaMemset(c->err, 0, sizeof(int));
+  *out = c;
+  return QI_OK;
+}
+
+int qi_ctx_destroy(qi_ctx* c) {
+  if (!c) return QI_OK;
+  for (auto& p : c->pending) {
+    cudaEventDestroy(p.second.first);
+    cudaEventDestroy(p.second.second);
+  }
+  for (cudaEvent_t e : c->pool) cudaEventDestroy(e);
+  for (int i = 0; i < B_COUNT; ++i)
+    if (c->buf[i]) cudaFree(c->buf[i]);
+  if (c->err) cudaFree(c->err);
+  delete c;
+  return QI_OK;
+}
+
+int qi_ctx_check(qi_ctx* c) {
+  if (!c) return QI_ERR_ARG;
+  int h = 0;
+  if (cudaMemcpy(&h, c->err, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return QI_ERR_CUDA;
+  if (h) cudaMemset(c->err, 0, sizeof(int));
+  return h ? QI_ERR_DEVICE : QI_OK;
+}
+
+int qi_ctx_last_launch_count(const qi_ctx* c) { return c ? c->launches : 0; }
+
+int qi_ctx_set_profiling(qi_ctx* c, int enable) {
+  if (!c) return QI_ERR_ARG;
+  c->profiling = enable != 0;
+  return QI_OK;
+}
+
+int qi_ctx_profile(qi_ctx* c, int* launches, float* ms, int reset) {
+  if (!c) return QI_ERR_ARG;
+  for (auto& p : c->pending) {
+    if (cudaEventSynchronize(p.second.second) != cudaSuccess) return QI_ERR_CUDA;
+    float t = 0.0f;
+    cudaEventElapsedTime(&t, p.second.first, p.second.second);
+    c->prof_ms[p.first] += t;
+    c->prof_launches[p.first] += 1;
+    c->pool.push_back(p.second.first);
+    c->pool.push_back(p.second.second);
+  }
+  c->pending.clear();
+  for (int i = 0; i < QI_PROF_COUNT; ++i) {
+    if (launches) launches[i] = c->prof_launches[i];
+    if (ms) ms[i] = static_cast<float>(c->prof_ms[i]);
+    if (reset) {
+      c->prof_launches[i] = 0;
+      c->prof_ms[i] = 0.0;
+    }
+  }
+  return QI_OK;
+}
+
+int qi_cfg_euler_step(float* latent, const void* cond_bf16, const void* uncond_bf16, float cfg_scale, float sigma,
+                      float sigma_next, int H, int W, void* latent_bf16, void* stream) {
+  if (!latent || !cond_bf16 || !uncond_bf16 || !latent_bf16 || sigma == 0.0f) return QI_ERR_ARG;
+  return cfg_euler_launch(latent, cond_bf16, uncond_bf16, cfg_scale, sigma, sigma_next, H, W, latent_bf16,
+                          reinterpret_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"
+
+// Default per-device context for the op-level entry points (they take no
+// context, like the reference's functions that use static workspaces).
+static qi_ctx* default_ctx() {
+  static std::mutex mu;
+  static std::map<int, qi_ctx*> ctxs;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = ctxs.find(dev);
+  if (it != ctxs.end()) return it->second;
+  qi_ctx* c = nullptr;
+  if (qi_ctx_create(dev, &c) != QI_OK) return nullptr;
+  ctxs[dev] = c;
+  return c;
+}
+
+extern "C" {
+
+// ------------------------------------------------------------------ op level
+int qi_quantize_weight(const void* w_bf16, int N, int K, int8_t* codes, float* scales, void* stream) {
+  if (!w_bf16 || !codes || !scales || N < 0 || K <= 0) return QI_ERR_ARG;
+  return fwht_quant_generic(w_bf16, 1, N, K, K & (-K), codes, scales, S_(stream));
+}
+
+int qi_fwht_quantize(const float* x, int M, int K, int had_block, int8_t* codes, float* scales, void* stream) {
+  if (!x || !codes || !scales || M < 0 || K <= 0) return QI_ERR_ARG;
+  if (had_block < 1) had_block = 1;
+  if ((K == 3072 || K == 12288 || K == 256) && ((reinterpret_cast<uintptr_t>(x) & 15) == 0)) {
+    RowSeg seg{x, K, nullptr, nullptr, M};
+    int st = rowquant_launch(kSrcF32, K, had_block, &seg, 1, codes, scales, 0.0f, S_(stream));
+    if (st != QI_ERR_UNSUPPORTED) return st;
+  }
+  return fwht_quant_generic(x, 0, M, K, had_block, codes, scales, S_(stream));
+}
+
+int qi_linear_i8(const int8_t* act, const float* act_scales, int M, int K, const int8_t* w, const float* w_scales,
+                 int N, const void* bias_bf16, int epilogue, const float* gate, float* out, int ldo, void* stream) {
+  if (!act || !act_scales || !w || !w_scales || !out || epilogue < 0 || epilogue > 2) return QI_ERR_ARG;
+  qi_ctx* c = default_ctx();
+  if (!c) return QI_ERR_CUDA;
+  GemmDesc d{act, act_scales, w, w_scales, bias_bf16, out, gate, M, N, K, ldo};
+  return gemm_i8_launch(&d, 1, epilogue, S_(stream), c->err, c->num_sms);
+}
+
+int qi_linear_i8_f32in(const float* x, int M, int K, const int8_t* w, const float* w_scales, int N,
+                       const void* bias_bf16, int apply_gelu, float* out, void* stream) {
+  qi_ctx* c = default_ctx();
+  if (!c) return QI_ERR_CUDA;
+  QI_TRY(c->ensure(B_ACT, static_cast<size_t>(M) * K));
+  QI_TRY(c->ensure(B_ACT_S, static_cast<size_t>(M) * 4));
+  QI_TRY(qi_fwht_quantize(x, M, K, K & (-K), c->p<int8_t>(B_ACT), c->p<float>(B_ACT_S), stream));
+  if (M == 1 && !apply_gelu) {
+    GemvJob j{w, w_scales, bias_bf16, out, N};
+    return gemv_i8_launch(c->p<int8_t>(B_ACT), c->p<float>(B_ACT_S), K, &j, 1, S_(stream));
+  }
+  GemmDesc d{c->p<int8_t>(B_ACT), c->p<float>(B_ACT_S), w, w_scales, bias_bf16, out, nullptr, M, N, K, N};
+  return gemm_i8_launch(&d, 1, apply_gelu ? kEpiGelu : kEpiStore, S_(stream), c->err, c->num_sms);
+}
+
+int qi_sage_quantize(const void* q_f16, const void* k_f16, int BH, int S, float* k_mean, int8_t* q_codes,
+                     float* q_scales, int8_t* k_codes, float* k_scales, void* stream) {
+  if (!q_f16 || !k_f16 || !k_mean || !q_codes || !q_scales || !k_codes || !k_scales) return QI_ERR_ARG;
+  return sage_quantize_launch(q_f16, k_f16, BH, S, k_mean, q_codes, q_scales, k_codes, k_scales, S_(stream));
+}
+
+int qi_sage_attention(const void* q_f16, const void* k_f16, const void* v_f16, float* out, float scale, int BH, int S,
+                      int D, void* stream) {
+  if (D != 128) return QI_ERR_UNSUPPORTED;
+  if (!q_f16 || !k_f16 || !v_f16 || !out || BH <= 0 || S <= 0) return QI_ERR_ARG;
+  qi_ctx* c = default_ctx();
+  if (!c) return QI_ERR_CUDA;
+  const size_t n = static_cast<size_t>(BH) * S * 128;
+  QI_TRY(c->ensure(B_QC, n));
+  QI_TRY(c->ensure(B_KC, n));
+  QI_TRY(c->ensure(B_QS, static_cast<size_t>(BH) * ((S + 127) / 128) * 32 * 4));
+  QI_TRY(c->ensure(B_KS, static_cast<size_t>(BH) * ((S + 63) / 64) * 4 * 4));
+  QI_TRY(c->ensure(B_KMEAN, static_cast<size_t>(BH) * 128 * 4));
+  QI_TRY(sage_quantize_launch(q_f16, k_f16, BH, S, c->p<float>(B_KMEAN), c->p<int8_t>(B_QC), c->p<float>(B_QS),
+                              c->p<int8_t>(B_KC), c->p<float>(B_KS), S_(stream)));
+  AttnArgs a{c->p<int8_t>(B_QC), c->p<float>(B_QS), c->p<int8_t>(B_KC), c->p<float>(B_KS), v_f16, out, BH, S, BH,
+             scale, 0, 1, 0, 0};
+  return attention_launch(a, S_(stream), c->err);
+}
+
+int qi_layer_norm_modulate(const float* x, const float* shift, const float* scale, float* out, int rows, int dim,
+                           float eps, void* stream) {
+  if (!x || !shift || !scale || !out || rows < 0 || dim <= 0) return QI_ERR_ARG;
+  return layernorm_mod_launch(x, shift, scale, rows, dim, eps, out, nullptr, S_(stream));
+}
+
+int qi_rms_norm(const float* x, const void* w_bf16, float* out, int rows, int dim, float eps, void* stream) {
+  if (!x || !w_bf16 || !out || rows < 0 || dim <= 0) return QI_ERR_ARG;
+  return rmsnorm_f32_launch(x, w_bf16, out, rows, dim, eps, S_(stream));
+}
+
+int qi_rope_table(int h, int w, int n_txt, float* pe_host) {
+  if (!pe_host || h <= 0 || w <= 0 || n_txt < 0) return QI_ERR_ARG;
+  return rope_table_host(h, w, n_txt, pe_host);
+}
+
+// Synthetic tensors (benchmarks and tests): value i = z_i * scale + offset.
+int qi_synth_fill(void* out, long long n, unsigned long long seed, float scale, float offset, int bf16, void* stream) {
+  if (!out || n < 0) return QI_ERR_ARG;
+  return synth_launch(seed, n, scale, offset, out, bf16, S_(stream));
+}
+unsigned long long qi_seed_for(unsigned long long base, const char* name) { return synth_seed_for(base, name); }
+
+// ------------------------------------------------------------------ model
+int qi_model_num_blocks(const qi_model* m) { return m ? m->nblocks : 0; }
+
+int qi_model_destroy(qi_model* m) {
+  delete m;
+  return QI_OK;
+}
+
+}  // extern "C"
+
+static int copy_lin(qi_model* m, Lin& L, const void* const* t, int base, int N, int K) {
+  L.N = N;
+  L.K = K;
+  L.w = m->alloc<int8_t>(static_cast<size_t>(N) * K);
+  L.s = m->alloc<float>(N);
+  L.b = m->alloc<__nv_bfloat16>(N);
+  if (!L.w || !L.s || !L.b) return QI_ERR_OOM;
+  if (!t[base] || !t[base + 1]) return QI_ERR_ARG;
+  cudaMemcpyAsync(L.w, t[base], static_cast<size_t>(N) * K, cudaMemcpyDeviceToDevice);
+  cudaMemcpyAsync(L.s, t[base + 1], N * 4, cudaMemcpyDeviceToDevice);
+  if (t[base + 2])
+    cudaMemcpyAsync(L.b, t[base + 2], N * 2, cudaMemcpyDeviceToDevice);
+  else
+    cudaMemsetAsync(L.b, 0, N * 2);
+  return QI_OK;
+}
+
+// Concatenates three [N,K] linears along N (Q, K, V share one quantized
+// activation, transformer.cu:217-230 can_share_qkv_quant).
+static int copy_fused3(qi_model* m, Lin& L, const void* const* t, int l0, int l1, int l2) {
+  const int N = 3 * kDim, K = kDim;
+  L.N = N;
+  L.K = K;
+  L.w = m->alloc<int8_t>(static_cast<size_t>(N) * K);
+  L.s = m->alloc<float>(N);
+  L.b = m->alloc<__nv_bfloat16>(N);
+  if (!L.w || !L.s || !L.b) return QI_ERR_OOM;
+  const int ls[3] = {l0, l1, l2};
+  for (int i = 0; i < 3; ++i) {
+    const void* const* e = t + 3 * ls[i];
+    if (!e[0] || !e[1]) return QI_ERR_ARG;
+    cudaMemcpyAsync(L.w + static_cast<size_t>(i) * kDim * K, e[0], static_cast<size_t>(kDim) * K,
+                    cudaMemcpyDeviceToDevice);
+    cudaMemcpyAsync(L.s + i * kDim, e[1], kDim * 4, cudaMemcpyDeviceToDevice);
+    if (e[2])
+      cudaMemcpyAsync(L.b + i * kDim, e[2], kDim * 2, cudaMemcpyDeviceToDevice);
+    else
+      cudaMemsetAsync(L.b + i * kDim, 0, kDim * 2);
+  }
+  return QI_OK;
+}
+
+static __nv_bfloat16* copy_bf16(qi_model* m, const void* src, size_t n) {
+  __nv_bfloat16* d = m->alloc<__nv_bfloat16>(n);
+  if (!d) return nullptr;
+  if (src)
+    cudaMemcpyAsync(d, src, n * 2, cudaMemcpyDeviceToDevice);
+  else
+    cudaMemsetAsync(d, 0, n * 2);
+  return d;
+}
+
+extern "C" int qi_model_create(qi_ctx* ctx, int num_blocks, const void* const* g, const void* const* const* bt,
+                               qi_model** out) {
+  if (!ctx || !g || !bt || !out || num_blocks <= 0) return QI_ERR_ARG;
+  cudaSetDevice(ctx->device);
+  qi_model* m = new qi_model();
+  m->nblocks = num_blocks;
+  int st = QI_OK;
+  auto fail = [&](int s) {
+    delete m;
+    return s;
+  };
+  if ((st = copy_lin(m, m->t1, g, QI_G_T1_W, kDim, 256)) != QI_OK) return fail(st);
+  if ((st = copy_lin(m, m->t2, g, QI_G_T2_W, kDim, kDim)) != QI_OK) return fail(st);
+  if (!g[QI_G_IMG_IN_W] || !g[QI_G_TXT_IN_W] || !g[QI_G_NORM_OUT_W] || !g[QI_G_PROJ_OUT_W] || !g[QI_G_TXT_NORM])
+    return fail(QI_ERR_ARG);
+  m->txt_norm = copy_bf16(m, g[QI_G_TXT_NORM], kTxtDim);
+  m->img_in_w = copy_bf16(m, g[QI_G_IMG_IN_W], static_cast<size_t>(kDim) * kPatchDim);
+  m->img_in_b = copy_bf16(m, g[QI_G_IMG_IN_B], kDim);
+  m->txt_in_w = copy_bf16(m, g[QI_G_TXT_IN_W], static_cast<size_t>(kDim) * kTxtDim);
+  m->txt_in_b = copy_bf16(m, g[QI_G_TXT_IN_B], kDim);
+  m->norm_out_w = copy_bf16(m, g[QI_G_NORM_OUT_W], static_cast<size_t>(2 * kDim) * kDim);
+  m->norm_out_b = copy_bf16(m, g[QI_G_NORM_OUT_B], 2 * kDim);
+  m->proj_out_w = copy_bf16(m, g[QI_G_PROJ_OUT_W], static_cast<size_t>(kPatchDim) * kDim);
+  m->proj_out_b = copy_bf16(m, g[QI_G_PROJ_OUT_B], kPatchDim);
+  // stacked modulation: [block][img, txt][18432][3072]
+  const size_t modN = static_cast<size_t>(num_blocks) * 2 * 6 * kDim;
+  m->mod.N = static_cast<int>(modN);
+  m->mod.K = kDim;
+  m->mod.w = m->alloc<int8_t>(modN * kDim);
+  m->mod.s = m->alloc<float>(modN);
+  m->mod.b = m->alloc<__nv_bfloat16>(modN);
+  if (!m->mod.w || !m->mod.s || !m->mod.b) return fail(QI_ERR_OOM);
+  m->blocks.resize(num_blocks);
+  for (int i = 0; i < num_blocks; ++i) {
+    const void* const* t = bt[i];
+    if (!t) return fail(QI_ERR_ARG);
+    for (int sidx = 0; sidx < 2; ++sidx) {
+      const int l = sidx == 0 ? QI_L_IMG_MOD : QI_L_TXT_MOD;
+      const size_t row0 = (static_cast<size_t>(i) * 2 + sidx) * 6 * kDim;
+      if (!t[3 * l] || !t[3 * l + 1]) return fail(QI_ERR_ARG);
+      cudaMemcpyAsync(m->mod.w + row0 * kDim, t[3 * l], static_cast<size_t>(6) * kDim * kDim, cudaMemcpyDeviceToDevice);
+      cudaMemcpyAsync(m->mod.s + row0, t[3 * l + 1], 6 * kDim * 4, cudaMemcpyDeviceToDevice);
+      if (t[3 * l + 2])
+        cudaMemcpyAsync(m->mod.b + row0, t[3 * l + 2], 6 * kDim * 2, cudaMemcpyDeviceToDevice);
+      else
+        cudaMemsetAsync(m->mod.b + row0, 0, 6 * kDim * 2);
+    }
+    BlockW& B = m->blocks[i];
+    if ((st = copy_fused3(m, B.qkv[0], t, QI_L_TO_Q, QI_L_TO_K, QI_L_TO_V)) != QI_OK) return fail(st);
+    if ((st = copy_fused3(m, B.qkv[1], t, QI_L_ADD_Q, QI_L_ADD_K, QI_L_ADD_V)) != QI_OK) return fail(st);
+    if ((st = copy_lin(m, B.out[0], t, 3 * QI_L_TO_OUT, kDim, kDim)) != QI_OK) return fail(st);
+    if ((st = copy_lin(m, B.out[1], t, 3 * QI_L_TO_ADD_OUT, kDim, kDim)) != QI_OK) return fail(st);
+    if ((st = copy_lin(m, B.fc1[0], t, 3 * QI_L_IMG_FC1, kMlp, kDim)) != QI_OK) return fail(st);
+    if ((st = copy_lin(m, B.fc2[0], t, 3 * QI_L_IMG_FC2, kDim, kMlp)) != QI_OK) return fail(st);
+    if ((st = copy_lin(m, B.fc1[1], t, 3 * QI_L_TXT_FC1, kMlp, kDim)) != QI_OK) return fail(st);
+    if ((st = copy_lin(m, B.fc2[1], t, 3 * QI_L_TXT_FC2, kDim, kMlp)) != QI_OK) return fail(st);
+    B.norms = m->alloc<__nv_bfloat16>(4 * kHeadDim);
+    if (!B.norms) return fail(QI_ERR_OOM);
+    for (int k = 0; k < 4; ++k) {
+      if (!t[QI_B_NORM_Q + k]) return fail(QI_ERR_ARG);
+      cudaMemcpyAsync(B.norms + k * kHeadDim, t[QI_B_NORM_Q + k], kHeadDim * 2, cudaMemcpyDeviceToDevice);
+    }
+  }
+  if (cudaDeviceSynchronize() != cudaSuccess) return fail(QI_ERR_CUDA);
+  *out = m;
+  return QI_OK;
+}
+
+// ------------------------------------------------------------------ forward
+extern "C" int qi_forward(qi_ctx* c, const qi_model* m, int nb, const void* x, float timestep, const void* ctx_txt,
+                          int n_txt, const float* pe, int H, int W, void* out, void* stream_) {
+  if (!c || !m || !x || !ctx_txt || !pe || !out) return QI_ERR_ARG;
+  if (nb < 1 || nb > 8 || n_txt < 1 || H < 2 || W < 2 || (H & 1) || (W & 1)) return QI_ERR_ARG;
+  cudaStream_t s = S_(stream_);
+  const int n_img = (H / 2) * (W / 2);
+  const int S = n_img + n_txt;
+  const long long Mi = static_cast<long long>(nb) * n_img, Mt = static_cast<long long>(nb) * n_txt, Ma = Mi + Mt;
+  const int BH = nb * kHeads;
+  const size_t hs = static_cast<size_t>(BH) * S * kHeadDim;
+  const int L = m->nblocks;
+
+  QI_TRY(c->ensure(B_PATCH, Mi * kPatchDim * 2));
+  QI_TRY(c->ensure(B_TEMB256, 256 * 4));
+  QI_TRY(c->ensure(B_TACT, kDim));
+  QI_TRY(c->ensure(B_TACT_S, 16));
+  QI_TRY(c->ensure(B_T1, kDim * 4));
+  QI_TRY(c->ensure(B_TEMB, kDim * 4));
+  QI_TRY(c->ensure(B_TSILU, kDim * 4));
+  QI_TRY(c->ensure(B_MODS, static_cast<size_t>(m->mod.N) * 4));
+  QI_TRY(c->ensure(B_ADA, 2 * kDim * 4));
+  QI_TRY(c->ensure(B_X, Ma * kDim * 4));
+  QI_TRY(c->ensure(B_TXTN, Mt * kTxtDim * 2));
+  QI_TRY(c->ensure(B_ACT, Ma * kMlp));
+  QI_TRY(c->ensure(B_ACT_S, Ma * 4));
+  QI_TRY(c->ensure(B_QKV, Ma * 3 * kDim * 4));
+  QI_TRY(c->ensure(B_QH, hs * 2));
+  QI_TRY(c->ensure(B_KH, hs * 2));
+  QI_TRY(c->ensure(B_VH, hs * 2));
+  QI_TRY(c->ensure(B_QC, hs));
+  QI_TRY(c->ensure(B_KC, hs));
+  QI_TRY(c->ensure(B_QS, static_cast<size_t>(BH) * ((S + 127) / 128) * 32 * 4));
+  QI_TRY(c->ensure(B_KS, static_cast<size_t>(BH) * ((S + 63) / 64) * 4 * 4));
+  QI_TRY(c->ensure(B_KMEAN, static_cast<size_t>(BH) * kHeadDim * 4));
+  QI_TRY(c->ensure(B_O, Ma * kDim * 2));
+  QI_TRY(c->ensure(B_H, Ma * kMlp * 4));
+  QI_TRY(c->ensure(B_FIN, Mi * kDim * 2));
+  QI_TRY(c->ensure(B_PROJ, Mi * kPatchDim * 4));
+
+  // One launch (or a fixed group) per QI_LAUNCH; with profiling on, an event
+  // pair brackets it on the stream and is resolved in qi_ctx_profile.
+#define QI_LAUNCH(stage, count, expr)                                 \
+  do {                                                                \
+    cudaEvent_t e0 = nullptr, e1 = nullptr;                           \
+    if (c->profiling) {                                               \
+      e0 = c->ev();                                                   \
+      e1 = c->ev();                                                   \
+      cudaEventRecord(e0, s);                                         \
+    }                                                                 \
+    QI_TRY(expr);                                                     \
+    if (c->profiling) {                                               \
+      cudaEventRecord(e1, s);                                         \
+      c->pending.push_back({stage, {e0, e1}});                        \
+    }                                                                 \
+    n += (count);                                                     \
+  } while (0)
+  int8_t* act = c->p<int8_t>(B_ACT);
+  float* act_s = c->p<float>(B_ACT_S);
+  float* x_img = c->p<float>(B_X);
+  float* x_txt = x_img + Mi * kDim;
+  float* mods = c->p<float>(B_MODS);
+  int n = 0;  // launches
+
+  // 1. patchify (transformer.cu:266-290)
+  QI_LAUNCH(QI_PROF_PRE, 1, patchify_launch(x, c->buf[B_PATCH], nb, H, W, s));
+  // 2. timestep MLP: sinusoid -> INT8 linear -> SiLU -> INT8 linear (transformer.cu:330-349)
+  QI_LAUNCH(QI_PROF_PRE, 1, timestep_embedding_launch(timestep, c->p<float>(B_TEMB256), s));
+  {
+    RowSeg seg{c->buf[B_TEMB256], 256, nullptr, nullptr, 1};
+    QI_LAUNCH(QI_PROF_PRE, 1, rowquant_launch(kSrcF32, 256, 256, &seg, 1, c->p<int8_t>(B_TACT), c->p<float>(B_TACT_S), 0.0f, s));
+    GemvJob j1{m->t1.w, m->t1.s, m->t1.b, c->p<float>(B_T1), kDim};
+    QI_LAUNCH(QI_PROF_PRE, 1, gemv_i8_launch(c->p<int8_t>(B_TACT), c->p<float>(B_TACT_S), 256, &j1, 1, s));
+    QI_LAUNCH(QI_PROF_PRE, 1, silu_launch(c->p<float>(B_T1), c->p<float>(B_T1), kDim, s));
+    RowSeg seg2{c->buf[B_T1], kDim, nullptr, nullptr, 1};
+    QI_LAUNCH(QI_PROF_PRE, 1, rowquant_launch(kSrcF32, kDim, 1024, &seg2, 1, c->p<int8_t>(B_TACT), c->p<float>(B_TACT_S), 0.0f, s));
+    GemvJob j2{m->t2.w, m->t2.s, m->t2.b, c->p<float>(B_TEMB), kDim};
+    QI_LAUNCH(QI_PROF_PRE, 1, gemv_i8_launch(c->p<int8_t>(B_TACT), c->p<float>(B_TACT_S), kDim, &j2, 1, s));
+  }
+  // 3. all modulation vectors (transformer.cu:506-515) and the output AdaLN
+  //    embedding (transformer.cu:874-877) from SiLU(t_emb)
+  QI_LAUNCH(QI_PROF_PRE, 1, silu_launch(c->p<float>(B_TEMB), c->p<float>(B_TSILU), kDim, s));
+  {
+    RowSeg seg{c->buf[B_TSILU], kDim, nullptr, nullptr, 1};
+    QI_LAUNCH(QI_PROF_PRE, 1, rowquant_launch(kSrcF32, kDim, 1024, &seg, 1, c->p<int8_t>(B_TACT), c->p<float>(B_TACT_S), 0.0f, s));
+    GemvJob jm{m->mod.w, m->mod.s, m->mod.b, mods, m->mod.N};
+    QI_LAUNCH(QI_PROF_PRE, 1, gemv_i8_launch(c->p<int8_t>(B_TACT), c->p<float>(B_TACT_S), kDim, &jm, 1, s));
+    QI_LAUNCH(QI_PROF_PRE, 1, gemv_bf16_launch(c->p<float>(B_TSILU), m->norm_out_w, m->norm_out_b, c->p<float>(B_ADA), 2 * kDim, kDim, s));
+  }
+  // 4. img_in (BF16) and txt_norm + txt_in (BF16) (transformer.cu:396-422)
+  {
+    GemmBf16Desc d{c->buf[B_PATCH], m->img_in_w, m->img_in_b, x_img, static_cast<int>(Mi), kDim, kPatchDim, kDim};
+    QI_LAUNCH(QI_PROF_PRE, 1, gemm_bf16_launch(d, s, c->err, c->num_sms));
+    QI_LAUNCH(QI_PROF_PRE, 1, rmsnorm_bf16_launch(ctx_txt, m->txt_norm, c->buf[B_TXTN], static_cast<int>(Mt), kTxtDim, 1e-6f, s));
+    GemmBf16Desc e{c->buf[B_TXTN], m->txt_in_w, m->txt_in_b, x_txt, static_cast<int>(Mt), kDim, kTxtDim, kDim};
+    QI_LAUNCH(QI_PROF_PRE, 1, gemm_bf16_launch(e, s, c->err, c->num_sms));
+  }
+  float* qkv = c->p<float>(B_QKV);
+  float* hbuf = c->p<float>(B_H);
+  // 5. the double-stream blocks (transformer.cu:497-836)
+  for (int bi = 0; bi < L; ++bi) {
+    const BlockW& B = m->blocks[bi];
+    const float* mi = mods + (static_cast<size_t>(bi) * 2 + 0) * 6 * kDim;
+    const float* mt = mods + (static_cast<size_t>(bi) * 2 + 1) * 6 * kDim;
+    // chunk order [shift1, scale1, gate1, shift2, scale2, gate2] (transformer.cu:529-531, 742-764, 814-817)
+    RowSeg ln1[2] = {{x_img, kDim, mi + 0 * kDim, mi + 1 * kDim, static_cast<int>(Mi)},
+                     {x_txt, kDim, mt + 0 * kDim, mt + 1 * kDim, static_cast<int>(Mt)}};
+    QI_LAUNCH(QI_PROF_QUANT_LN, 1, rowquant_launch(kSrcLnMod, kDim, 1024, ln1, 2, act, act_s, 1e-6f, s));
+    GemmDesc gq[2] = {{act, act_s, B.qkv[0].w, B.qkv[0].s, B.qkv[0].b, qkv, nullptr, static_cast<int>(Mi), 3 * kDim,
+                       kDim, 3 * kDim},
+                      {act + Mi * kDim, act_s + Mi, B.qkv[1].w, B.qkv[1].s, B.qkv[1].b, qkv + Mi * 3 * kDim, nullptr,
+                       static_cast<int>(Mt), 3 * kDim, kDim, 3 * kDim}};
+    QI_LAUNCH(QI_PROF_GEMM_QKV, 1, gemm_i8_launch(gq, 2, kEpiStore, s, c->err, c->num_sms));
+    QkvPostArgs qa{qkv, qkv + Mi * 3 * kDim, B.norms, B.norms + kHeadDim, B.norms + 2 * kHeadDim,
+                   B.norms + 3 * kHeadDim, pe, c->buf[B_QH], c->buf[B_KH], c->buf[B_VH], nb, n_img, n_txt};
+    QI_LAUNCH(QI_PROF_QKV_POST, 1, qkv_post_launch(qa, s));
+    QI_LAUNCH(QI_PROF_SAGE_QUANT, 3, sage_quantize_launch(c->buf[B_QH], c->buf[B_KH], BH, S, c->p<float>(B_KMEAN), c->p<int8_t>(B_QC),
+                                c->p<float>(B_QS), c->p<int8_t>(B_KC), c->p<float>(B_KS), s));
+    AttnArgs aa{c->p<int8_t>(B_QC), c->p<float>(B_QS), c->p<int8_t>(B_KC), c->p<float>(B_KS), c->buf[B_VH],
+                c->buf[B_O], BH, S, kHeads, 1.0f / sqrtf(128.0f), 1, nb, n_img, n_txt};
+    QI_LAUNCH(QI_PROF_ATTENTION, 1, attention_launch(aa, s, c->err));
+    RowSeg os{c->buf[B_O], kDim, nullptr, nullptr, static_cast<int>(Ma)};
+    QI_LAUNCH(QI_PROF_QUANT_O, 1, rowquant_launch(kSrcF16, kDim, 1024, &os, 1, act, act_s, 0.0f, s));
+    GemmDesc go[2] = {{act, act_s, B.out[0].w, B.out[0].s, B.out[0].b, x_img, mi + 2 * kDim, static_cast<int>(Mi), kDim,
+                       kDim, kDim},
+                      {act + Mi * kDim, act_s + Mi, B.out[1].w, B.out[1].s, B.out[1].b, x_txt, mt + 2 * kDim,
+                       static_cast<int>(Mt), kDim, kDim, kDim}};
+    QI_LAUNCH(QI_PROF_GEMM_OUT, 1, gemm_i8_launch(go, 2, kEpiResidual, s, c->err, c->num_sms));
+    RowSeg ln2[2] = {{x_img, kDim, mi + 3 * kDim, mi + 4 * kDim, static_cast<int>(Mi)},
+                     {x_txt, kDim, mt + 3 * kDim, mt + 4 * kDim, static_cast<int>(Mt)}};
+    QI_LAUNCH(QI_PROF_QUANT_LN, 1, rowquant_launch(kSrcLnMod, kDim, 1024, ln2, 2, act, act_s, 1e-6f, s));
+    GemmDesc g1[2] = {{act, act_s, B.fc1[0].w, B.fc1[0].s, B.fc1[0].b, hbuf, nullptr, static_cast<int>(Mi), kMlp, kDim,
+                       kMlp},
+                      {act + Mi * kDim, act_s + Mi, B.fc1[1].w, B.fc1[1].s, B.fc1[1].b, hbuf + Mi * kMlp, nullptr,
+                       static_cast<int>(Mt), kMlp, kDim, kMlp}};
+    QI_LAUNCH(QI_PROF_GEMM_FC1, 1, gemm_i8_launch(g1, 2, kEpiGelu, s, c->err, c->num_sms));
+    RowSeg hs2{hbuf, kMlp, nullptr, nullptr, static_cast<int>(Ma)};
+    QI_LAUNCH(QI_PROF_QUANT_H, 1, rowquant_launch(kSrcF32, kMlp, 4096, &hs2, 1, act, act_s, 0.0f, s));
+    GemmDesc g2[2] = {{act, act_s, B.fc2[0].w, B.fc2[0].s, B.fc2[0].b, x_img, mi + 5 * kDim, static_cast<int>(Mi), kDim,
+                       kMlp, kDim},
+                      {act + Mi * kMlp, act_s + Mi, B.fc2[1].w, B.fc2[1].s, B.fc2[1].b, x_txt, mt + 5 * kDim,
+                       static_cast<int>(Mt), kDim, kMlp, kDim}};
+    QI_LAUNCH(QI_PROF_GEMM_FC2, 1, gemm_i8_launch(g2, 2, kEpiResidual, s, c->err, c->num_sms));
+  }
+  // 6. AdaLayerNormContinuous (scale = first half, shift = second half,
+  //    transformer.cu:881-884) -> BF16 -> proj_out -> unpatchify
+  const float* ada = c->p<float>(B_ADA);
+  QI_LAUNCH(QI_PROF_POST, 1, layernorm_mod_launch(x_img, ada + kDim, ada, static_cast<int>(Mi), kDim, 1e-6f, nullptr, c->buf[B_FIN], s));
+  GemmBf16Desc pd{c->buf[B_FIN], m->proj_out_w, m->proj_out_b, c->p<float>(B_PROJ), static_cast<int>(Mi), kPatchDim,
+                  kDim, kPatchDim};
+  QI_LAUNCH(QI_PROF_POST, 1, gemm_bf16_launch(pd, s, c->err, c->num_sms));
+  QI_LAUNCH(QI_PROF_POST, 1, unpatchify_launch(c->p<float>(B_PROJ), out, nb, H, W, s));
+  c->launches = n;
+  return QI_OK;
+#undef QI_LAUNCH
+}

@@ -1,0 +1,395 @@
+// gemm_i8.cu -- W8A8 (and BF16) linear layers on the 5th-generation tensor cores.
+//
+// Replaces the reference's three-launch INT8 linear (cuda_kernels.cu:2674-2773:
+// FWHT+quant, cublasGemmEx S8xS8->S32 into HBM, dequant(+GELU) kernel) with one
+// persistent tcgen05 kernel per layer group whose epilogue applies the
+// reference's dequantisation  out = acc * s_act[m] * s_w[n] + bias[n]
+// (cuda_kernels.cu:2623-2668) straight from TMEM, optionally GELU-tanh, or the
+// gated residual update x += gate[n] * out (gate_add_fp32f, cuda_kernels.cu:
+// 2181-2189), so the INT32 accumulators never touch HBM.
+//
+// Layout: A = activation codes [M, K] int8 row-major, B = weight codes [N, K]
+// int8 row-major (quantize.cu's "<name>" I8 tensor), both K-major.  Tiles are
+// 128 x 256 x 128 bytes; a 4-stage TMA ring (48 KB per stage, 128-byte
+// swizzle) feeds tcgen05.mma.kind::i8 (M=128, N=256, K=32); the 128x256 S32
+// accumulator lives in TMEM, double buffered (512 columns) so the epilogue of
+// one tile overlaps the main loop of the next.
+//
+// Warp roles (192 threads): warp 0 TMA producer, warp 1 MMA issuer (and TMEM
+// owner), warps 2-5 epilogue (one TMEM lane = one output row per thread).
+#include "qi_internal.h"
+#include "sm100.cuh"
+
+namespace qi {
+
+namespace gemm {
+constexpr int BM = 128, BN = 256, BK = 128, STAGES = 4;
+constexpr int A_BYTES = BM * BK;                 // 16 KB
+constexpr int B_BYTES = BN * BK;                 // 32 KB
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;   // 48 KB
+constexpr int TMEM_COLS = 512;                   // 2 accumulators x 256 columns
+constexpr int THREADS = 192;
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+}  // namespace gemm
+
+struct alignas(64) GemmProblemDev {
+  CUtensorMap tmA;
+  CUtensorMap tmB;
+  const float* sa;
+  const float* sw;
+  const __nv_bfloat16* bias;
+  float* out;
+  const float* gate;
+  int M, N, K, ldo;
+  int tiles_n, tile_begin, tile_end, pad;
+};
+
+struct alignas(64) GemmArgsDev {
+  GemmProblemDev p[2];
+  int nprob;
+  int total_tiles;
+  int epi;
+  int* err;
+};
+
+__device__ __forceinline__ float gelu_tanh_dev(float v) {
+  // Same expression as dequantize_bias_gelu_kernel (cuda_kernels.cu:2656-2658).
+  const float c = 0.7978845608f;
+  float inner = c * (v + 0.044715f * v * v * v);
+  return 0.5f * v * (1.0f + tanhf(inner));
+}
+
+// BF16 = false: kind::i8 with the INT8 dequant epilogue.  BF16 = true:
+// kind::f16 on BF16 operands (64 elements per 128-byte K block), epilogue
+// out = acc + bias (the boundary layers' cuBLAS BF16 GEMM + bias_add_fp32,
+// cuda_kernels.cu:4535-4596).
+template <bool BF16>
+__global__ void __launch_bounds__(gemm::THREADS, 1) gemm_kernel(const __grid_constant__ GemmArgsDev args) {
+  using namespace gemm;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 4);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+    for (int i = 0; i < args.nprob; ++i) {
+      tma_prefetch_desc(&args.p[i].tmA);
+      tma_prefetch_desc(&args.p[i].tmB);
+    }
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  auto locate = [&](int t, int& pi, int& m0, int& n0) {
+    pi = (args.nprob > 1 && t >= args.p[0].tile_end) ? 1 : 0;
+    const GemmProblemDev& P = args.p[pi];
+    int lt = t - P.tile_begin;
+    m0 = (lt / P.tiles_n) * BM;
+    n0 = (lt % P.tiles_n) * BN;
+  };
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued_mask = 0, issued_parity = 0;  // last phase issued per stage
+      bool ok = true;
+      for (int t = blockIdx.x; t < args.total_tiles && ok; t += gridDim.x) {
+        int pi, m0, n0;
+        locate(t, pi, m0, n0);
+        const GemmProblemDev& P = args.p[pi];
+        const int kblocks = (P.K * (BF16 ? 2 : 1) + BK - 1) / BK;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag)) {
+            ok = false;
+            break;
+          }
+          mbar_expect_tx(&full[stage], STAGE_BYTES);
+          const int kc = kb * (BF16 ? BK / 2 : BK);  // element coordinate
+          tma_load_2d(sA + stage * A_BYTES, &P.tmA, kc, m0, &full[stage]);
+          tma_load_2d(sB + stage * B_BYTES, &P.tmB, kc, n0, &full[stage]);
+          issued_mask |= 1u << stage;
+          issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok) {
+        *abort_flag = 1;
+        atomicCAS(args.err, 0, kErrTimeoutProducer);
+        // Let copies already in flight land before the CTA exits.
+        for (int s = 0; s < STAGES; ++s) {
+          if (!(issued_mask & (1u << s))) continue;
+          const uint32_t par = (issued_parity >> s) & 1u;
+          uint64_t t0 = global_timer_ns();
+          while (!mbar_try_wait(&full[s], par) && global_timer_ns() - t0 < kWaitLimitNs / 4) {
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      bool ok = true;
+      const uint32_t idesc = BF16 ? idesc_bf16(BM, BN) : idesc_i8(BM, BN);
+      for (int t = blockIdx.x; t < args.total_tiles && ok; t += gridDim.x, ++local) {
+        int pi, m0, n0;
+        locate(t, pi, m0, n0);
+        const GemmProblemDev& P = args.p[pi];
+        const int kblocks = (P.K * (BF16 ? 2 : 1) + BK - 1) / BK;
+        const int buf = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
+        if (!mbar_wait(&tempty[buf], acc_phase ^ 1u, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + buf * BN;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(&full[stage], phase, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(sA + stage * A_BYTES);
+          const uint32_t b_addr = smem_u32(sB + stage * B_BYTES);
+#pragma unroll
+          for (int k = 0; k < BK / 32; ++k) {
+            uint64_t ad = umma_desc_sw128(a_addr + k * 32, 16, 1024);
+            uint64_t bd = umma_desc_sw128(b_addr + k * 32, 16, 1024);
+            if (BF16)
+              mma_f16_ss(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+            else
+              mma_i8_ss(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+          }
+          mma_commit(&empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        mma_commit(&tfull[buf]);
+      }
+      if (!ok) {
+        *abort_flag = 1;
+        atomicCAS(args.err, 0, kErrTimeoutMma);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int quarter = warp & 3;  // TMEM lane quarter this warp may access
+    const int row_in_tile = quarter * 32 + lane;
+    int local = 0;
+    for (int t = blockIdx.x; t < args.total_tiles; t += gridDim.x, ++local) {
+      int pi, m0, n0;
+      locate(t, pi, m0, n0);
+      const GemmProblemDev& P = args.p[pi];
+      const int buf = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      bool ok = mbar_wait(&tfull[buf], acc_phase, abort_flag);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) {
+        if (lane == 0) {
+          *abort_flag = 1;
+          atomicCAS(args.err, 0, kErrTimeoutEpilogue);
+        }
+        break;
+      }
+      tc_fence_after();
+      const int grow = m0 + row_in_tile;
+      const bool row_ok = grow < P.M;
+      const float sa = (row_ok && !BF16) ? __ldg(P.sa + grow) : 0.0f;
+      float* orow = P.out + static_cast<size_t>(row_ok ? grow : 0) * P.ldo;
+      const uint32_t taddr_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + buf * BN;
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        uint32_t acc[32];
+        tmem_ld32(taddr_row + c, acc);
+        tmem_ld_wait();
+        const int gcol = n0 + c;
+        if (!row_ok || gcol >= P.N) continue;
+        const float4* sw4 = BF16 ? nullptr : reinterpret_cast<const float4*>(P.sw + gcol);
+#pragma unroll
+        for (int j = 0; j < 32; j += 4) {
+          float v[4];
+          if (BF16) {
+            v[0] = __uint_as_float(acc[j + 0]);
+            v[1] = __uint_as_float(acc[j + 1]);
+            v[2] = __uint_as_float(acc[j + 2]);
+            v[3] = __uint_as_float(acc[j + 3]);
+          } else {
+            float4 w = __ldg(sw4 + j / 4);
+            v[0] = static_cast<float>(static_cast<int32_t>(acc[j + 0])) * sa * w.x;
+            v[1] = static_cast<float>(static_cast<int32_t>(acc[j + 1])) * sa * w.y;
+            v[2] = static_cast<float>(static_cast<int32_t>(acc[j + 2])) * sa * w.z;
+            v[3] = static_cast<float>(static_cast<int32_t>(acc[j + 3])) * sa * w.w;
+          }
+          if (P.bias) {
+            const __nv_bfloat162* b2 = reinterpret_cast<const __nv_bfloat162*>(P.bias + gcol + j);
+            float2 b01 = __bfloat1622float2(b2[0]);
+            float2 b23 = __bfloat1622float2(b2[1]);
+            v[0] += b01.x;
+            v[1] += b01.y;
+            v[2] += b23.x;
+            v[3] += b23.y;
+          }
+          float4* dst = reinterpret_cast<float4*>(orow + gcol + j);
+          if (args.epi == kEpiGelu) {
+            *dst = make_float4(gelu_tanh_dev(v[0]), gelu_tanh_dev(v[1]), gelu_tanh_dev(v[2]), gelu_tanh_dev(v[3]));
+          } else if (args.epi == kEpiResidual) {
+            float4 g = __ldg(reinterpret_cast<const float4*>(P.gate + gcol + j));
+            float4 x = *dst;
+            x.x = x.x + g.x * v[0];
+            x.y = x.y + g.y * v[1];
+            x.z = x.z + g.z * v[2];
+            x.w = x.w + g.w * v[3];
+            *dst = x;
+          } else {
+            *dst = make_float4(v[0], v[1], v[2], v[3]);
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[buf]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+// ------------------------------------------------------------------ host
+static int encode_kmajor(CUtensorMap* tm, const void* base, int rows, int K, int box_rows, bool bf16) {
+  const int esize = bf16 ? 2 : 1;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(K) * esize};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(gemm::BK / esize), static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = qi_encode_tiled(tm, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8, 2,
+                                      const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                      CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? QI_OK : QI_ERR_CUDA;
+}
+
+template <bool BF16>
+static int launch_args(GemmArgsDev& args, cudaStream_t stream, int num_sms) {
+  static bool attr_set = false;
+  if (!attr_set) {
+    if (cudaFuncSetAttribute(gemm_kernel<BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, gemm::SMEM_BYTES) !=
+        cudaSuccess)
+      return QI_ERR_CUDA;
+    attr_set = true;
+  }
+  int grid = args.total_tiles < num_sms ? args.total_tiles : num_sms;
+  gemm_kernel<BF16><<<grid, gemm::THREADS, gemm::SMEM_BYTES, stream>>>(args);
+  return cudaGetLastError() == cudaSuccess ? QI_OK : QI_ERR_CUDA;
+}
+
+static void fill_problem(GemmProblemDev& P, int M, int N, int K, int ldo, int& tiles) {
+  P.M = M;
+  P.N = N;
+  P.K = K;
+  P.ldo = ldo;
+  P.tiles_n = (N + gemm::BN - 1) / gemm::BN;
+  const int tm = (M + gemm::BM - 1) / gemm::BM;
+  P.tile_begin = tiles;
+  tiles += tm * P.tiles_n;
+  P.tile_end = tiles;
+}
+
+int gemm_i8_launch(const GemmDesc* descs, int n, int epi, cudaStream_t stream, int* err_dev, int num_sms) {
+  if (n < 1 || n > 2) return QI_ERR_ARG;
+  GemmArgsDev args;
+  memset(&args, 0, sizeof(args));
+  int tiles = 0;
+  for (int i = 0; i < n; ++i) {
+    const GemmDesc& d = descs[i];
+    if (d.M < 0 || d.N <= 0 || d.K <= 0) return QI_ERR_ARG;
+    if (d.K % 16 != 0 || d.N % 32 != 0 || d.ldo % 4 != 0) return QI_ERR_ARG;
+    if ((reinterpret_cast<uintptr_t>(d.a) & 15) || (reinterpret_cast<uintptr_t>(d.w) & 15) ||
+        (reinterpret_cast<uintptr_t>(d.out) & 15) || (reinterpret_cast<uintptr_t>(d.sw) & 15))
+      return QI_ERR_ALIGN;
+    if (epi == kEpiResidual && (d.gate == nullptr || (reinterpret_cast<uintptr_t>(d.gate) & 15)))
+      return QI_ERR_ARG;
+    GemmProblemDev& P = args.p[i];
+    if (d.M > 0) {
+      if (encode_kmajor(&P.tmA, d.a, d.M, d.K, gemm::BM, false) != QI_OK) return QI_ERR_CUDA;
+      if (encode_kmajor(&P.tmB, d.w, d.N, d.K, gemm::BN, false) != QI_OK) return QI_ERR_CUDA;
+    }
+    P.sa = d.sa;
+    P.sw = d.sw;
+    P.bias = reinterpret_cast<const __nv_bfloat16*>(d.bias);
+    P.out = d.out;
+    P.gate = d.gate;
+    fill_problem(P, d.M, d.N, d.K, d.ldo, tiles);
+  }
+  if (tiles == 0) return QI_OK;
+  args.nprob = n;
+  args.total_tiles = tiles;
+  args.epi = epi;
+  args.err = err_dev;
+  return launch_args<false>(args, stream, num_sms);
+}
+
+int gemm_bf16_launch(const GemmBf16Desc& d, cudaStream_t stream, int* err_dev, int num_sms) {
+  if (d.M < 0 || d.N <= 0 || d.K <= 0) return QI_ERR_ARG;
+  if (d.K % 8 != 0 || d.N % 32 != 0 || d.ldo % 4 != 0) return QI_ERR_ARG;
+  if ((reinterpret_cast<uintptr_t>(d.a) & 15) || (reinterpret_cast<uintptr_t>(d.w) & 15) ||
+      (reinterpret_cast<uintptr_t>(d.out) & 15))
+    return QI_ERR_ALIGN;
+  if (d.M == 0) return QI_OK;
+  GemmArgsDev args;
+  memset(&args, 0, sizeof(args));
+  GemmProblemDev& P = args.p[0];
+  if (encode_kmajor(&P.tmA, d.a, d.M, d.K, gemm::BM, true) != QI_OK) return QI_ERR_CUDA;
+  if (encode_kmajor(&P.tmB, d.w, d.N, d.K, gemm::BN, true) != QI_OK) return QI_ERR_CUDA;
+  P.bias = reinterpret_cast<const __nv_bfloat16*>(d.bias);
+  P.out = d.out;
+  int tiles = 0;
+  fill_problem(P, d.M, d.N, d.K, d.ldo, tiles);
+  args.nprob = 1;
+  args.total_tiles = tiles;
+  args.epi = kEpiStore;
+  args.err = err_dev;
+  return launch_args<true>(args, stream, num_sms);
+}
+
+}  // namespace qi

@@ -1,0 +1,137 @@
+// qi_internal.h -- launchers shared between the kernel files and the host
+// orchestration.  Not part of the public ABI (include/qwen_image_b200.h).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <string.h>
+
+#include "../../include/qwen_image_b200.h"
+
+namespace qi {
+
+constexpr int kDim = 3072;      // inner_dim (transformer.cu:244)
+constexpr int kHeads = 24;      // n_heads
+constexpr int kHeadDim = 128;   // head_dim
+constexpr int kMlp = 12288;     // mlp_dim
+constexpr int kTxtDim = 3584;   // text-encoder hidden size
+constexpr int kPatchDim = 64;   // 16 channels x 2 x 2 patch
+constexpr int kOutCh = 16;
+
+enum Epilogue { kEpiStore = 0, kEpiGelu = 1, kEpiResidual = 2 };
+
+// ---------------------------------------------------------------- GEMMs
+// INT8: out = acc * sa[m] * sw[n] + bias[n] (+ epilogue).  a [M,K], w [N,K].
+struct GemmDesc {
+  const int8_t* a;
+  const float* sa;
+  const int8_t* w;
+  const float* sw;
+  const void* bias;  // BF16 [N] or null
+  float* out;
+  const float* gate;  // FP32 [N] for kEpiResidual
+  int M, N, K, ldo;
+};
+int gemm_i8_launch(const GemmDesc* descs, int n, int epi, cudaStream_t stream, int* err_dev, int num_sms);
+
+// BF16 x BF16 -> FP32 on the tensor cores: out = a[M,K] * w[N,K]^T + bias.
+struct GemmBf16Desc {
+  const void* a;  // BF16 [M,K]
+  const void* w;  // BF16 [N,K]
+  const void* bias;
+  float* out;
+  int M, N, K, ldo;
+};
+int gemm_bf16_launch(const GemmBf16Desc& d, cudaStream_t stream, int* err_dev, int num_sms);
+
+// ---------------------------------------------------------------- quantizers
+// Row sources for the fused activation quantizer.  Rows of all segments are
+// written consecutively to codes/scales.
+enum RowSrc { kSrcF32 = 0, kSrcF16 = 1, kSrcLnMod = 2 };
+struct RowSeg {
+  const void* in;      // FP32 or FP16 rows
+  long long ld;        // elements between rows
+  const float* shift;  // kSrcLnMod: modulation shift [K]
+  const float* scale;  // kSrcLnMod: modulation scale [K] (used as 1 + scale)
+  int rows;
+};
+int rowquant_launch(int src, int K, int had_block, const RowSeg* segs, int nseg, int8_t* codes, float* scales,
+                    float eps, cudaStream_t stream);
+// Generic shared-memory FWHT + per-row INT8 for any K <= 12288 and any
+// power-of-two block; BF16 or FP32 input.  Used for weights (load time) and
+// for activation shapes the fused kernels do not cover.
+int fwht_quant_generic(const void* in, int in_bf16, int M, int K, int had_block, int8_t* codes, float* scales,
+                       cudaStream_t stream);
+
+// LayerNorm + modulate to BF16 or FP32 (final AdaLN, transformer.cu:881-884).
+int layernorm_mod_launch(const float* x, const float* shift, const float* scale, int rows, int dim, float eps,
+                         float* out_f32, void* out_bf16, cudaStream_t stream);
+int rmsnorm_f32_launch(const float* x, const void* w, float* out, int rows, int dim, float eps,
+                       cudaStream_t stream);
+int rmsnorm_bf16_launch(const void* x, const void* w, void* out, int rows, int dim, float eps, cudaStream_t stream);
+
+// ---------------------------------------------------------------- GEMV (M = 1)
+// out[j][n] = dot(act, w_j[n]) * act_scale * sw_j[n] + bias_j[n] for a batch of
+// linears that share one quantized activation row.
+struct GemvJob {
+  const int8_t* w;
+  const float* sw;
+  const void* bias;
+  float* out;
+  int N;
+};
+int gemv_i8_launch(const int8_t* act, const float* act_scale, int K, const GemvJob* jobs, int njobs,
+                   cudaStream_t stream);
+int gemv_bf16_launch(const float* x, const void* w, const void* bias, float* out, int N, int K, cudaStream_t stream);
+
+// ---------------------------------------------------------------- elementwise
+int timestep_embedding_launch(float t, float* out256, cudaStream_t stream);
+int silu_launch(const float* x, float* out, int n, cudaStream_t stream);
+int patchify_launch(const void* x_bf16, void* patches_bf16, int nb, int H, int W, cudaStream_t stream);
+int unpatchify_launch(const float* proj, void* out_bf16, int nb, int H, int W, cudaStream_t stream);
+
+// q/k RMSNorm + RoPE + FP16 + head-major joint layout.  qkv rows hold
+// [q | k | v] (3 x 3072).  Rows [0, nb*n_img) are image tokens, rows
+// [nb*n_img, nb*(n_img+n_txt)) text tokens.  Outputs [nb, 24, S, 128] FP16.
+struct QkvPostArgs {
+  const float* qkv_img;
+  const float* qkv_txt;
+  const void* nq_img;  // BF16 [128] norm_q
+  const void* nk_img;
+  const void* nq_txt;  // norm_added_q
+  const void* nk_txt;
+  const float* pe;     // nb x [S, 64, 2, 2]
+  void* q;
+  void* k;
+  void* v;
+  int nb, n_img, n_txt;
+};
+int qkv_post_launch(const QkvPostArgs& a, cudaStream_t stream);
+
+// ---------------------------------------------------------------- attention
+int sage_quantize_launch(const void* q, const void* k, int BH, int S, float* kmean, int8_t* qc, float* qs,
+                         int8_t* kc, float* ks, cudaStream_t stream);
+// out_mode 0: FP32 [BH, S, 128] head-major.
+// out_mode 1: FP16 token-major rows for the out-projection: joint position p
+//   of batch b goes to row (p < n_txt ? nb*n_img + b*n_txt + p
+//                                     : b*n_img + p - n_txt), 3072 columns.
+struct AttnArgs {
+  const int8_t* qc;
+  const float* qs;
+  const int8_t* kc;
+  const float* ks;
+  const void* v;  // FP16 [BH, S, 128]
+  void* out;
+  int BH, S, heads;
+  float sm_scale;
+  int out_mode;
+  int nb, n_img, n_txt;
+};
+int attention_launch(const AttnArgs& a, cudaStream_t stream, int* err_dev);
+
+int cfg_euler_launch(float* x, const void* cond, const void* uncond, float cfg, float sigma, float sigma_next, int H,
+                     int W, void* x_bf16, cudaStream_t stream);
+
+int device_num_sms();
+
+}  // namespace qi

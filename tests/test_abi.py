@@ -1,0 +1,68 @@
+"""The C-ABI library: loads without a GPU, exports every function the public
+header declares, validates arguments before touching the device, and its
+host-side RoPE table matches the CPU oracle's restatement of rope.h."""
+import ctypes
+import os
+import re
+
+import numpy as np
+import pytest
+
+import qib200 as Q
+import qi_oracle as O
+
+
+def declared_functions():
+    src = open(Q.HEADER).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"\b(qi_[a-z0-9_]+)\s*\(", src)))
+
+
+def test_library_loads_and_exports_all_symbols():
+    L = Q.lib()
+    names = declared_functions()
+    assert len(names) >= 20
+    missing = [n for n in names if not hasattr(L, n)]
+    assert not missing, f"declared but not exported: {missing}"
+
+
+def test_status_strings():
+    L = Q.lib()
+    assert L.qi_status_string(0) == b"ok"
+    for st in range(1, 9):
+        assert L.qi_status_string(st) not in (b"ok", b"unknown status")
+    assert L.qi_status_string(99) == b"unknown status"
+
+
+def test_argument_validation_without_device():
+    L = Q.lib()
+    null = ctypes.c_void_p(0)
+    assert L.qi_quantize_weight(null, 4, 64, null, null, null) == 1
+    assert L.qi_fwht_quantize(null, 4, 64, 64, null, null, null) == 1
+    assert L.qi_linear_i8(null, null, 4, 64, null, null, 32, null, 0, null, null, 32, null) == 1
+    assert L.qi_linear_i8(null, null, 4, 64, null, null, 32, null, 7, null, null, 32, null) == 1
+    assert L.qi_sage_attention(null, null, null, null, 0.1, 1, 8, 64, null) == 5  # head_dim 64 unsupported
+    assert L.qi_forward(null, null, 1, null, 0.0, null, 8, null, 8, 8, null, null) == 1
+    assert L.qi_model_create(null, 1, null, null, None) == 1
+    assert L.qi_rope_table(8, 8, 8, null) == 1
+
+
+@pytest.mark.parametrize("h,w,n_txt", [(8, 8, 8), (128, 128, 256), (166, 166, 256), (7, 9, 5)])
+def test_rope_table_matches_oracle(h, w, n_txt):
+    a = Q.rope_table(h, w, n_txt)
+    b = O.rope_table(h, w, n_txt)
+    assert a.shape == b.shape == (n_txt + ((h + 1) // 2) * ((w + 1) // 2), 64, 2, 2)
+    np.testing.assert_array_equal(a, b)
+
+
+def test_rope_table_matches_reference_digest(golden_dir):
+    import hashlib
+    path = os.path.join(golden_dir, "rope.npz")
+    if not os.path.exists(path):
+        pytest.skip("golden fixtures not generated")
+    g = np.load(path)
+    for key in g.files:
+        if not key.startswith("sha256_"):
+            continue
+        h, w, n = (int(v) for v in key.split("_")[1:])
+        assert hashlib.sha256(Q.rope_table(h, w, n).tobytes()).digest() == bytes(g[key]), key

@@ -1,0 +1,164 @@
+"""Model-level parity: the product's forward (qi_forward through the C ABI)
+against the reference's own transformer_forward (Sage path) on identical
+weights and inputs, against the CPU oracle, and CFG batching against two
+single forwards.  Tolerance: cosine >= 0.999 and
+normwise max relative error max|a-b| / max|b| <= 2e-2."""
+import json
+import os
+import struct
+import tempfile
+
+import numpy as np
+import pytest
+import torch
+
+import qib200 as Q
+import qi_oracle as O
+import qi_ref as R
+
+pytestmark = pytest.mark.gpu
+
+COS_MIN, MAXREL_MAX = 0.999, 2e-2
+
+
+def metrics(a, b):
+    a = a.double().flatten()
+    b = b.double().flatten()
+    return float(a @ b / (a.norm() * b.norm())), float((a - b).abs().max() / b.abs().max())
+
+
+@pytest.fixture(scope="module")
+def env():
+    torch.cuda.set_device(0)
+    if not R.available():
+        pytest.skip("reference build oracle/_ref/libqiref.so missing")
+    g, blocks = R.make_table(60, distinct=2)
+    ctx = Q.Context(0)
+    model = Q.Model(ctx, g, blocks)
+    ptrs = R.table_pointers(g, blocks)
+    yield dict(g=g, blocks=blocks, ctx=ctx, model=model, ptrs=ptrs)
+    model.close()
+    ctx.close()
+    torch.cuda.synchronize()
+
+
+def inputs(H, W, n_txt, nb=1, seed=1):
+    x = R.synth((1, 16, H, W), R.seed_for(seed, "latent"), 1.0, dtype=torch.bfloat16)
+    txts = [R.synth((1, n_txt, 3584), R.seed_for(seed + b, "context"), 1.0, dtype=torch.bfloat16) for b in range(nb)]
+    pe = torch.from_numpy(Q.rope_table(H, W, n_txt)).cuda()
+    return x, txts, pe
+
+
+@pytest.mark.parametrize("H,W,n_txt,t", [(8, 8, 8, 500.0), (64, 64, 64, 500.0), (32, 48, 30, 871.3),
+                                         (128, 128, 256, 250.0)])
+def test_forward_matches_reference(env, H, W, n_txt, t):
+    x, (txt,), pe = inputs(H, W, n_txt)
+    garr, _, bt = env["ptrs"]
+    ref = R.transformer_forward(garr, bt, x, t, txt, pe, H, W, sage=True)
+    ours = Q.forward(env["ctx"], env["model"], x, t, txt, pe[None])
+    env["ctx"].check()
+    cos, maxrel = metrics(ours.float(), ref.float())
+    print(f"forward {H}x{W} n_txt={n_txt}: cos={cos:.6f} maxrel={maxrel:.4g}")
+    assert cos >= COS_MIN and maxrel <= MAXREL_MAX, (cos, maxrel)
+
+
+def test_cfg_batch_equals_two_single_forwards(env):
+    H, W, n_txt, t = 32, 32, 24, 600.0
+    x, (c0, c1), pe = inputs(H, W, n_txt, nb=2)
+    ctx, model = env["ctx"], env["model"]
+    y0 = Q.forward(ctx, model, x, t, c0, pe[None])
+    y1 = Q.forward(ctx, model, x, t, c1, pe[None])
+    yb = Q.forward(ctx, model, torch.cat([x, x]), t, torch.cat([c0, c1]), torch.stack([pe, pe]))
+    ctx.check()
+    assert torch.equal(yb[0:1], y0)
+    assert torch.equal(yb[1:2], y1)
+    assert not torch.equal(y0, y1)
+
+
+def test_forward_is_deterministic(env):
+    x, (txt,), pe = inputs(16, 16, 16)
+    a = Q.forward(env["ctx"], env["model"], x, 400.0, txt, pe[None])
+    b = Q.forward(env["ctx"], env["model"], x, 400.0, txt, pe[None])
+    assert torch.equal(a, b)
+
+
+def test_one_block_matches_cpu_oracle():
+    """One double-stream block (plus the boundary layers) at a tiny size
+    against the CPU oracle: its quantization-emulating mode at the north-star
+    tolerance, and its unquantized FP32 mode (the W8A8 + INT8-attention error
+    itself) at the looser bar the reference's own arithmetic meets."""
+    torch.cuda.set_device(0)
+    g, blocks = Q.make_weight_table(1, base_seed=0)
+    ctx = Q.Context(0)
+    model = Q.Model(ctx, g, blocks)
+    H = W = 8
+    n_txt = 8
+    xs = O.gen_bf16(O.seed_for(1, "latent"), (1, 16, H, W), 1.0)
+    ts = O.gen_bf16(O.seed_for(1, "context"), (n_txt, 3584), 1.0)
+    pe = O.rope_table(H, W, n_txt)
+    x = torch.from_numpy(xs.view(np.int16)).cuda().view(torch.bfloat16)
+    txt = torch.from_numpy(ts.view(np.int16)).cuda().view(torch.bfloat16)[None]
+    ours = Q.forward(ctx, model, x, 500.0, txt, torch.from_numpy(pe).cuda()[None]).float().cpu()
+    ctx.check()
+    W1 = O.Weights(1, base_seed=0)
+    oq = torch.from_numpy(O.forward(W1, xs, 500.0, ts, pe, mode="quant"))
+    of = torch.from_numpy(O.forward(W1, xs, 500.0, ts, pe, mode="fp32"))
+    cq, mq = metrics(ours, oq)
+    cf, mf = metrics(ours, of)
+    print(f"one block vs oracle quant: cos={cq:.6f} maxrel={mq:.4g}; vs fp32: cos={cf:.6f} maxrel={mf:.4g}")
+    assert cq >= COS_MIN and mq <= MAXREL_MAX, (cq, mq)
+    assert cf >= 0.998 and mf <= 0.1, (cf, mf)
+    model.close()
+    ctx.close()
+
+
+def _write_safetensors(path, tensors):
+    header, blobs, off = {}, [], 0
+    for name, (dtype, arr) in tensors.items():
+        b = arr.tobytes()
+        header[name] = {"dtype": dtype, "shape": list(arr.shape), "data_offsets": [off, off + len(b)]}
+        blobs.append(b)
+        off += len(b)
+    h = json.dumps(header).encode()
+    h += b" " * ((8 - len(h) % 8) % 8)
+    with open(path, "wb") as f:
+        f.write(struct.pack("<Q", len(h)))
+        f.write(h)
+        for b in blobs:
+            f.write(b)
+
+
+def test_safetensors_checkpoint_roundtrip():
+    """A quantize.cu-format checkpoint (I8 codes + __scales__, BF16 rest) loads
+    into the same model as the device table it was written from."""
+    torch.cuda.set_device(0)
+    g, blocks = Q.make_weight_table(1, base_seed=5)
+    cpu = lambda t: t.cpu().numpy() if t.dtype != torch.bfloat16 else t.view(torch.int16).cpu().numpy()
+    tensors = {}
+    dt = {torch.int8: "I8", torch.float32: "F32", torch.bfloat16: "BF16"}
+    for (name, kind), t in zip(Q.G_NAMES, g):
+        tensors[name] = (dt[t.dtype], cpu(t))
+    pre = "transformer_blocks.0."
+    for li, (lname, N, K) in enumerate(Q.L_NAMES):
+        c, s, b = blocks[0][3 * li:3 * li + 3]
+        tensors[pre + lname + ".weight"] = ("I8", cpu(c))
+        tensors[pre + lname + ".weight.__scales__"] = ("F32", cpu(s))
+        tensors[pre + lname + ".bias"] = ("BF16", cpu(b))
+    for k, nname in enumerate(Q.B_NORMS):
+        tensors[pre + nname] = ("BF16", cpu(blocks[0][3 * len(Q.L_NAMES) + k]))
+    ctx = Q.Context(0)
+    with tempfile.TemporaryDirectory() as d:
+        path = os.path.join(d, "model.safetensors")
+        _write_safetensors(path, tensors)
+        m_file = Q.Model.from_safetensors(ctx, path)
+        assert m_file.num_blocks() == 1
+    m_tab = Q.Model(ctx, g, blocks)
+    x = Q.synth((1, 16, 16, 16), Q.seed_for(9, "x"), 1.0, dtype=torch.bfloat16)
+    txt = Q.synth((1, 12, 3584), Q.seed_for(9, "c"), 1.0, dtype=torch.bfloat16)
+    pe = torch.from_numpy(Q.rope_table(16, 16, 12)).cuda()[None]
+    a = Q.forward(ctx, m_file, x, 300.0, txt, pe)
+    b = Q.forward(ctx, m_tab, x, 300.0, txt, pe)
+    assert torch.equal(a, b)
+    m_file.close()
+    m_tab.close()
+    ctx.close()
