@@ -191,8 +191,7 @@ def run_ours(args):
             v = gathered
         else:
             v = vel
-        Q.check(Q.lib().qi_cfg_euler_step(Q._p(latent), Q._p(v[0]), Q._p(v[1]), CFG_SCALE, s, s_next, H_LAT, W_LAT,
-                                          Q._p(lat_bf), Q._stream()))
+        Q.cfg_euler_step(latent, v[0], v[1], CFG_SCALE, s, s_next, lat_bf)
 
     for i in range(args.warmup):
         step(i)

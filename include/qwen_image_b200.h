@@ -157,6 +157,15 @@ int qi_model_num_blocks(const qi_model* model);
 int qi_forward(qi_ctx* ctx, const qi_model* model, int nb, const void* x_bf16, float timestep,
                const void* ctx_bf16, int n_txt, const float* pe, int H, int W, void* out_bf16, void* stream);
 
+/* The block loop alone (transformer.cu:497-836, with the modulation of
+ * `timestep`, :506-515) on caller-held FP32 residual streams, in place:
+ * img [nb*n_img, 3072] and txt [nb*n_txt, 3072] (batch-major rows), blocks
+ * [block_begin, block_end).  pe as for qi_forward.  Lets a caller run the
+ * forward in pieces (per-block parity checks against the reference's block
+ * dumps, multi-GPU schedules that own the residual streams).              */
+int qi_forward_blocks(qi_ctx* ctx, const qi_model* model, int nb, int n_img, int n_txt, float* img, float* txt,
+                      float timestep, const float* pe, int block_begin, int block_end, void* stream);
+
 /* RoPE table of rope.h gen_qwen_image_pe (h, w = latent size): host memory,
  * [n_txt + n_img, 64, 2, 2] FP32.                                            */
 int qi_rope_table(int h, int w, int n_txt, float* pe_host);

@@ -1,12 +1,16 @@
 #!/bin/sh
-# Builds the reference's own CUDA hot path (cuda_kernels.cu, transformer.cu,
-# sageattention_sm80.cu via ref_harness.cu) from the reference tree, with the
-# reference Makefile's flags (its Makefile:11) for sm_100a, into
-# oracle/_ref/libqiref.so.  Test infrastructure: the parity checker and the
-# reference arm of bench.py.  main.cu is not built (it needs libpng).
+# Builds the reference's own CUDA hot path from the reference tree (cuda_kernels.cu,
+# transformer.cu, and sageattention_sm80.cu included by ref_harness.cu) with the
+# reference Makefile's flags (its Makefile:11) for sm_100a:
+#   oracle/_ref/libqiref.so     reference ops + transformer_forward (parity checker,
+#                               reference arm of bench.py)
+#   oracle/_ref/libshimtest.so  the same caller code (ref_driver.cu) linked against the
+#                               product's drop-in shim instead of transformer.cu
+# Test infrastructure.  main.cu is not built (it needs libpng).
 set -e
 REF=${QI_REFERENCE_DIR:-/root/reference}
 HERE=$(cd "$(dirname "$0")" && pwd)
+PKG="$HERE/../qwen-image.cu_b200"
 OUT="$HERE/_ref"
 if [ ! -f "$REF/transformer.cu" ]; then
   echo "reference sources not found at $REF; skipping oracle/_ref" >&2
@@ -16,11 +20,18 @@ mkdir -p "$OUT"
 NVCC=${NVCC:-/usr/local/cuda/bin/nvcc}
 FLAGS="-O2 -std=c++17 --expt-relaxed-constexpr --extended-lambda -diag-suppress=177 --use_fast_math"
 ARCH="-gencode arch=compute_100a,code=sm_100a"
-for src in cuda_kernels transformer; do
-  "$NVCC" $FLAGS $ARCH -I"$REF" -Xcompiler -fPIC -ccbin g++ -c "$REF/$src.cu" -o "$OUT/$src.o" &
-done
-"$NVCC" $FLAGS $ARCH -I"$REF" -Xcompiler -fPIC -ccbin g++ -c "$HERE/ref_harness.cu" -o "$OUT/ref_harness.o" &
+CC="$NVCC $FLAGS $ARCH -I$REF -I$HERE/../include -Xcompiler -fPIC -ccbin g++"
+$CC -c "$REF/cuda_kernels.cu" -o "$OUT/cuda_kernels.o" &
+$CC -c "$REF/transformer.cu" -o "$OUT/transformer.o" &
+$CC -c "$HERE/ref_harness.cu" -o "$OUT/ref_harness.o" &
+$CC -c "$HERE/ref_driver.cu" -o "$OUT/ref_driver.o" &
+$CC -x cu -c "$PKG/shim/transformer_b200.cpp" -o "$OUT/transformer_b200.o" &
 wait
+for o in cuda_kernels transformer ref_harness ref_driver transformer_b200; do
+  [ -f "$OUT/$o.o" ] || { echo "compile of $o failed" >&2; exit 1; }
+done
 "$NVCC" $ARCH -shared -ccbin g++ -o "$OUT/libqiref.so" "$OUT/cuda_kernels.o" "$OUT/transformer.o" \
-  "$OUT/ref_harness.o" -lcublas -lcusolver
-echo "built $OUT/libqiref.so"
+  "$OUT/ref_harness.o" "$OUT/ref_driver.o" -lcublas -lcusolver
+"$NVCC" $ARCH -shared -ccbin g++ -o "$OUT/libshimtest.so" "$OUT/cuda_kernels.o" "$OUT/transformer_b200.o" \
+  "$OUT/ref_driver.o" -L"$PKG/lib" -lqib200 -Xlinker -rpath='$ORIGIN/../../qwen-image.cu_b200/lib' -lcublas -lcusolver
+echo "built $OUT/libqiref.so $OUT/libshimtest.so"

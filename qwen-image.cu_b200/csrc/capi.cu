@@ -482,19 +482,50 @@ extern "C" int qi_model_create(qi_ctx* ctx, int num_blocks, const void* const* g
 }
 
 // ------------------------------------------------------------------ forward
-extern "C" int qi_forward(qi_ctx* c, const qi_model* m, int nb, const void* x, float timestep, const void* ctx_txt,
-                          int n_txt, const float* pe, int H, int W, void* out, void* stream_) {
-  if (!c || !m || !x || !ctx_txt || !pe || !out) return QI_ERR_ARG;
-  if (nb < 1 || nb > 8 || n_txt < 1 || H < 2 || W < 2 || (H & 1) || (W & 1)) return QI_ERR_ARG;
-  cudaStream_t s = S_(stream_);
-  const int n_img = (H / 2) * (W / 2);
-  const int S = n_img + n_txt;
-  const long long Mi = static_cast<long long>(nb) * n_img, Mt = static_cast<long long>(nb) * n_txt, Ma = Mi + Mt;
-  const int BH = nb * kHeads;
-  const size_t hs = static_cast<size_t>(BH) * S * kHeadDim;
-  const int L = m->nblocks;
+// Shapes and workspace views of one forward; the stages below share it.
+namespace {
+struct Fwd {
+  qi_ctx* c;
+  const qi_model* m;
+  cudaStream_t s;
+  int nb, n_img, n_txt, S, BH;
+  long long Mi, Mt, Ma;
+  int n = 0;  // launches issued
+};
 
-  QI_TRY(c->ensure(B_PATCH, Mi * kPatchDim * 2));
+// One launch (or a fixed group) per QI_LAUNCH; with profiling on, an event
+// pair brackets it on the stream and is resolved in qi_ctx_profile.
+#define QI_LAUNCH(stage, count, expr)        \
+  do {                                       \
+    qi_ctx* c_ = f.c;                        \
+    cudaEvent_t e0 = nullptr, e1 = nullptr;  \
+    if (c_->profiling) {                     \
+      e0 = c_->ev();                         \
+      e1 = c_->ev();                         \
+      cudaEventRecord(e0, f.s);              \
+    }                                        \
+    QI_TRY(expr);                            \
+    if (c_->profiling) {                     \
+      cudaEventRecord(e1, f.s);              \
+      c_->pending.push_back({stage, {e0, e1}}); \
+    }                                        \
+    f.n += (count);                          \
+  } while (0)
+
+int fwd_init(Fwd& f, qi_ctx* c, const qi_model* m, int nb, int n_img, int n_txt, void* stream) {
+  f.c = c;
+  f.m = m;
+  f.s = S_(stream);
+  f.nb = nb;
+  f.n_img = n_img;
+  f.n_txt = n_txt;
+  f.S = n_img + n_txt;
+  f.BH = nb * kHeads;
+  f.Mi = static_cast<long long>(nb) * n_img;
+  f.Mt = static_cast<long long>(nb) * n_txt;
+  f.Ma = f.Mi + f.Mt;
+  const size_t hs = static_cast<size_t>(f.BH) * f.S * kHeadDim;
+  QI_TRY(c->ensure(B_PATCH, f.Mi * kPatchDim * 2));
   QI_TRY(c->ensure(B_TEMB256, 256 * 4));
   QI_TRY(c->ensure(B_TACT, kDim));
   QI_TRY(c->ensure(B_TACT_S, 16));
@@ -503,85 +534,84 @@ extern "C" int qi_forward(qi_ctx* c, const qi_model* m, int nb, const void* x, f
   QI_TRY(c->ensure(B_TSILU, kDim * 4));
   QI_TRY(c->ensure(B_MODS, static_cast<size_t>(m->mod.N) * 4));
   QI_TRY(c->ensure(B_ADA, 2 * kDim * 4));
-  QI_TRY(c->ensure(B_X, Ma * kDim * 4));
-  QI_TRY(c->ensure(B_TXTN, Mt * kTxtDim * 2));
-  QI_TRY(c->ensure(B_ACT, Ma * kMlp));
-  QI_TRY(c->ensure(B_ACT_S, Ma * 4));
-  QI_TRY(c->ensure(B_QKV, Ma * 3 * kDim * 4));
+  QI_TRY(c->ensure(B_X, f.Ma * kDim * 4));
+  QI_TRY(c->ensure(B_TXTN, f.Mt * kTxtDim * 2));
+  QI_TRY(c->ensure(B_ACT, f.Ma * kMlp));
+  QI_TRY(c->ensure(B_ACT_S, f.Ma * 4));
+  QI_TRY(c->ensure(B_QKV, f.Ma * 3 * kDim * 4));
   QI_TRY(c->ensure(B_QH, hs * 2));
   QI_TRY(c->ensure(B_KH, hs * 2));
   QI_TRY(c->ensure(B_VH, hs * 2));
   QI_TRY(c->ensure(B_QC, hs));
   QI_TRY(c->ensure(B_KC, hs));
-  QI_TRY(c->ensure(B_QS, static_cast<size_t>(BH) * ((S + 127) / 128) * 32 * 4));
-  QI_TRY(c->ensure(B_KS, static_cast<size_t>(BH) * ((S + 63) / 64) * 4 * 4));
-  QI_TRY(c->ensure(B_KMEAN, static_cast<size_t>(BH) * kHeadDim * 4));
-  QI_TRY(c->ensure(B_O, Ma * kDim * 2));
-  QI_TRY(c->ensure(B_H, Ma * kMlp * 4));
-  QI_TRY(c->ensure(B_FIN, Mi * kDim * 2));
-  QI_TRY(c->ensure(B_PROJ, Mi * kPatchDim * 4));
+  QI_TRY(c->ensure(B_QS, static_cast<size_t>(f.BH) * ((f.S + 127) / 128) * 32 * 4));
+  QI_TRY(c->ensure(B_KS, static_cast<size_t>(f.BH) * ((f.S + 63) / 64) * 4 * 4));
+  QI_TRY(c->ensure(B_KMEAN, static_cast<size_t>(f.BH) * kHeadDim * 4));
+  QI_TRY(c->ensure(B_O, f.Ma * kDim * 2));
+  QI_TRY(c->ensure(B_H, f.Ma * kMlp * 4));
+  QI_TRY(c->ensure(B_FIN, f.Mi * kDim * 2));
+  QI_TRY(c->ensure(B_PROJ, f.Mi * kPatchDim * 4));
+  return QI_OK;
+}
 
-  // One launch (or a fixed group) per QI_LAUNCH; with profiling on, an event
-  // pair brackets it on the stream and is resolved in qi_ctx_profile.
-#define QI_LAUNCH(stage, count, expr)                                 \
-  do {                                                                \
-    cudaEvent_t e0 = nullptr, e1 = nullptr;                           \
-    if (c->profiling) {                                               \
-      e0 = c->ev();                                                   \
-      e1 = c->ev();                                                   \
-      cudaEventRecord(e0, s);                                         \
-    }                                                                 \
-    QI_TRY(expr);                                                     \
-    if (c->profiling) {                                               \
-      cudaEventRecord(e1, s);                                         \
-      c->pending.push_back({stage, {e0, e1}});                        \
-    }                                                                 \
-    n += (count);                                                     \
-  } while (0)
+// Timestep MLP (transformer.cu:330-349), all modulation vectors of the
+// forward (transformer.cu:506-515: they depend only on t) and the output
+// AdaLN embedding (transformer.cu:874-877).
+int fwd_modulation(Fwd& f, float timestep) {
+  qi_ctx* c = f.c;
+  const qi_model* m = f.m;
+  cudaStream_t s = f.s;
+  int8_t* tact = c->p<int8_t>(B_TACT);
+  float* tact_s = c->p<float>(B_TACT_S);
+  QI_LAUNCH(QI_PROF_PRE, 1, timestep_embedding_launch(timestep, c->p<float>(B_TEMB256), s));
+  RowSeg seg{c->buf[B_TEMB256], 256, nullptr, nullptr, 1};
+  QI_LAUNCH(QI_PROF_PRE, 1, rowquant_launch(kSrcF32, 256, 256, &seg, 1, tact, tact_s, 0.0f, s));
+  GemvJob j1{m->t1.w, m->t1.s, m->t1.b, c->p<float>(B_T1), kDim};
+  QI_LAUNCH(QI_PROF_PRE, 1, gemv_i8_launch(tact, tact_s, 256, &j1, 1, s));
+  QI_LAUNCH(QI_PROF_PRE, 1, silu_launch(c->p<float>(B_T1), c->p<float>(B_T1), kDim, s));
+  RowSeg seg2{c->buf[B_T1], kDim, nullptr, nullptr, 1};
+  QI_LAUNCH(QI_PROF_PRE, 1, rowquant_launch(kSrcF32, kDim, 1024, &seg2, 1, tact, tact_s, 0.0f, s));
+  GemvJob j2{m->t2.w, m->t2.s, m->t2.b, c->p<float>(B_TEMB), kDim};
+  QI_LAUNCH(QI_PROF_PRE, 1, gemv_i8_launch(tact, tact_s, kDim, &j2, 1, s));
+  QI_LAUNCH(QI_PROF_PRE, 1, silu_launch(c->p<float>(B_TEMB), c->p<float>(B_TSILU), kDim, s));
+  RowSeg seg3{c->buf[B_TSILU], kDim, nullptr, nullptr, 1};
+  QI_LAUNCH(QI_PROF_PRE, 1, rowquant_launch(kSrcF32, kDim, 1024, &seg3, 1, tact, tact_s, 0.0f, s));
+  GemvJob jm{m->mod.w, m->mod.s, m->mod.b, c->p<float>(B_MODS), m->mod.N};
+  QI_LAUNCH(QI_PROF_PRE, 1, gemv_i8_launch(tact, tact_s, kDim, &jm, 1, s));
+  QI_LAUNCH(QI_PROF_PRE, 1,
+            gemv_bf16_launch(c->p<float>(B_TSILU), m->norm_out_w, m->norm_out_b, c->p<float>(B_ADA), 2 * kDim, kDim, s));
+  return QI_OK;
+}
+
+// patchify + img_in (BF16) and txt_norm + txt_in (BF16) (transformer.cu:266-290, 396-422).
+int fwd_inputs(Fwd& f, const void* x, const void* ctx_txt, int H, int W, float* x_img, float* x_txt) {
+  qi_ctx* c = f.c;
+  const qi_model* m = f.m;
+  cudaStream_t s = f.s;
+  QI_LAUNCH(QI_PROF_PRE, 1, patchify_launch(x, c->buf[B_PATCH], f.nb, H, W, s));
+  GemmBf16Desc d{c->buf[B_PATCH], m->img_in_w, m->img_in_b, x_img, static_cast<int>(f.Mi), kDim, kPatchDim, kDim};
+  QI_LAUNCH(QI_PROF_PRE, 1, gemm_bf16_launch(d, s, c->err, c->num_sms));
+  QI_LAUNCH(QI_PROF_PRE, 1,
+            rmsnorm_bf16_launch(ctx_txt, m->txt_norm, c->buf[B_TXTN], static_cast<int>(f.Mt), kTxtDim, 1e-6f, s));
+  GemmBf16Desc e{c->buf[B_TXTN], m->txt_in_w, m->txt_in_b, x_txt, static_cast<int>(f.Mt), kDim, kTxtDim, kDim};
+  QI_LAUNCH(QI_PROF_PRE, 1, gemm_bf16_launch(e, s, c->err, c->num_sms));
+  return QI_OK;
+}
+
+// The double-stream blocks [b0, b1) on residual streams x_img [Mi,3072] and
+// x_txt [Mt,3072] (transformer.cu:497-836).
+int fwd_blocks(Fwd& f, float* x_img, float* x_txt, const float* pe, int b0, int b1) {
+  qi_ctx* c = f.c;
+  const qi_model* m = f.m;
+  cudaStream_t s = f.s;
+  const long long Mi = f.Mi, Mt = f.Mt, Ma = f.Ma;
+  const int nb = f.nb, n_img = f.n_img, n_txt = f.n_txt, S = f.S, BH = f.BH;
   int8_t* act = c->p<int8_t>(B_ACT);
   float* act_s = c->p<float>(B_ACT_S);
-  float* x_img = c->p<float>(B_X);
-  float* x_txt = x_img + Mi * kDim;
-  float* mods = c->p<float>(B_MODS);
-  int n = 0;  // launches
-
-  // 1. patchify (transformer.cu:266-290)
-  QI_LAUNCH(QI_PROF_PRE, 1, patchify_launch(x, c->buf[B_PATCH], nb, H, W, s));
-  // 2. timestep MLP: sinusoid -> INT8 linear -> SiLU -> INT8 linear (transformer.cu:330-349)
-  QI_LAUNCH(QI_PROF_PRE, 1, timestep_embedding_launch(timestep, c->p<float>(B_TEMB256), s));
-  {
-    RowSeg seg{c->buf[B_TEMB256], 256, nullptr, nullptr, 1};
-    QI_LAUNCH(QI_PROF_PRE, 1, rowquant_launch(kSrcF32, 256, 256, &seg, 1, c->p<int8_t>(B_TACT), c->p<float>(B_TACT_S), 0.0f, s));
-    GemvJob j1{m->t1.w, m->t1.s, m->t1.b, c->p<float>(B_T1), kDim};
-    QI_LAUNCH(QI_PROF_PRE, 1, gemv_i8_launch(c->p<int8_t>(B_TACT), c->p<float>(B_TACT_S), 256, &j1, 1, s));
-    QI_LAUNCH(QI_PROF_PRE, 1, silu_launch(c->p<float>(B_T1), c->p<float>(B_T1), kDim, s));
-    RowSeg seg2{c->buf[B_T1], kDim, nullptr, nullptr, 1};
-    QI_LAUNCH(QI_PROF_PRE, 1, rowquant_launch(kSrcF32, kDim, 1024, &seg2, 1, c->p<int8_t>(B_TACT), c->p<float>(B_TACT_S), 0.0f, s));
-    GemvJob j2{m->t2.w, m->t2.s, m->t2.b, c->p<float>(B_TEMB), kDim};
-    QI_LAUNCH(QI_PROF_PRE, 1, gemv_i8_launch(c->p<int8_t>(B_TACT), c->p<float>(B_TACT_S), kDim, &j2, 1, s));
-  }
-  // 3. all modulation vectors (transformer.cu:506-515) and the output AdaLN
-  //    embedding (transformer.cu:874-877) from SiLU(t_emb)
-  QI_LAUNCH(QI_PROF_PRE, 1, silu_launch(c->p<float>(B_TEMB), c->p<float>(B_TSILU), kDim, s));
-  {
-    RowSeg seg{c->buf[B_TSILU], kDim, nullptr, nullptr, 1};
-    QI_LAUNCH(QI_PROF_PRE, 1, rowquant_launch(kSrcF32, kDim, 1024, &seg, 1, c->p<int8_t>(B_TACT), c->p<float>(B_TACT_S), 0.0f, s));
-    GemvJob jm{m->mod.w, m->mod.s, m->mod.b, mods, m->mod.N};
-    QI_LAUNCH(QI_PROF_PRE, 1, gemv_i8_launch(c->p<int8_t>(B_TACT), c->p<float>(B_TACT_S), kDim, &jm, 1, s));
-    QI_LAUNCH(QI_PROF_PRE, 1, gemv_bf16_launch(c->p<float>(B_TSILU), m->norm_out_w, m->norm_out_b, c->p<float>(B_ADA), 2 * kDim, kDim, s));
-  }
-  // 4. img_in (BF16) and txt_norm + txt_in (BF16) (transformer.cu:396-422)
-  {
-    GemmBf16Desc d{c->buf[B_PATCH], m->img_in_w, m->img_in_b, x_img, static_cast<int>(Mi), kDim, kPatchDim, kDim};
-    QI_LAUNCH(QI_PROF_PRE, 1, gemm_bf16_launch(d, s, c->err, c->num_sms));
-    QI_LAUNCH(QI_PROF_PRE, 1, rmsnorm_bf16_launch(ctx_txt, m->txt_norm, c->buf[B_TXTN], static_cast<int>(Mt), kTxtDim, 1e-6f, s));
-    GemmBf16Desc e{c->buf[B_TXTN], m->txt_in_w, m->txt_in_b, x_txt, static_cast<int>(Mt), kDim, kTxtDim, kDim};
-    QI_LAUNCH(QI_PROF_PRE, 1, gemm_bf16_launch(e, s, c->err, c->num_sms));
-  }
+  const float* mods = c->p<float>(B_MODS);
   float* qkv = c->p<float>(B_QKV);
   float* hbuf = c->p<float>(B_H);
-  // 5. the double-stream blocks (transformer.cu:497-836)
-  for (int bi = 0; bi < L; ++bi) {
+  for (int bi = b0; bi < b1; ++bi) {
     const BlockW& B = m->blocks[bi];
     const float* mi = mods + (static_cast<size_t>(bi) * 2 + 0) * 6 * kDim;
     const float* mt = mods + (static_cast<size_t>(bi) * 2 + 1) * 6 * kDim;
@@ -597,8 +627,9 @@ extern "C" int qi_forward(qi_ctx* c, const qi_model* m, int nb, const void* x, f
     QkvPostArgs qa{qkv, qkv + Mi * 3 * kDim, B.norms, B.norms + kHeadDim, B.norms + 2 * kHeadDim,
                    B.norms + 3 * kHeadDim, pe, c->buf[B_QH], c->buf[B_KH], c->buf[B_VH], nb, n_img, n_txt};
     QI_LAUNCH(QI_PROF_QKV_POST, 1, qkv_post_launch(qa, s));
-    QI_LAUNCH(QI_PROF_SAGE_QUANT, 3, sage_quantize_launch(c->buf[B_QH], c->buf[B_KH], BH, S, c->p<float>(B_KMEAN), c->p<int8_t>(B_QC),
-                                c->p<float>(B_QS), c->p<int8_t>(B_KC), c->p<float>(B_KS), s));
+    QI_LAUNCH(QI_PROF_SAGE_QUANT, 3,
+              sage_quantize_launch(c->buf[B_QH], c->buf[B_KH], BH, S, c->p<float>(B_KMEAN), c->p<int8_t>(B_QC),
+                                   c->p<float>(B_QS), c->p<int8_t>(B_KC), c->p<float>(B_KS), s));
     AttnArgs aa{c->p<int8_t>(B_QC), c->p<float>(B_QS), c->p<int8_t>(B_KC), c->p<float>(B_KS), c->buf[B_VH],
                 c->buf[B_O], BH, S, kHeads, 1.0f / sqrtf(128.0f), 1, nb, n_img, n_txt};
     QI_LAUNCH(QI_PROF_ATTENTION, 1, attention_launch(aa, s, c->err));
@@ -625,15 +656,54 @@ extern "C" int qi_forward(qi_ctx* c, const qi_model* m, int nb, const void* x, f
                        static_cast<int>(Mt), kDim, kMlp, kDim}};
     QI_LAUNCH(QI_PROF_GEMM_FC2, 1, gemm_i8_launch(g2, 2, kEpiResidual, s, c->err, c->num_sms));
   }
-  // 6. AdaLayerNormContinuous (scale = first half, shift = second half,
-  //    transformer.cu:881-884) -> BF16 -> proj_out -> unpatchify
+  return QI_OK;
+}
+
+// AdaLayerNormContinuous (scale = first half, shift = second half,
+// transformer.cu:881-884) -> BF16 -> proj_out -> unpatchify (:889-926).
+int fwd_output(Fwd& f, const float* x_img, int H, int W, void* out) {
+  qi_ctx* c = f.c;
+  const qi_model* m = f.m;
+  cudaStream_t s = f.s;
   const float* ada = c->p<float>(B_ADA);
-  QI_LAUNCH(QI_PROF_POST, 1, layernorm_mod_launch(x_img, ada + kDim, ada, static_cast<int>(Mi), kDim, 1e-6f, nullptr, c->buf[B_FIN], s));
-  GemmBf16Desc pd{c->buf[B_FIN], m->proj_out_w, m->proj_out_b, c->p<float>(B_PROJ), static_cast<int>(Mi), kPatchDim,
+  QI_LAUNCH(QI_PROF_POST, 1,
+            layernorm_mod_launch(x_img, ada + kDim, ada, static_cast<int>(f.Mi), kDim, 1e-6f, nullptr, c->buf[B_FIN], s));
+  GemmBf16Desc pd{c->buf[B_FIN], m->proj_out_w, m->proj_out_b, c->p<float>(B_PROJ), static_cast<int>(f.Mi), kPatchDim,
                   kDim, kPatchDim};
   QI_LAUNCH(QI_PROF_POST, 1, gemm_bf16_launch(pd, s, c->err, c->num_sms));
-  QI_LAUNCH(QI_PROF_POST, 1, unpatchify_launch(c->p<float>(B_PROJ), out, nb, H, W, s));
-  c->launches = n;
+  QI_LAUNCH(QI_PROF_POST, 1, unpatchify_launch(c->p<float>(B_PROJ), out, f.nb, H, W, s));
   return QI_OK;
+}
 #undef QI_LAUNCH
+}  // namespace
+
+extern "C" int qi_forward(qi_ctx* c, const qi_model* m, int nb, const void* x, float timestep, const void* ctx_txt,
+                          int n_txt, const float* pe, int H, int W, void* out, void* stream) {
+  if (!c || !m || !x || !ctx_txt || !pe || !out) return QI_ERR_ARG;
+  if (nb < 1 || nb > 8 || n_txt < 1 || H < 2 || W < 2 || (H & 1) || (W & 1)) return QI_ERR_ARG;
+  Fwd f;
+  QI_TRY(fwd_init(f, c, m, nb, (H / 2) * (W / 2), n_txt, stream));
+  float* x_img = c->p<float>(B_X);
+  float* x_txt = x_img + f.Mi * kDim;
+  QI_TRY(fwd_inputs(f, x, ctx_txt, H, W, x_img, x_txt));
+  QI_TRY(fwd_modulation(f, timestep));
+  QI_TRY(fwd_blocks(f, x_img, x_txt, pe, 0, m->nblocks));
+  QI_TRY(fwd_output(f, x_img, H, W, out));
+  c->launches = f.n;
+  return QI_OK;
+}
+
+extern "C" int qi_forward_blocks(qi_ctx* c, const qi_model* m, int nb, int n_img, int n_txt, float* img, float* txt,
+                                 float timestep, const float* pe, int block_begin, int block_end, void* stream) {
+  if (!c || !m || !img || !txt || !pe) return QI_ERR_ARG;
+  if (nb < 1 || nb > 8 || n_img < 1 || n_txt < 1 || block_begin < 0 || block_end > m->nblocks ||
+      block_begin > block_end)
+    return QI_ERR_ARG;
+  if ((reinterpret_cast<uintptr_t>(img) & 15) || (reinterpret_cast<uintptr_t>(txt) & 15)) return QI_ERR_ALIGN;
+  Fwd f;
+  QI_TRY(fwd_init(f, c, m, nb, n_img, n_txt, stream));
+  QI_TRY(fwd_modulation(f, timestep));
+  QI_TRY(fwd_blocks(f, img, txt, pe, block_begin, block_end));
+  c->launches = f.n;
+  return QI_OK;
 }

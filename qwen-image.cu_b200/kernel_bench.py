@@ -1,0 +1,98 @@
+"""Kernel-level timing of the hot kernels at the forward's shapes (C ABI calls,
+CUDA events on the launching stream).  Also the target of the ncu captures
+summarised in profiles/.
+
+    python qwen-image.cu_b200/kernel_bench.py [--which gemm,attn,quant] [--iters N] [--config c4|c2]
+
+GEMM shapes are those of one CFG-batched C4 forward (M = 2 x 6889 image +
+2 x 256 text tokens): fused QKV (N 9216), out-projection (N 3072), fc1
+(N 12288), fc2 (K 12288).  Attention: BASELINE config 2 (B 2, 24 heads,
+4352 tokens) or the C4 joint sequence (7145 tokens).
+"""
+import argparse
+import json
+import os
+import sys
+
+import torch
+
+sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
+import qib200 as Q  # noqa: E402
+
+M_IMG, M_TXT = 2 * 6889, 2 * 256
+GEMMS = {"qkv": (9216, 3072), "out": (3072, 3072), "fc1": (12288, 3072), "fc2": (3072, 12288)}
+
+
+def time_it(fn, iters, warmup=3):
+    for _ in range(warmup):
+        fn()
+    s = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    for _ in range(iters):
+        fn()
+    e1.record(s)
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / iters
+
+
+def bench_gemm(iters, res):
+    for name, (N, K) in GEMMS.items():
+        M = M_IMG + M_TXT
+        a = torch.randint(-127, 128, (M, K), dtype=torch.int8, device="cuda")
+        w = torch.randint(-127, 128, (N, K), dtype=torch.int8, device="cuda")
+        sa = torch.rand(M, device="cuda") * 1e-3
+        sw = torch.rand(N, device="cuda") * 1e-3
+        b = torch.zeros(N, dtype=torch.bfloat16, device="cuda")
+        out = torch.empty(M, N, device="cuda")
+        epi = Q.EPI_GELU if name == "fc1" else Q.EPI_STORE
+        ms = time_it(lambda: Q.linear_i8(a, sa, w, sw, b, epi, out=out), iters)
+        tf = 2.0 * M * N * K / (ms * 1e-3) / 1e12
+        res[f"gemm_{name}"] = {"M": M, "N": N, "K": K, "ms": round(ms, 4), "tops": round(tf, 1)}
+        del a, w, out
+
+
+def bench_attn(iters, res, config):
+    B, S = (2, 4352) if config == "c2" else (2, 7145)
+    BH = B * 24
+    q = Q.synth((BH, S, 128), 1, 1.0).half()
+    k = Q.synth((BH, S, 128), 2, 1.0).half()
+    v = Q.synth((BH, S, 128), 3, 1.0).half()
+    kmean, qc, qs, kc, ks = Q.sage_quantize(q, k)
+    ms_q = time_it(lambda: Q.sage_quantize(q, k), iters)
+    ms = time_it(lambda: Q.sage_attention(q, k, v), iters)
+    flops = 4.0 * BH * S * S * 128
+    res["sage_quant"] = {"BH": BH, "S": S, "ms": round(ms_q, 4)}
+    res["attention_incl_quant"] = {"BH": BH, "S": S, "ms": round(ms, 4),
+                                   "tflops": round(flops / ((ms - ms_q) * 1e-3) / 1e12, 1)}
+
+
+def bench_quant(iters, res):
+    M = M_IMG + M_TXT
+    for K, B in ((3072, 1024), (12288, 4096)):
+        x = Q.synth((M, K), 7, 1.0)
+        ms = time_it(lambda: Q.fwht_quantize(x, B), iters)
+        gbs = (M * K * 4 + M * K + M * 4) / (ms * 1e-3) / 1e9
+        res[f"fwht_quant_{K}"] = {"M": M, "K": K, "ms": round(ms, 4), "gbs": round(gbs, 1)}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--which", default="gemm,attn,quant")
+    ap.add_argument("--iters", type=int, default=10)
+    ap.add_argument("--config", default="c2")
+    a = ap.parse_args()
+    torch.cuda.set_device(0)
+    res = {}
+    w = a.which.split(",")
+    if "gemm" in w:
+        bench_gemm(a.iters, res)
+    if "attn" in w:
+        bench_attn(a.iters, res, a.config)
+    if "quant" in w:
+        bench_quant(a.iters, res)
+    print(json.dumps(res))
+
+
+if __name__ == "__main__":
+    main()

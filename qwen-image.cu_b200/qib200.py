@@ -89,6 +89,10 @@ def lib():
             "qi_model_destroy": ([vp], i),
             "qi_model_num_blocks": ([vp], i),
             "qi_forward": ([vp, vp, i, vp, f, vp, i, vp, i, i, vp, vp], i),
+            "qi_forward_blocks": ([vp, vp, i, i, i, vp, vp, f, vp, i, i, vp], i),
+            "qi_cfg_euler_step": ([vp, vp, vp, f, f, f, i, i, vp, vp], i),
+            "qi_ctx_set_profiling": ([vp, i], i),
+            "qi_ctx_profile": ([vp, vp, vp, i], i),
             "qi_rope_table": ([i, i, i, vp], i),
             "qi_synth_fill": ([vp, ll, ull, f, f, i, vp], i),
             "qi_seed_for": ([ull, ctypes.c_char_p], ull),
@@ -330,3 +334,17 @@ def forward(ctx, model, x, t, txt, pe, out=None):
         out = torch.empty_like(x)
     check(lib().qi_forward(ctx.h, model.h, nb, _p(x), float(t), _p(txt), n_txt, _p(pe), H, W, _p(out), _stream()))
     return out
+
+
+def forward_blocks(ctx, model, img, txt, t, pe, b0, b1, nb=1):
+    """Runs blocks [b0, b1) in place on FP32 residual streams img [nb*n_img,3072], txt [nb*n_txt,3072]."""
+    n_img = img.shape[0] // nb
+    n_txt = txt.shape[0] // nb
+    check(lib().qi_forward_blocks(ctx.h, model.h, nb, n_img, n_txt, _p(img), _p(txt), float(t), _p(pe), b0, b1,
+                                  _stream()))
+
+
+def cfg_euler_step(latent, cond, uncond, cfg_scale, sigma, sigma_next, latent_bf16):
+    _, _, H, W = latent.shape
+    check(lib().qi_cfg_euler_step(_p(latent), _p(cond), _p(uncond), float(cfg_scale), float(sigma), float(sigma_next),
+                                  H, W, _p(latent_bf16), _stream()))

@@ -100,7 +100,9 @@ def main(out):
         d = {"out": y.float().cpu().numpy()}
         for f in sorted(glob.glob("cuda_*.bin")):
             a = np.fromfile(f, dtype=np.float32)
-            key = os.path.basename(f)[5:-4]
+            key = os.path.basename(f)[5:]
+            while key.endswith(".bin"):  # block stems already end in .bin (transformer.cu:503)
+                key = key[:-4]
             keep32 = a.size <= 20000
             d[key] = a if keep32 else a.astype(np.float16)
         os.chdir(cwd)
