@@ -173,6 +173,12 @@ int qi_rope_table(int h, int w, int n_txt, float* pe_host);
 /* Number of kernel launches issued by the last qi_forward on this context. */
 int qi_ctx_last_launch_count(const qi_ctx* ctx);
 
+/* Failure-path self test: launches a kernel that waits on an mbarrier nothing
+ * arrives on, giving up after limit_us (<= 2 s), the way every wait in the
+ * tensor-core kernels gives up instead of hanging.  The next qi_ctx_check
+ * returns QI_ERR_DEVICE; the context stays usable.                          */
+int qi_selftest_wait_timeout(qi_ctx* ctx, int limit_us, void* stream);
+
 /* Per-stage timing of qi_forward with CUDA events (the reference's
  * PROFILE_BLOCK hook, transformer.cu:486-495 / 838-860).  While enabled each
  * forward records an event pair around every launch; qi_ctx_profile then

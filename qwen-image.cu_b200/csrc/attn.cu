@@ -367,110 +367,157 @@ __device__ __forceinline__ int8_t cvt_rni_sat_s8(float x) {
   return static_cast<int8_t>(d & 0xff);
 }
 
-// Per (head, dim): serial sum over tokens in order (the reference's order),
-// 32 dims per warp so each token read is one 64-byte segment.
-__global__ void sage_kmean_kernel(const __half* __restrict__ k, float* __restrict__ kmean, int S) {
-  const int bh = blockIdx.x;
-  const int d = blockIdx.y * 32 + threadIdx.x;
-  const __half* p = k + static_cast<size_t>(bh) * S * 128 + d;
+// K mean per (batch-head, dim): the reference sums over tokens serially in
+// token order (sageattention_sm80.cu:759-773); the K codes depend on it, so the
+// order is kept.  One CTA per (batch-head, 32 dims): all 256 threads prefetch
+// the next 256-token x 32-dim tile into shared memory while warp 0 runs the
+// 32 serial chains (lane = dim) over the current one.
+__global__ void __launch_bounds__(256) sage_kmean_kernel(const __half* __restrict__ k, float* __restrict__ kmean, int S) {
+  constexpr int T = 256;
+  __shared__ __align__(16) __half tile[2][T][32];
+  const int bh = blockIdx.x, d0 = blockIdx.y * 32;
+  const __half* base = k + static_cast<size_t>(bh) * S * 128 + d0;
+  const int tid = threadIdx.x;
+  const int nchunks = (S + T - 1) / T;
+  uint4 pre[4];
+  auto load = [&](int c) {
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const int t = c * T + (tid >> 2) + 64 * r;
+      pre[r] = (t < S) ? *reinterpret_cast<const uint4*>(base + static_cast<size_t>(t) * 128 + (tid & 3) * 8)
+                       : make_uint4(0, 0, 0, 0);
+    }
+  };
+  auto stash = [&](int b) {
+#pragma unroll
+    for (int r = 0; r < 4; ++r) *reinterpret_cast<uint4*>(&tile[b][(tid >> 2) + 64 * r][(tid & 3) * 8]) = pre[r];
+  };
   float sum = 0.0f;
-  int s = 0;
-  for (; s + 8 <= S; s += 8) {
-    __half h[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) h[i] = p[static_cast<size_t>(s + i) * 128];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) sum += __half2float(h[i]);
+  load(0);
+  stash(0);
+  __syncthreads();
+  for (int c = 0; c < nchunks; ++c) {
+    if (c + 1 < nchunks) load(c + 1);
+    if (tid < 32) {
+      const int n = min(T, S - c * T);
+      const __half* col = &tile[c & 1][0][tid];
+#pragma unroll 8
+      for (int t = 0; t < n; ++t) sum += __half2float(col[t * 32]);
+    }
+    __syncthreads();
+    if (c + 1 < nchunks) stash((c + 1) & 1);
+    __syncthreads();
   }
-  for (; s < S; ++s) sum += __half2float(p[static_cast<size_t>(s) * 128]);
-  kmean[bh * 128 + d] = sum / fmaxf(static_cast<float>(S), 1.0f);
+  if (tid < 32) kmean[bh * 128 + d0 + tid] = sum / fmaxf(static_cast<float>(S), 1.0f);
 }
 
-__device__ __forceinline__ float block128_max(float v, float* red) {
+__device__ __forceinline__ float warp_max_f(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
-  __syncthreads();
-  return fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+  return v;
 }
 
-__global__ void sage_quant_q_kernel(const __half* __restrict__ q, int8_t* __restrict__ qc, float* __restrict__ qs,
-                                    int S) {
-  __shared__ float red[4];
-  __shared__ float block_scale;
-  const int group = blockIdx.x, bh = blockIdx.y, d = threadIdx.x;
-  const int token_base = (group / 32) * 128 + ((group % 32) / 8) * 32 + (group % 8);
-  const __half* hp = q + static_cast<size_t>(bh) * S * 128;
-  float vals[4];
-  float amax = 1e-7f;
+// Q per-thread INT8 (sageattention_sm80.cu:775-824): one CTA per (128-query
+// block, batch-head), one warp per scale group at a time; group g of the
+// block covers tokens (g/8)*32 + g%8 + {0, 8, 16, 24}; lane l holds dims
+// 4l..4l+3.  The group max is order-free; scale and codes use the
+// reference's expressions.
+__global__ void __launch_bounds__(256) sage_quant_q_kernel(const __half* __restrict__ q, int8_t* __restrict__ qc,
+                                                           float* __restrict__ qs, int S) {
+  const int blk = blockIdx.x, bh = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const __half* hp = q + static_cast<size_t>(bh) * S * 128 + lane * 4;
+  int8_t* out = qc + static_cast<size_t>(bh) * S * 128 + lane * 4;
+  const int ngq = ((S + 127) / 128) * 32;
+#pragma unroll 1
+  for (int g = warp; g < 32; g += 8) {
+    const int token_base = blk * 128 + (g / 8) * 32 + (g % 8);
+    float vals[4][4];
+    float amax = 1e-7f;
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int t = token_base + i * 8;
-    float v = 0.0f;
-    if (t < S) v = __half2float(hp[static_cast<size_t>(t) * 128 + d]);
-    vals[i] = v;
-    amax = fmaxf(amax, fabsf(v));
-  }
-  const float block_amax = block128_max(amax, red);
-  if (threadIdx.x == 0) {
-    block_scale = block_amax / 127.0f + 1e-7f;
-    qs[static_cast<size_t>(bh) * (((S + 127) / 128) * 32) + group] = block_scale;
-  }
-  __syncthreads();
-  const float inv_scale = 1.0f / block_scale;
-  int8_t* out = qc + static_cast<size_t>(bh) * S * 128;
+    for (int i = 0; i < 4; ++i) {
+      const int t = token_base + i * 8;
+      uint2 raw = make_uint2(0, 0);
+      if (t < S) raw = *reinterpret_cast<const uint2*>(hp + static_cast<size_t>(t) * 128);
+      const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
+      const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
+      vals[i][0] = a.x;
+      vals[i][1] = a.y;
+      vals[i][2] = b.x;
+      vals[i][3] = b.y;
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int t = token_base + i * 8;
-    if (t < S) out[static_cast<size_t>(t) * 128 + d] = cvt_rni_sat_s8(vals[i] * inv_scale);
+      for (int e = 0; e < 4; ++e) amax = fmaxf(amax, fabsf(vals[i][e]));
+    }
+    const float block_amax = warp_max_f(amax);
+    const float block_scale = block_amax / 127.0f + 1e-7f;
+    if (lane == 0) qs[static_cast<size_t>(bh) * ngq + blk * 32 + g] = block_scale;
+    const float inv_scale = 1.0f / block_scale;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int t = token_base + i * 8;
+      if (t >= S) continue;
+      char4 c;
+      c.x = cvt_rni_sat_s8(vals[i][0] * inv_scale);
+      c.y = cvt_rni_sat_s8(vals[i][1] * inv_scale);
+      c.z = cvt_rni_sat_s8(vals[i][2] * inv_scale);
+      c.w = cvt_rni_sat_s8(vals[i][3] * inv_scale);
+      *reinterpret_cast<char4*>(out + static_cast<size_t>(t) * 128) = c;
+    }
   }
 }
 
-__global__ void sage_quant_k_kernel(const __half* __restrict__ k, const float* __restrict__ kmean,
-                                    int8_t* __restrict__ kc, float* __restrict__ ks, int S) {
-  __shared__ float red[4];
-  __shared__ float block_scale;
-  const int group = blockIdx.x, bh = blockIdx.y, d = threadIdx.x;
-  const int token_base = (group / 4) * 64 + (group % 4) * 2;
-  const __half* hp = k + static_cast<size_t>(bh) * S * 128;
-  const float mean = kmean[bh * 128 + d];
-  float vals[16];
+// K per-thread INT8 after mean smoothing (sageattention_sm80.cu:826-886): one
+// CTA per (64-key block, batch-head), warp w = scale group w covering tokens
+// 2w + 8i + {0, 1}, i = 0..7.
+__global__ void __launch_bounds__(128) sage_quant_k_kernel(const __half* __restrict__ k, const float* __restrict__ kmean,
+                                                           int8_t* __restrict__ kc, float* __restrict__ ks, int S) {
+  const int blk = blockIdx.x, bh = blockIdx.y;
+  const int g = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const __half* hp = k + static_cast<size_t>(bh) * S * 128 + lane * 4;
+  int8_t* out = kc + static_cast<size_t>(bh) * S * 128 + lane * 4;
+  const float4 mean = *reinterpret_cast<const float4*>(kmean + bh * 128 + lane * 4);
+  const int token_base = blk * 64 + g * 2;
+  float vals[16][4];
   float amax = 1e-7f;
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const int t0 = token_base + i * 8, t1 = t0 + 1;
-    float v0 = 0.0f, v1 = 0.0f;
-    if (t0 < S) v0 = __half2float(hp[static_cast<size_t>(t0) * 128 + d]) - mean;
-    if (t1 < S) v1 = __half2float(hp[static_cast<size_t>(t1) * 128 + d]) - mean;
-    vals[2 * i] = v0;
-    vals[2 * i + 1] = v1;
-    amax = fmaxf(amax, fabsf(v0));
-    amax = fmaxf(amax, fabsf(v1));
-  }
-  const float block_amax = block128_max(amax, red);
-  if (threadIdx.x == 0) {
-    block_scale = block_amax / 127.0f + 1e-7f;
-    ks[static_cast<size_t>(bh) * (((S + 63) / 64) * 4) + group] = block_scale;
-  }
-  __syncthreads();
-  const float inv_scale = 1.0f / block_scale;
-  int8_t* out = kc + static_cast<size_t>(bh) * S * 128;
+  for (int i = 0; i < 16; ++i) {
+    const int t = token_base + (i >> 1) * 8 + (i & 1);
+    uint2 raw = make_uint2(0, 0);
+    const bool in = t < S;
+    if (in) raw = *reinterpret_cast<const uint2*>(hp + static_cast<size_t>(t) * 128);
+    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
+    const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
+    vals[i][0] = in ? a.x - mean.x : 0.0f;
+    vals[i][1] = in ? a.y - mean.y : 0.0f;
+    vals[i][2] = in ? b.x - mean.z : 0.0f;
+    vals[i][3] = in ? b.y - mean.w : 0.0f;
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const int t0 = token_base + i * 8, t1 = t0 + 1;
-    if (t0 < S) out[static_cast<size_t>(t0) * 128 + d] = cvt_rni_sat_s8(vals[2 * i] * inv_scale);
-    if (t1 < S) out[static_cast<size_t>(t1) * 128 + d] = cvt_rni_sat_s8(vals[2 * i + 1] * inv_scale);
+    for (int e = 0; e < 4; ++e) amax = fmaxf(amax, fabsf(vals[i][e]));
+  }
+  const float block_amax = warp_max_f(amax);
+  const float block_scale = block_amax / 127.0f + 1e-7f;
+  if (lane == 0) ks[static_cast<size_t>(bh) * (((S + 63) / 64) * 4) + blk * 4 + g] = block_scale;
+  const float inv_scale = 1.0f / block_scale;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const int t = token_base + (i >> 1) * 8 + (i & 1);
+    if (t >= S) continue;
+    char4 c;
+    c.x = cvt_rni_sat_s8(vals[i][0] * inv_scale);
+    c.y = cvt_rni_sat_s8(vals[i][1] * inv_scale);
+    c.z = cvt_rni_sat_s8(vals[i][2] * inv_scale);
+    c.w = cvt_rni_sat_s8(vals[i][3] * inv_scale);
+    *reinterpret_cast<char4*>(out + static_cast<size_t>(t) * 128) = c;
   }
 }
 
 int sage_quantize_launch(const void* q, const void* k, int BH, int S, float* kmean, int8_t* qc, float* qs, int8_t* kc,
                          float* ks, cudaStream_t stream) {
   if (BH <= 0 || S <= 0) return QI_ERR_ARG;
-  sage_kmean_kernel<<<dim3(BH, 4), 32, 0, stream>>>(reinterpret_cast<const __half*>(k), kmean, S);
-  sage_quant_q_kernel<<<dim3(((S + 127) / 128) * 32, BH), 128, 0, stream>>>(reinterpret_cast<const __half*>(q), qc,
-                                                                           qs, S);
-  sage_quant_k_kernel<<<dim3(((S + 63) / 64) * 4, BH), 128, 0, stream>>>(reinterpret_cast<const __half*>(k), kmean,
-                                                                         kc, ks, S);
+  sage_kmean_kernel<<<dim3(BH, 4), 256, 0, stream>>>(reinterpret_cast<const __half*>(k), kmean, S);
+  sage_quant_q_kernel<<<dim3((S + 127) / 128, BH), 256, 0, stream>>>(reinterpret_cast<const __half*>(q), qc, qs, S);
+  sage_quant_k_kernel<<<dim3((S + 63) / 64, BH), 128, 0, stream>>>(reinterpret_cast<const __half*>(k), kmean, kc, ks,
+                                                                    S);
   return cudaGetLastError() == cudaSuccess ? QI_OK : QI_ERR_CUDA;
 }
 

@@ -206,6 +206,11 @@ int qi_ctx_check(qi_ctx* c) {
 
 int qi_ctx_last_launch_count(const qi_ctx* c) { return c ? c->launches : 0; }
 
+int qi_selftest_wait_timeout(qi_ctx* c, int limit_us, void* stream) {
+  if (!c) return QI_ERR_ARG;
+  return selftest_wait_timeout(c->err, limit_us, reinterpret_cast<cudaStream_t>(stream));
+}
+
 int qi_ctx_set_profiling(qi_ctx* c, int enable) {
   if (!c) return QI_ERR_ARG;
   c->profiling = enable != 0;

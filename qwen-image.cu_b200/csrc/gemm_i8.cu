@@ -16,7 +16,9 @@
 // one tile overlaps the main loop of the next.
 //
 // Warp roles (192 threads): warp 0 TMA producer, warp 1 MMA issuer (and TMEM
-// owner), warps 2-5 epilogue (one TMEM lane = one output row per thread).
+// owner), warps 2-5 epilogue (one TMEM lane = one output row per thread); the
+// epilogue writes through swizzled shared-memory sub-tiles and TMA stores, so
+// global writes are full lines instead of one row per lane.
 #include "qi_internal.h"
 #include "sm100.cuh"
 
@@ -29,12 +31,16 @@ constexpr int B_BYTES = BN * BK;                 // 32 KB
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;   // 48 KB
 constexpr int TMEM_COLS = 512;                   // 2 accumulators x 256 columns
 constexpr int THREADS = 192;
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+constexpr int EPI_WARPS = 4;
+constexpr int EPI_BUF = 32 * 32 * 4;                  // one warp's 32x32 FP32 sub-tile
+constexpr int EPI_BYTES = EPI_WARPS * 2 * EPI_BUF;    // double buffered per warp: 32 KB
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + EPI_BYTES + 1024 /*align*/ + 256 /*barriers*/;
 }  // namespace gemm
 
 struct alignas(64) GemmProblemDev {
   CUtensorMap tmA;
   CUtensorMap tmB;
+  CUtensorMap tmO;  // FP32 output [M, N] (ldo), 32x32 boxes, 128-byte swizzle
   const float* sa;
   const float* sw;
   const __nv_bfloat16* bias;
@@ -70,11 +76,14 @@ __global__ void __launch_bounds__(gemm::THREADS, 1) gemm_kernel(const __grid_con
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * A_BYTES;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint8_t* sE = smem + STAGES * STAGE_BYTES;  // epilogue staging
+  uint64_t* full = reinterpret_cast<uint64_t*>(sE + EPI_BYTES);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  uint64_t* xfull = tempty + 2;  // [4 warps][2 buffers] residual sub-tile loaded
+  uint64_t* drain = xfull + 2 * EPI_WARPS;  // MMA completion before teardown
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -89,11 +98,14 @@ __global__ void __launch_bounds__(gemm::THREADS, 1) gemm_kernel(const __grid_con
       mbar_init(&tfull[b], 1);
       mbar_init(&tempty[b], 4);
     }
+    for (int b = 0; b < 2 * EPI_WARPS; ++b) mbar_init(&xfull[b], 1);
+    mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
     for (int i = 0; i < args.nprob; ++i) {
       tma_prefetch_desc(&args.p[i].tmA);
       tma_prefetch_desc(&args.p[i].tmB);
+      tma_prefetch_desc(&args.p[i].tmO);
     }
   }
   if (warp == 1) {
@@ -206,84 +218,151 @@ __global__ void __launch_bounds__(gemm::THREADS, 1) gemm_kernel(const __grid_con
         *abort_flag = 1;
         atomicCAS(args.err, 0, kErrTimeoutMma);
       }
+      // every MMA issued above has completed before TMEM is released
+      mma_commit(drain);
+      const uint64_t t0 = global_timer_ns();
+      while (!mbar_try_wait(drain, 0) && global_timer_ns() - t0 < kWaitLimitNs / 4) {
+      }
     }
   } else {
     // ------------------------------------------------------------ epilogue
+    // Each warp owns 32 accumulator rows (its TMEM lane quarter).  Per 32-column
+    // chunk: TMEM -> registers (thread = row) -> dequant (+GELU / gated
+    // residual) -> the warp's swizzled 32x32 FP32 staging buffer -> one TMA
+    // tensor store.  Two buffers per warp; the residual sub-tile of the next
+    // chunk is TMA-loaded into the free buffer while this one is computed.
     const int quarter = warp & 3;  // TMEM lane quarter this warp may access
-    const int row_in_tile = quarter * 32 + lane;
+    const int ew = warp - 2;       // epilogue warp index 0..3
+    uint8_t* ebuf = sE + ew * 2 * EPI_BUF;
+    uint64_t* xb = xfull + ew * 2;
+    uint32_t xphase = 0;   // parity bit per buffer
+    uint32_t xpending = 0; // buffers with a residual load issued and not yet waited
+    constexpr int NCH = BN / 32;
     int local = 0;
-    for (int t = blockIdx.x; t < args.total_tiles; t += gridDim.x, ++local) {
+    bool ok = true;
+    for (int t = blockIdx.x; t < args.total_tiles && ok; t += gridDim.x, ++local) {
       int pi, m0, n0;
       locate(t, pi, m0, n0);
       const GemmProblemDev& P = args.p[pi];
       const int buf = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
-      bool ok = mbar_wait(&tfull[buf], acc_phase, abort_flag);
-      ok = __all_sync(0xffffffffu, ok);
-      if (!ok) {
-        if (lane == 0) {
-          *abort_flag = 1;
-          atomicCAS(args.err, 0, kErrTimeoutEpilogue);
-        }
+      const int r0 = m0 + quarter * 32;  // first output row of this warp
+      const bool resid = args.epi == kEpiResidual;
+      const int nch = min(NCH, (P.N - n0 + 31) / 32);
+      // residual: fetch chunk 0 before waiting for the accumulator
+      if (resid && r0 < P.M && lane == 0) {
+        bulk_wait_read<0>();
+        mbar_expect_tx(&xb[0], EPI_BUF);
+        tma_load_2d(ebuf, &P.tmO, n0, r0, &xb[0]);
+        xpending |= 1u;
+      }
+      bool w = mbar_wait(&tfull[buf], acc_phase, abort_flag);
+      if (!__all_sync(0xffffffffu, w)) {
+        ok = false;
         break;
       }
       tc_fence_after();
-      const int grow = m0 + row_in_tile;
-      const bool row_ok = grow < P.M;
-      const float sa = (row_ok && !BF16) ? __ldg(P.sa + grow) : 0.0f;
-      float* orow = P.out + static_cast<size_t>(row_ok ? grow : 0) * P.ldo;
+      const int grow = r0 + lane;
+      const float sa = (grow < P.M && !BF16) ? __ldg(P.sa + grow) : 0.0f;
       const uint32_t taddr_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + buf * BN;
 #pragma unroll 1
-      for (int c = 0; c < BN; c += 32) {
+      for (int c = 0; c < nch; ++c) {
+        const int b = c & 1;
+        uint8_t* sbuf = ebuf + b * EPI_BUF;
         uint32_t acc[32];
-        tmem_ld32(taddr_row + c, acc);
+        tmem_ld32(taddr_row + c * 32, acc);
         tmem_ld_wait();
-        const int gcol = n0 + c;
-        if (!row_ok || gcol >= P.N) continue;
-        const float4* sw4 = BF16 ? nullptr : reinterpret_cast<const float4*>(P.sw + gcol);
+        if (r0 >= P.M) continue;  // the whole 32-row slab is past M (all lanes agree)
+        const int gcol = n0 + c * 32;
+        if (resid) {
+          // prefetch the next chunk's residual into the other buffer
+          if (lane == 0 && c + 1 < nch) {
+            bulk_wait_read<0>();
+            mbar_expect_tx(&xb[b ^ 1], EPI_BUF);
+            tma_load_2d(ebuf + (b ^ 1) * EPI_BUF, &P.tmO, gcol + 32, r0, &xb[b ^ 1]);
+            xpending |= 1u << (b ^ 1);
+          }
+          w = mbar_wait(&xb[b], (xphase >> b) & 1, abort_flag);
+          xphase ^= 1u << b;
+          xpending &= ~(1u << b);
+          if (!__all_sync(0xffffffffu, w)) {
+            ok = false;
+            break;
+          }
+        } else {
+          // the store issued from this buffer two chunks ago must have read it
+          if (lane == 0) bulk_wait_read<1>();
+          __syncwarp();
+        }
+        float v[32];
+        if (BF16) {
 #pragma unroll
-        for (int j = 0; j < 32; j += 4) {
-          float v[4];
-          if (BF16) {
-            v[0] = __uint_as_float(acc[j + 0]);
-            v[1] = __uint_as_float(acc[j + 1]);
-            v[2] = __uint_as_float(acc[j + 2]);
-            v[3] = __uint_as_float(acc[j + 3]);
-          } else {
-            float4 w = __ldg(sw4 + j / 4);
-            v[0] = static_cast<float>(static_cast<int32_t>(acc[j + 0])) * sa * w.x;
-            v[1] = static_cast<float>(static_cast<int32_t>(acc[j + 1])) * sa * w.y;
-            v[2] = static_cast<float>(static_cast<int32_t>(acc[j + 2])) * sa * w.z;
-            v[3] = static_cast<float>(static_cast<int32_t>(acc[j + 3])) * sa * w.w;
-          }
-          if (P.bias) {
-            const __nv_bfloat162* b2 = reinterpret_cast<const __nv_bfloat162*>(P.bias + gcol + j);
-            float2 b01 = __bfloat1622float2(b2[0]);
-            float2 b23 = __bfloat1622float2(b2[1]);
-            v[0] += b01.x;
-            v[1] += b01.y;
-            v[2] += b23.x;
-            v[3] += b23.y;
-          }
-          float4* dst = reinterpret_cast<float4*>(orow + gcol + j);
-          if (args.epi == kEpiGelu) {
-            *dst = make_float4(gelu_tanh_dev(v[0]), gelu_tanh_dev(v[1]), gelu_tanh_dev(v[2]), gelu_tanh_dev(v[3]));
-          } else if (args.epi == kEpiResidual) {
-            float4 g = __ldg(reinterpret_cast<const float4*>(P.gate + gcol + j));
-            float4 x = *dst;
-            x.x = x.x + g.x * v[0];
-            x.y = x.y + g.y * v[1];
-            x.z = x.z + g.z * v[2];
-            x.w = x.w + g.w * v[3];
-            *dst = x;
-          } else {
-            *dst = make_float4(v[0], v[1], v[2], v[3]);
+          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(acc[j]);
+        } else {
+          const float4* sw4 = reinterpret_cast<const float4*>(P.sw + gcol);
+#pragma unroll
+          for (int j = 0; j < 32; j += 4) {
+            const float4 ws = __ldg(sw4 + j / 4);
+            v[j + 0] = static_cast<float>(static_cast<int32_t>(acc[j + 0])) * sa * ws.x;
+            v[j + 1] = static_cast<float>(static_cast<int32_t>(acc[j + 1])) * sa * ws.y;
+            v[j + 2] = static_cast<float>(static_cast<int32_t>(acc[j + 2])) * sa * ws.z;
+            v[j + 3] = static_cast<float>(static_cast<int32_t>(acc[j + 3])) * sa * ws.w;
           }
         }
+        if (P.bias) {
+          const __nv_bfloat162* b2 = reinterpret_cast<const __nv_bfloat162*>(P.bias + gcol);
+#pragma unroll
+          for (int j = 0; j < 32; j += 2) {
+            const float2 bb = __bfloat1622float2(b2[j / 2]);
+            v[j] += bb.x;
+            v[j + 1] += bb.y;
+          }
+        }
+        if (args.epi == kEpiGelu) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = gelu_tanh_dev(v[j]);
+        }
+        // row `lane` of the swizzled sub-tile: 16-byte chunk k at k ^ (lane & 7)
+        float4* srow = reinterpret_cast<float4*>(sbuf + lane * 128);
+        if (resid) {
+          const float4* g4 = reinterpret_cast<const float4*>(P.gate + gcol);
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            const float4 x = srow[k ^ (lane & 7)];
+            const float4 g = __ldg(g4 + k);
+            srow[k ^ (lane & 7)] = make_float4(x.x + g.x * v[4 * k + 0], x.y + g.y * v[4 * k + 1],
+                                               x.z + g.z * v[4 * k + 2], x.w + g.w * v[4 * k + 3]);
+          }
+        } else {
+#pragma unroll
+          for (int k = 0; k < 8; ++k)
+            srow[k ^ (lane & 7)] = make_float4(v[4 * k + 0], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(&P.tmO, sbuf, gcol, r0);
+          bulk_commit();
+        }
       }
+      if (!ok) break;
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[buf]);
+    }
+    if (lane == 0) {
+      bulk_wait<0>();  // stores done before the CTA exits
+      for (int b = 0; b < 2; ++b) {  // an abandoned residual load lands before exit
+        if (!(xpending & (1u << b))) continue;
+        const uint64_t t0 = global_timer_ns();
+        while (!mbar_try_wait(&xb[b], (xphase >> b) & 1) && global_timer_ns() - t0 < kWaitLimitNs / 4) {
+        }
+      }
+    }
+    __syncwarp();
+    if (!ok && lane == 0) {
+      *abort_flag = 1;
+      atomicCAS(args.err, 0, kErrTimeoutEpilogue);
     }
   }
 
@@ -296,6 +375,19 @@ __global__ void __launch_bounds__(gemm::THREADS, 1) gemm_kernel(const __grid_con
 }
 
 // ------------------------------------------------------------------ host
+// FP32 output (and residual) [rows, cols] with leading dimension ldo: 32x32
+// boxes, 128-byte swizzle (the epilogue's staging layout).
+static int encode_out(CUtensorMap* tm, const float* base, int rows, int cols, int ldo) {
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ldo) * 4};
+  cuuint32_t box[2] = {32, 32};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = qi_encode_tiled(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box,
+                               estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? QI_OK : QI_ERR_CUDA;
+}
+
 static int encode_kmajor(CUtensorMap* tm, const void* base, int rows, int K, int box_rows, bool bf16) {
   const int esize = bf16 ? 2 : 1;
   cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(rows)};
@@ -353,6 +445,7 @@ int gemm_i8_launch(const GemmDesc* descs, int n, int epi, cudaStream_t stream, i
     if (d.M > 0) {
       if (encode_kmajor(&P.tmA, d.a, d.M, d.K, gemm::BM, false) != QI_OK) return QI_ERR_CUDA;
       if (encode_kmajor(&P.tmB, d.w, d.N, d.K, gemm::BN, false) != QI_OK) return QI_ERR_CUDA;
+      if (encode_out(&P.tmO, d.out, d.M, d.N, d.ldo) != QI_OK) return QI_ERR_CUDA;
     }
     P.sa = d.sa;
     P.sw = d.sw;
@@ -381,6 +474,7 @@ int gemm_bf16_launch(const GemmBf16Desc& d, cudaStream_t stream, int* err_dev, i
   GemmProblemDev& P = args.p[0];
   if (encode_kmajor(&P.tmA, d.a, d.M, d.K, gemm::BM, true) != QI_OK) return QI_ERR_CUDA;
   if (encode_kmajor(&P.tmB, d.w, d.N, d.K, gemm::BN, true) != QI_OK) return QI_ERR_CUDA;
+  if (encode_out(&P.tmO, d.out, d.M, d.N, d.ldo) != QI_OK) return QI_ERR_CUDA;
   P.bias = reinterpret_cast<const __nv_bfloat16*>(d.bias);
   P.out = d.out;
   int tiles = 0;

@@ -132,6 +132,8 @@ int attention_launch(const AttnArgs& a, cudaStream_t stream, int* err_dev);
 int cfg_euler_launch(float* x, const void* cond, const void* uncond, float cfg, float sigma, float sigma_next, int H,
                      int W, void* x_bf16, cudaStream_t stream);
 
+int selftest_wait_timeout(int* err, int limit_us, cudaStream_t stream);
+
 int device_num_sms();
 
 }  // namespace qi

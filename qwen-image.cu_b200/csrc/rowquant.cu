@@ -11,10 +11,9 @@
 //   * normalisation by rsqrtf((float)B) after the butterflies, evaluated at
 //     run time (never constant-folded) with the same fast-math flags;
 //   * scale = max / 127, inverse = 127 / max, code = sat(__float2int_rn(v * inv)).
-// Only the placement of the butterflies differs: the fused kernel keeps EPT
-// consecutive elements per thread in registers (stages < EPT), exchanges
-// with warp shuffles (stages < 32 * EPT) and goes through shared memory only
-// for the widest stages, instead of running every stage in shared memory.
+// Only the placement of the butterflies differs: each warp owns whole
+// Hadamard blocks with a coalesced element layout and runs every stage in
+// registers or warp shuffles; only the row statistics cross warps.
 //
 // The fused kernel also takes the producing op as its prologue:
 //   kSrcLnMod: LayerNorm (no affine) + modulate of the FP32 residual stream
@@ -47,165 +46,180 @@ __device__ __forceinline__ float warp_max(float v) {
   return v;
 }
 
-template <int NT>
-__device__ __forceinline__ float block_sum(float v, float* red) {
-  v = warp_sum(v);
-  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
-  if (l == 0) red[w] = v;
-  __syncthreads();
-  float r = (l < NT / 32) ? red[l] : 0.0f;
-  r = warp_sum(r);
-  __syncthreads();
-  return r;
-}
-template <int NT>
-__device__ __forceinline__ float block_max(float v, float* red) {
-  v = warp_max(v);
-  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
-  if (l == 0) red[w] = v;
-  __syncthreads();
-  float r = (l < NT / 32) ? red[l] : 0.0f;
-  r = warp_max(r);
-  __syncthreads();
-  return r;
-}
+// One row per CTA, NW warps per row; warp w owns the contiguous chunk
+// [w*CH, (w+1)*CH) of CH = K/NW elements, which holds whole Hadamard blocks
+// (had_block <= CH).  Lane l keeps float4 j at element w*CH + 128*j + 4*l, so
+// every warp load and store is one contiguous 512 B (or 256/128 B) span, and
+// the butterfly stages run on the element-index bits they pair:
+//   half = 1, 2        -> the float4's components (registers)
+//   half = 4 .. 64     -> lane bits (warp shuffles, partner lane ^ half/4)
+//   half = 128 ..      -> register index bits (registers)
+// in the reference's stage order.  Only the row statistics cross warps.
+template <int K, int NW, int SRC>
+__global__ void __launch_bounds__(NW * 32) rowquant_warp_kernel(RowSegs segs, int had_block, int8_t* __restrict__ codes,
+                                                                float* __restrict__ scales, float eps) {
+  constexpr int CH = K / NW;
+  constexpr int J = CH / 128;
+  static_assert(CH % 128 == 0, "chunk must be a multiple of 128");
+  __shared__ float red[3][NW];
 
-template <int K, int EPT, int SRC>
-__global__ void __launch_bounds__(K / EPT) rowquant_fused_kernel(RowSegs segs, int had_block, int8_t* __restrict__ codes,
-                                                                 float* __restrict__ scales, float eps) {
-  constexpr int NT = K / EPT;
-  extern __shared__ float xs[];  // K floats (wide stages) + 32 (reductions)
-  float* red = xs + K;
-
-  int row = blockIdx.x;
+  const int row = blockIdx.x;
   const bool second = segs.nseg > 1 && row >= segs.s[0].rows;
-  RowSeg sg;
-  sg.in = second ? segs.s[1].in : segs.s[0].in;
-  sg.ld = second ? segs.s[1].ld : segs.s[0].ld;
-  sg.shift = second ? segs.s[1].shift : segs.s[0].shift;
-  sg.scale = second ? segs.s[1].scale : segs.s[0].scale;
+  const void* in = second ? segs.s[1].in : segs.s[0].in;
+  const long long ld = second ? segs.s[1].ld : segs.s[0].ld;
+  const float* shift = second ? segs.s[1].shift : segs.s[0].shift;
+  const float* scale = second ? segs.s[1].scale : segs.s[0].scale;
   const int local = second ? row - segs.s[0].rows : row;
-  const int t = threadIdx.x;
-  const int c0 = t * EPT;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int base = warp * CH + 4 * lane;
 
-  float v[EPT];
+  float v[J][4];
   if (SRC == kSrcF16) {
-    const __half* in = reinterpret_cast<const __half*>(sg.in) + static_cast<long long>(local) * sg.ld + c0;
+    const __half* src = reinterpret_cast<const __half*>(in) + static_cast<long long>(local) * ld + base;
 #pragma unroll
-    for (int e = 0; e < EPT; e += 8) {
-      uint4 raw = *reinterpret_cast<const uint4*>(in + e);
-      const __half2* h2 = reinterpret_cast<const __half2*>(&raw);
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        float2 f = __half22float2(h2[j]);
-        v[e + 2 * j] = f.x;
-        v[e + 2 * j + 1] = f.y;
-      }
+    for (int j = 0; j < J; ++j) {
+      const uint2 raw = *reinterpret_cast<const uint2*>(src + 128 * j);
+      const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
+      const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
+      v[j][0] = a.x;
+      v[j][1] = a.y;
+      v[j][2] = b.x;
+      v[j][3] = b.y;
     }
   } else {
-    const float* in = reinterpret_cast<const float*>(sg.in) + static_cast<long long>(local) * sg.ld + c0;
+    const float* src = reinterpret_cast<const float*>(in) + static_cast<long long>(local) * ld + base;
 #pragma unroll
-    for (int e = 0; e < EPT; e += 4) {
-      float4 f = *reinterpret_cast<const float4*>(in + e);
-      v[e] = f.x;
-      v[e + 1] = f.y;
-      v[e + 2] = f.z;
-      v[e + 3] = f.w;
+    for (int j = 0; j < J; ++j) {
+      const float4 f = *reinterpret_cast<const float4*>(src + 128 * j);
+      v[j][0] = f.x;
+      v[j][1] = f.y;
+      v[j][2] = f.z;
+      v[j][3] = f.w;
     }
   }
 
   if (SRC == kSrcLnMod) {
     float s = 0.0f;
 #pragma unroll
-    for (int e = 0; e < EPT; ++e) s += v[e];
-    const float mean = block_sum<NT>(s, red) / K;
+    for (int j = 0; j < J; ++j) s += (v[j][0] + v[j][1]) + (v[j][2] + v[j][3]);
+    s = warp_sum(s);
+    if (lane == 0) red[0][warp] = s;
+    __syncthreads();
+    float tot = 0.0f;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) tot += red[0][w];
+    const float mean = tot / K;
     float q = 0.0f;
 #pragma unroll
-    for (int e = 0; e < EPT; ++e) {
-      float d = v[e] - mean;
-      q += d * d;
-    }
-    const float inv_std = rsqrtf(block_sum<NT>(q, red) / K + eps);
+    for (int j = 0; j < J; ++j)
 #pragma unroll
-    for (int e = 0; e < EPT; e += 4) {
-      float4 sc = __ldg(reinterpret_cast<const float4*>(sg.scale + c0 + e));
-      float4 sh = __ldg(reinterpret_cast<const float4*>(sg.shift + c0 + e));
-      v[e + 0] = (v[e + 0] - mean) * inv_std * (1.0f + sc.x) + sh.x;
-      v[e + 1] = (v[e + 1] - mean) * inv_std * (1.0f + sc.y) + sh.y;
-      v[e + 2] = (v[e + 2] - mean) * inv_std * (1.0f + sc.z) + sh.z;
-      v[e + 3] = (v[e + 3] - mean) * inv_std * (1.0f + sc.w) + sh.w;
+      for (int e = 0; e < 4; ++e) {
+        const float d = v[j][e] - mean;
+        q += d * d;
+      }
+    q = warp_sum(q);
+    if (lane == 0) red[1][warp] = q;
+    __syncthreads();
+    float var = 0.0f;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) var += red[1][w];
+    const float inv_std = rsqrtf(var / K + eps);
+#pragma unroll
+    for (int j = 0; j < J; ++j) {
+      const float4 sc = __ldg(reinterpret_cast<const float4*>(scale + base + 128 * j));
+      const float4 sh = __ldg(reinterpret_cast<const float4*>(shift + base + 128 * j));
+      v[j][0] = (v[j][0] - mean) * inv_std * (1.0f + sc.x) + sh.x;
+      v[j][1] = (v[j][1] - mean) * inv_std * (1.0f + sc.y) + sh.y;
+      v[j][2] = (v[j][2] - mean) * inv_std * (1.0f + sc.z) + sh.z;
+      v[j][3] = (v[j][3] - mean) * inv_std * (1.0f + sc.w) + sh.w;
     }
   }
 
-  // Butterfly stages, lowest first.  Register stages:
+  // half = 1, 2: within the float4
+  if (had_block > 1) {
 #pragma unroll
-  for (int half = 1; half < EPT; half <<= 1) {
-    if (half >= had_block) break;
+    for (int j = 0; j < J; ++j) {
+      float a = v[j][0], b = v[j][1];
+      v[j][0] = a + b;
+      v[j][1] = a - b;
+      a = v[j][2];
+      b = v[j][3];
+      v[j][2] = a + b;
+      v[j][3] = a - b;
+    }
+  }
+  if (had_block > 2) {
 #pragma unroll
-    for (int e = 0; e < EPT; ++e) {
-      if ((e & half) == 0) {
-        float a = v[e], b = v[e + half];
-        v[e] = a + b;
-        v[e + half] = a - b;
+    for (int j = 0; j < J; ++j) {
+      float a = v[j][0], b = v[j][2];
+      v[j][0] = a + b;
+      v[j][2] = a - b;
+      a = v[j][1];
+      b = v[j][3];
+      v[j][1] = a + b;
+      v[j][3] = a - b;
+    }
+  }
+  // half = 4 .. 64: across lanes
+#pragma unroll
+  for (int m = 1; m < 32; m <<= 1) {
+    if (4 * m >= had_block) break;
+    const bool upper = (lane & m) != 0;
+#pragma unroll
+    for (int j = 0; j < J; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float p = __shfl_xor_sync(0xffffffffu, v[j][e], m);
+        v[j][e] = upper ? (p - v[j][e]) : (v[j][e] + p);
+      }
+  }
+  // half = 128 ..: across registers
+#pragma unroll
+  for (int jm = 1; jm < J; jm <<= 1) {
+    if (128 * jm >= had_block) break;
+#pragma unroll
+    for (int j = 0; j < J; ++j) {
+      if (j & jm) continue;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float a = v[j][e], b = v[j | jm][e];
+        v[j][e] = a + b;
+        v[j | jm][e] = a - b;
       }
     }
-  }
-  // Warp-shuffle stages (partner thread = t ^ (half / EPT)):
-#pragma unroll
-  for (int half = EPT; half < 32 * EPT; half <<= 1) {
-    if (half >= had_block) break;
-    const int m = half / EPT;
-    const bool upper = (t & m) != 0;
-#pragma unroll
-    for (int e = 0; e < EPT; ++e) {
-      float p = __shfl_xor_sync(0xffffffffu, v[e], m);
-      v[e] = upper ? (p - v[e]) : (v[e] + p);
-    }
-  }
-  // Shared-memory stages:
-  for (int half = 32 * EPT; half < had_block; half <<= 1) {
-#pragma unroll
-    for (int e = 0; e < EPT; e += 4)
-      *reinterpret_cast<float4*>(xs + c0 + e) = make_float4(v[e], v[e + 1], v[e + 2], v[e + 3]);
-    __syncthreads();
-    const bool upper = (c0 & half) != 0;
-    const int pc = c0 ^ half;
-#pragma unroll
-    for (int e = 0; e < EPT; e += 4) {
-      float4 p = *reinterpret_cast<const float4*>(xs + pc + e);
-      v[e + 0] = upper ? (p.x - v[e + 0]) : (v[e + 0] + p.x);
-      v[e + 1] = upper ? (p.y - v[e + 1]) : (v[e + 1] + p.y);
-      v[e + 2] = upper ? (p.z - v[e + 2]) : (v[e + 2] + p.z);
-      v[e + 3] = upper ? (p.w - v[e + 3]) : (v[e + 3] + p.w);
-    }
-    __syncthreads();
   }
 
   float mx = 0.0f;
   if (had_block > 1) {
     const float norm = rsqrtf(static_cast<float>(had_block));
 #pragma unroll
-    for (int e = 0; e < EPT; ++e) v[e] *= norm;
+    for (int j = 0; j < J; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) v[j][e] *= norm;
   }
 #pragma unroll
-  for (int e = 0; e < EPT; ++e) mx = fmaxf(mx, fabsf(v[e]));
-  mx = block_max<NT>(mx, red);
-  if (t == 0) scales[row] = mx / 127.0f;
+  for (int j = 0; j < J; ++j)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) mx = fmaxf(mx, fabsf(v[j][e]));
+  mx = warp_max(mx);
+  if (lane == 0) red[2][warp] = mx;
+  __syncthreads();
+  mx = red[2][0];
+#pragma unroll
+  for (int w = 1; w < NW; ++w) mx = fmaxf(mx, red[2][w]);
+  if (threadIdx.x == 0) scales[row] = mx / 127.0f;
   const float inv = (mx > 0.0f) ? 127.0f / mx : 0.0f;
-
-  int8_t q[EPT];
+  int8_t* dst = codes + static_cast<long long>(row) * K + base;
 #pragma unroll
-  for (int e = 0; e < EPT; ++e) {
-    int vi = __float2int_rn(v[e] * inv);
-    vi = max(-128, min(127, vi));
-    q[e] = static_cast<int8_t>(vi);
-  }
-  int8_t* dst = codes + static_cast<long long>(row) * K + c0;
-  if (EPT == 8) {
-    *reinterpret_cast<uint2*>(dst) = *reinterpret_cast<const uint2*>(q);
-  } else {
-#pragma unroll
-    for (int e = 0; e < EPT; e += 16) *reinterpret_cast<uint4*>(dst + e) = *reinterpret_cast<const uint4*>(q + e);
+  for (int j = 0; j < J; ++j) {
+    char4 q;
+    int t0 = __float2int_rn(v[j][0] * inv), t1 = __float2int_rn(v[j][1] * inv);
+    int t2 = __float2int_rn(v[j][2] * inv), t3 = __float2int_rn(v[j][3] * inv);
+    q.x = static_cast<signed char>(max(-128, min(127, t0)));
+    q.y = static_cast<signed char>(max(-128, min(127, t1)));
+    q.z = static_cast<signed char>(max(-128, min(127, t2)));
+    q.w = static_cast<signed char>(max(-128, min(127, t3)));
+    *reinterpret_cast<char4*>(dst + 128 * j) = q;
   }
 }
 
@@ -264,18 +278,11 @@ __global__ void fwht_quant_generic_kernel(const void* __restrict__ in, int in_bf
   }
 }
 
-template <int K, int EPT, int SRC>
-int launch_fused(const RowSegs& segs, int rows, int had_block, int8_t* codes, float* scales, float eps,
-                 cudaStream_t stream) {
-  const int smem = (K + 32) * static_cast<int>(sizeof(float));
-  static bool attr = false;
-  if (!attr) {
-    if (cudaFuncSetAttribute(rowquant_fused_kernel<K, EPT, SRC>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
-        cudaSuccess)
-      return QI_ERR_CUDA;
-    attr = true;
-  }
-  rowquant_fused_kernel<K, EPT, SRC><<<rows, K / EPT, smem, stream>>>(segs, had_block, codes, scales, eps);
+template <int K, int NW, int SRC>
+int launch_warp(const RowSegs& segs, int rows, int had_block, int8_t* codes, float* scales, float eps,
+                cudaStream_t stream) {
+  if (had_block > K / NW) return QI_ERR_UNSUPPORTED;
+  rowquant_warp_kernel<K, NW, SRC><<<rows, NW * 32, 0, stream>>>(segs, had_block, codes, scales, eps);
   return cudaGetLastError() == cudaSuccess ? QI_OK : QI_ERR_CUDA;
 }
 
@@ -293,17 +300,19 @@ int rowquant_launch(int src, int K, int had_block, const RowSeg* segs, int nseg,
     rows += segs[i].rows;
     if (reinterpret_cast<uintptr_t>(segs[i].in) & 15) return QI_ERR_ALIGN;
     if (segs[i].ld % 8) return QI_ERR_ALIGN;
+    if (src == kSrcLnMod && ((reinterpret_cast<uintptr_t>(segs[i].shift) & 15) || (reinterpret_cast<uintptr_t>(segs[i].scale) & 15)))
+      return QI_ERR_ALIGN;
     if (src == kSrcLnMod && (!segs[i].shift || !segs[i].scale)) return QI_ERR_ARG;
   }
   s.nseg = nseg;
   if (rows == 0) return QI_OK;
-  if (K == 3072 && src == kSrcF32) return launch_fused<3072, 8, kSrcF32>(s, rows, had_block, codes, scales, eps, stream);
-  if (K == 3072 && src == kSrcF16) return launch_fused<3072, 8, kSrcF16>(s, rows, had_block, codes, scales, eps, stream);
+  if (K == 3072 && src == kSrcF32) return launch_warp<3072, 3, kSrcF32>(s, rows, had_block, codes, scales, eps, stream);
+  if (K == 3072 && src == kSrcF16) return launch_warp<3072, 3, kSrcF16>(s, rows, had_block, codes, scales, eps, stream);
   if (K == 3072 && src == kSrcLnMod)
-    return launch_fused<3072, 8, kSrcLnMod>(s, rows, had_block, codes, scales, eps, stream);
+    return launch_warp<3072, 3, kSrcLnMod>(s, rows, had_block, codes, scales, eps, stream);
   if (K == 12288 && src == kSrcF32)
-    return launch_fused<12288, 16, kSrcF32>(s, rows, had_block, codes, scales, eps, stream);
-  if (K == 256 && src == kSrcF32) return launch_fused<256, 8, kSrcF32>(s, rows, had_block, codes, scales, eps, stream);
+    return launch_warp<12288, 3, kSrcF32>(s, rows, had_block, codes, scales, eps, stream);
+  if (K == 256 && src == kSrcF32) return launch_warp<256, 1, kSrcF32>(s, rows, had_block, codes, scales, eps, stream);
   return QI_ERR_UNSUPPORTED;
 }
 

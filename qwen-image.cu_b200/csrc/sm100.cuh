@@ -29,6 +29,7 @@ enum DeviceError : int {
   kErrTimeoutMma = 2,
   kErrTimeoutEpilogue = 3,
   kErrTimeoutSoftmax = 4,
+  kErrTimeoutSelftest = 5,
 };
 
 // A bounded wait gives up after this many nanoseconds of %globaltimer.  One
@@ -72,14 +73,17 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // Waits for the phase with the given parity to complete.  Returns false when
 // the wait gives up (time limit) or when another role has raised *abort; the
 // caller then leaves its loop and the kernel tears down normally.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
+__device__ __forceinline__ bool mbar_wait_limit(uint64_t* bar, uint32_t parity, volatile int* abort, uint64_t limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   uint64_t t0 = global_timer_ns();
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
     if (*abort) return false;
-    if (global_timer_ns() - t0 > kWaitLimitNs) return false;
+    if (global_timer_ns() - t0 > limit_ns) return false;
   }
+}
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
+  return mbar_wait_limit(bar, parity, abort, kWaitLimitNs);
 }
 
 // ---------------------------------------------------------------- TMA
@@ -99,6 +103,24 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* tm, in
           smem_u32(dst)),
       "l"(reinterpret_cast<uint64_t>(tm)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
       : "memory");
+}
+
+// TMA tile store shared -> global (bulk-group completion) and its waits.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* tm, const void* src, int c0, int c1) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(tm)),
+               "r"(smem_u32(src)), "r"(c0), "r"(c1)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Waits until at most N committed bulk groups still read their shared source.
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+template <int N>
+__device__ __forceinline__ void bulk_wait() {
+  asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
 }
 
 // Makes generic-proxy shared-memory writes visible to the async proxy (the

@@ -92,6 +92,7 @@ def lib():
             "qi_forward_blocks": ([vp, vp, i, i, i, vp, vp, f, vp, i, i, vp], i),
             "qi_cfg_euler_step": ([vp, vp, vp, f, f, f, i, i, vp, vp], i),
             "qi_ctx_set_profiling": ([vp, i], i),
+            "qi_selftest_wait_timeout": ([vp, i, vp], i),
             "qi_ctx_profile": ([vp, vp, vp, i], i),
             "qi_rope_table": ([i, i, i, vp], i),
             "qi_synth_fill": ([vp, ll, ull, f, f, i, vp], i),
