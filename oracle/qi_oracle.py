@@ -363,6 +363,64 @@ def unpatchify(p, nb, H, Wd):
     return t.reshape(nb, OUT_CH, H, Wd)
 
 
+def block(W, img, txt, mi, mt, pe, mode="quant", bi=0, rec=None):
+    """One double-stream block (transformer.cu:497-836) on FP32 residual
+    streams img [n_img,3072], txt [n_txt,3072] with modulation vectors mi, mt
+    ([18432] each, chunks [shift1, scale1, gate1, shift2, scale2, gate2]).
+    Returns the updated (img, txt); `rec` receives the block's stage values."""
+    rec = rec if rec is not None else {}
+    pre = f"transformer_blocks.{bi}."
+    n_img, n_txt = img.shape[0], txt.shape[0]
+    S = n_img + n_txt
+    pos_img = np.arange(n_txt, S, dtype=np.int32)
+    pos_txt = np.arange(0, n_txt, dtype=np.int32)
+    scale = np.float32(1.0 / np.sqrt(128.0))
+    ch = lambda m, k: m[k * DIM:(k + 1) * DIM]
+    img_n = layernorm_modulate(img, ch(mi, 0), ch(mi, 1))
+    txt_n = layernorm_modulate(txt, ch(mt, 0), ch(mt, 1))
+    rec["img_modulated"] = img_n.copy()
+    aq_i = fwht_quant(img_n, 1024) if mode == "quant" else None
+    aq_t = fwht_quant(txt_n, 1024) if mode == "quant" else None
+    qi_ = _linear(W, pre + "attn.to_q", DIM, DIM, img_n, mode, act_q=aq_i)
+    ki_ = _linear(W, pre + "attn.to_k", DIM, DIM, img_n, mode, act_q=aq_i)
+    vi_ = _linear(W, pre + "attn.to_v", DIM, DIM, img_n, mode, act_q=aq_i)
+    qt_ = _linear(W, pre + "attn.add_q_proj", DIM, DIM, txt_n, mode, act_q=aq_t)
+    kt_ = _linear(W, pre + "attn.add_k_proj", DIM, DIM, txt_n, mode, act_q=aq_t)
+    vt_ = _linear(W, pre + "attn.add_v_proj", DIM, DIM, txt_n, mode, act_q=aq_t)
+    nq = W.bf16(pre + "attn.norm_q.weight", (128,), 1.0)
+    nk = W.bf16(pre + "attn.norm_k.weight", (128,), 1.0)
+    naq = W.bf16(pre + "attn.norm_added_q.weight", (128,), 1.0)
+    nak = W.bf16(pre + "attn.norm_added_k.weight", (128,), 1.0)
+    qi_ = rmsnorm(qi_.reshape(-1, 128), nq).reshape(n_img, HEADS, 128)
+    ki_ = rmsnorm(ki_.reshape(-1, 128), nk).reshape(n_img, HEADS, 128)
+    qt_ = rmsnorm(qt_.reshape(-1, 128), naq).reshape(n_txt, HEADS, 128)
+    kt_ = rmsnorm(kt_.reshape(-1, 128), nak).reshape(n_txt, HEADS, 128)
+    rec["img_q_normed"] = qi_.reshape(n_img, DIM).copy()
+    q = np.concatenate([rope_apply(qt_, pe, pos_txt), rope_apply(qi_, pe, pos_img)], 0)
+    k = np.concatenate([rope_apply(kt_, pe, pos_txt), rope_apply(ki_, pe, pos_img)], 0)
+    v = np.concatenate([vt_.reshape(n_txt, HEADS, 128), vi_.reshape(n_img, HEADS, 128)], 0)
+    qh, kh, vh = (a.transpose(1, 0, 2).copy() for a in (q, k, v))  # [H, S, 128]
+    if mode == "quant":
+        o = sage_attention(f32_to_f16(qh).astype(np.float32), f32_to_f16(kh).astype(np.float32),
+                           f32_to_f16(vh).astype(np.float32), scale)
+    else:
+        o = attention_exact(qh, kh, vh, scale)
+    o = o.transpose(1, 0, 2).reshape(S, DIM)
+    o_txt, o_img = o[:n_txt], o[n_txt:]
+    rec["attn_out_img"], rec["attn_out_txt"] = o_img.copy(), o_txt.copy()
+    img = img + ch(mi, 2)[None, :] * _linear(W, pre + "attn.to_out.0", DIM, DIM, o_img, mode)
+    txt = txt + ch(mt, 2)[None, :] * _linear(W, pre + "attn.to_add_out", DIM, DIM, o_txt, mode)
+    rec["img_after_attn"] = img.copy()
+    img_n = layernorm_modulate(img, ch(mi, 3), ch(mi, 4))
+    txt_n = layernorm_modulate(txt, ch(mt, 3), ch(mt, 4))
+    hi = _linear(W, pre + "img_mlp.net.0.proj", MLP, DIM, img_n, mode, gelu=True)
+    ht = _linear(W, pre + "txt_mlp.net.0.proj", MLP, DIM, txt_n, mode, gelu=True)
+    img = img + ch(mi, 5)[None, :] * _linear(W, pre + "img_mlp.net.2", DIM, MLP, hi, mode)
+    txt = txt + ch(mt, 5)[None, :] * _linear(W, pre + "txt_mlp.net.2", DIM, MLP, ht, mode)
+    rec["img_after_mlp"], rec["txt_after_mlp"] = img.copy(), txt.copy()
+    return img.astype(np.float32), txt.astype(np.float32)
+
+
 def forward(W, x_u16, t, txt_u16, pe, mode="quant", num_blocks=None, record=None):
     """One transformer_forward for a single batch element.
 
@@ -390,65 +448,13 @@ def forward(W, x_u16, t, txt_u16, pe, mode="quant", num_blocks=None, record=None
     tn = round_bf16(rmsnorm(ctx, W.bf16("txt_norm.weight", (TXT_DIM,), 1.0)))
     txt = _linear_bf16w(W, "txt_in", DIM, TXT_DIM, tn)
     rec["txt_after_proj"] = txt.copy()
-    pos_img = np.arange(n_txt, S, dtype=np.int32)
-    pos_txt = np.arange(0, n_txt, dtype=np.int32)
-    scale = np.float32(1.0 / np.sqrt(128.0))
     for bi in range(L):
         pre = f"transformer_blocks.{bi % W.num_blocks}."
         mi = _linear(W, pre + "img_mod.1", 6 * DIM, DIM, tsilu, mode)[0]
         mt = _linear(W, pre + "txt_mod.1", 6 * DIM, DIM, tsilu, mode)[0]
         if bi == 0:
             rec["img_mods"], rec["txt_mods"] = mi.copy(), mt.copy()
-        ch = lambda m, k: m[k * DIM:(k + 1) * DIM]
-        img_n = layernorm_modulate(img, ch(mi, 0), ch(mi, 1))
-        txt_n = layernorm_modulate(txt, ch(mt, 0), ch(mt, 1))
-        if bi == 0:
-            rec["img_modulated"] = img_n.copy()
-        aq_i = fwht_quant(img_n, 1024) if mode == "quant" else None
-        aq_t = fwht_quant(txt_n, 1024) if mode == "quant" else None
-        qi_ = _linear(W, pre + "attn.to_q", DIM, DIM, img_n, mode, act_q=aq_i)
-        ki_ = _linear(W, pre + "attn.to_k", DIM, DIM, img_n, mode, act_q=aq_i)
-        vi_ = _linear(W, pre + "attn.to_v", DIM, DIM, img_n, mode, act_q=aq_i)
-        qt_ = _linear(W, pre + "attn.add_q_proj", DIM, DIM, txt_n, mode, act_q=aq_t)
-        kt_ = _linear(W, pre + "attn.add_k_proj", DIM, DIM, txt_n, mode, act_q=aq_t)
-        vt_ = _linear(W, pre + "attn.add_v_proj", DIM, DIM, txt_n, mode, act_q=aq_t)
-        nq = W.bf16(pre + "attn.norm_q.weight", (128,), 1.0)
-        nk = W.bf16(pre + "attn.norm_k.weight", (128,), 1.0)
-        naq = W.bf16(pre + "attn.norm_added_q.weight", (128,), 1.0)
-        nak = W.bf16(pre + "attn.norm_added_k.weight", (128,), 1.0)
-        qi_ = rmsnorm(qi_.reshape(-1, 128), nq).reshape(n_img, HEADS, 128)
-        ki_ = rmsnorm(ki_.reshape(-1, 128), nk).reshape(n_img, HEADS, 128)
-        qt_ = rmsnorm(qt_.reshape(-1, 128), naq).reshape(n_txt, HEADS, 128)
-        kt_ = rmsnorm(kt_.reshape(-1, 128), nak).reshape(n_txt, HEADS, 128)
-        if bi == 0:
-            rec["img_q_normed"] = qi_.reshape(n_img, DIM).copy()
-        q = np.concatenate([rope_apply(qt_, pe, pos_txt), rope_apply(qi_, pe, pos_img)], 0)
-        k = np.concatenate([rope_apply(kt_, pe, pos_txt), rope_apply(ki_, pe, pos_img)], 0)
-        v = np.concatenate([vt_.reshape(n_txt, HEADS, 128), vi_.reshape(n_img, HEADS, 128)], 0)
-        qh, kh, vh = (a.transpose(1, 0, 2).copy() for a in (q, k, v))  # [H, S, 128]
-        if mode == "quant":
-            o = sage_attention(f32_to_f16(qh).astype(np.float32), f32_to_f16(kh).astype(np.float32),
-                               f32_to_f16(vh).astype(np.float32), scale)
-        else:
-            o = attention_exact(qh, kh, vh, scale)
-        o = o.transpose(1, 0, 2).reshape(S, DIM)
-        o_txt, o_img = o[:n_txt], o[n_txt:]
-        if bi == 0:
-            rec["attn_out_img"], rec["attn_out_txt"] = o_img.copy(), o_txt.copy()
-        img = img + ch(mi, 2)[None, :] * _linear(W, pre + "attn.to_out.0", DIM, DIM, o_img, mode)
-        txt = txt + ch(mt, 2)[None, :] * _linear(W, pre + "attn.to_add_out", DIM, DIM, o_txt, mode)
-        if bi == 0:
-            rec["img_after_attn"] = img.copy()
-        img_n = layernorm_modulate(img, ch(mi, 3), ch(mi, 4))
-        txt_n = layernorm_modulate(txt, ch(mt, 3), ch(mt, 4))
-        hi = _linear(W, pre + "img_mlp.net.0.proj", MLP, DIM, img_n, mode, gelu=True)
-        ht = _linear(W, pre + "txt_mlp.net.0.proj", MLP, DIM, txt_n, mode, gelu=True)
-        img = img + ch(mi, 5)[None, :] * _linear(W, pre + "img_mlp.net.2", DIM, MLP, hi, mode)
-        txt = txt + ch(mt, 5)[None, :] * _linear(W, pre + "txt_mlp.net.2", DIM, MLP, ht, mode)
-        if bi == 0:
-            rec["img_after_mlp"], rec["txt_after_mlp"] = img.copy(), txt.copy()
-        img = img.astype(np.float32)
-        txt = txt.astype(np.float32)
+        img, txt = block(W, img, txt, mi, mt, pe, mode, bi % W.num_blocks, rec if bi == 0 else None)
     rec["img_final"] = img.copy()
     # output AdaLN (transformer.cu:873-926)
     ada = _linear_bf16w(W, "norm_out.linear", 2 * DIM, DIM, round_bf16(tsilu))[0]

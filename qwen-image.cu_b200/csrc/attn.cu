@@ -12,9 +12,12 @@
 //     * sm_scale * log2(e);
 //   * online softmax in base 2 (ex2.approx, m initialised to -5e6, the
 //     reference's update_mdo, sageattention_attn_utils.cuh:352-456);
-//   * P is rounded to FP16 and the row sum is accumulated from the rounded
-//     values; O += P.V runs as tcgen05.mma.kind::f16 with FP32 accumulation in
-//     TMEM; the running output is rescaled in TMEM when the row max grows;
+//   * P is rounded to FP16; O += P.V runs as tcgen05.mma.kind::f16 with FP32
+//     accumulation in TMEM; the row sum is accumulated in FP32; the running
+//     max used for P moves only when the row max grows by more than 2^8 (then
+//     O is rescaled in TMEM), which leaves O / l unchanged in exact arithmetic;
+//   * half of the exponentials run on MUFU (ex2.approx), half as a degree-3
+//     polynomial on the FMA pipe, so the softmax is not MUFU-bound;
 //   * the result is O * rcp(l) rounded to FP16 (normalize_d, :719-760).
 //
 // Tiling: one CTA per (128 queries, batch-head); keys in blocks of 128 (two
@@ -60,6 +63,23 @@ __device__ __forceinline__ float ex2_approx(float x) {
   asm volatile("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
+// 2^x for x <= 0 on the FMA/ALU pipes (half of the softmax exponentials go
+// here, half to MUFU ex2, so neither pipe limits the softmax): x = n + f with
+// n = round(x), |f| <= 1/2; 2^f by a degree-3 polynomial fitted on [-1/2, 1/2]
+// (max relative error 7.5e-5, under FP16's 4.9e-4 half ulp); 2^n is added to
+// the exponent field.  x is clamped at -125 so the exponent cannot underflow
+// (2^-125 rounds to zero in FP16 anyway).
+__device__ __forceinline__ float exp2_poly(float x) {
+  x = fmaxf(x, -125.0f);
+  const float t = __fadd_rn(x, 12582912.0f);  // 1.5 * 2^23: rounds x to an integer in the low mantissa bits
+  const float n = __fadd_rn(t, -12582912.0f);
+  const float f = __fadd_rn(x, -n);
+  float p = fmaf(0x1.c3f73ep-5f, f, 0x1.f0de18p-3f);
+  p = fmaf(p, f, 0x1.62f31ap-1f);
+  p = fmaf(p, f, 0x1.fff692p-1f);
+  return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
+}
+
 __device__ __forceinline__ float rcp_approx(float x) {
   float y;
   asm volatile("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -219,83 +239,101 @@ __global__ void __launch_bounds__(attn::THREADS, 1) sage_attn_kernel(const __gri
       bool w = mbar_wait(&s_full[sb], (j >> 1) & 1, abort_flag);
       if (!__all_sync(0xffffffffu, w)) { ok = false; break; }
       tc_fence_after();
-      // column factors: k_scale[(2j + c/64)*4 + (c%8)/2] * q_scale * sm_scale * log2e
-      float kf[8];
+      // column factors: k_scale[(2j + c/64)*4 + (c%8)/2] * q_scale * sm_scale * log2e,
+      // and their products with -1.5*2^23 for the exact int->float conversion below
+      float kf[8], kb[8];
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         const int kb64 = 2 * j + h;
 #pragma unroll
-        for (int g = 0; g < 4; ++g)
-          kf[h * 4 + g] = (kb64 * 64 < S) ? args.ks[static_cast<size_t>(bh) * args.ngk + kb64 * 4 + g] * qsm : 0.0f;
-      }
-      float s[BKV];
-      const uint32_t s_addr = tmem + lane_off + (sb ? TM_S1 : TM_S0);
-#pragma unroll
-      for (int c = 0; c < BKV; c += 32) {
-        uint32_t r[32];
-        tmem_ld32(s_addr + c, r);
-        tmem_ld_wait();
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int col = c + i;
-          s[col] = static_cast<float>(static_cast<int32_t>(r[i])) * kf[(col >> 6) * 4 + ((col & 7) >> 1)];
+        for (int g = 0; g < 4; ++g) {
+          const float f = (kb64 * 64 < S) ? args.ks[static_cast<size_t>(bh) * args.ngk + kb64 * 4 + g] * qsm : 0.0f;
+          kf[h * 4 + g] = f;
+          kb[h * 4 + g] = -12582912.0f * f;
         }
       }
+      // all four 32-column loads in flight, one wait
+      uint32_t r[BKV];
+      const uint32_t s_addr = tmem + lane_off + (sb ? TM_S1 : TM_S0);
+      tmem_ld32(s_addr + 0, *reinterpret_cast<uint32_t(*)[32]>(r + 0));
+      tmem_ld32(s_addr + 32, *reinterpret_cast<uint32_t(*)[32]>(r + 32));
+      tmem_ld32(s_addr + 64, *reinterpret_cast<uint32_t(*)[32]>(r + 64));
+      tmem_ld32(s_addr + 96, *reinterpret_cast<uint32_t(*)[32]>(r + 96));
+      tmem_ld_wait();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&s_free[sb]);
+      // |acc| <= 128^3 < 2^22: float bits (acc + 0x4B400000) are exactly 1.5*2^23 + acc,
+      // so s = (1.5*2^23 + acc) * kf - 1.5*2^23 * kf, one integer add and one FMA.
+      float sv[BKV];
+#pragma unroll
+      for (int i = 0; i < BKV; ++i) {
+        const int g = (i >> 6) * 4 + ((i & 7) >> 1);
+        sv[i] = fmaf(__int_as_float(static_cast<int>(r[i]) + 0x4B400000), kf[g], kb[g]);
+      }
       if (j == nkb - 1 && (j + 1) * BKV > S) {
 #pragma unroll
         for (int i = 0; i < BKV; ++i)
-          if (j * BKV + i >= S) s[i] = -5000000.0f;
+          if (j * BKV + i >= S) sv[i] = -5000000.0f;
       }
-      float mloc = s[0];
+      float mp[8];
 #pragma unroll
-      for (int i = 1; i < BKV; ++i) mloc = fmaxf(mloc, s[i]);
+      for (int u = 0; u < 8; ++u) mp[u] = sv[u];
+#pragma unroll
+      for (int i = 8; i < BKV; ++i) mp[i & 7] = fmaxf(mp[i & 7], sv[i]);
+      const float mloc = fmaxf(fmaxf(fmaxf(mp[0], mp[1]), fmaxf(mp[2], mp[3])),
+                               fmaxf(fmaxf(mp[4], mp[5]), fmaxf(mp[6], mp[7])));
+      // Lazy rescale: the running max used for P only moves when the row max
+      // grows by more than 8 (P stays <= 2^8, exact in FP16 range); O and l are
+      // rescaled with it, so O / l is unchanged in exact arithmetic.
       const float m_new = fmaxf(m, mloc);
-      const float alpha = ex2_approx(m - m_new);
+      const bool grow = m_new > m + 8.0f;
+      const float alpha = grow ? ex2_approx(m - m_new) : 1.0f;
+      const float m_use = grow ? m_new : m;
       if (j > 0) {
         w = mbar_wait(o_done, (j - 1) & 1, abort_flag);
         if (!__all_sync(0xffffffffu, w)) { ok = false; break; }
         tc_fence_after();
-        if (__any_sync(0xffffffffu, alpha != 1.0f)) {
+        if (__any_sync(0xffffffffu, grow)) {
 #pragma unroll 1
           for (int c = 0; c < D; c += 32) {
-            uint32_t r[32];
-            tmem_ld32(tmem + lane_off + TM_O + c, r);
+            uint32_t o[32];
+            tmem_ld32(tmem + lane_off + TM_O + c, o);
             tmem_ld_wait();
 #pragma unroll
-            for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
-            tmem_st32(tmem + lane_off + TM_O + c, r);
+            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+            tmem_st32(tmem + lane_off + TM_O + c, o);
           }
           tmem_st_wait();
         }
       }
-      l *= alpha;
-      // P = exp2(s - m_new) -> FP16, row sum from the rounded values, store
-      // into the K-major 128-byte-swizzled A-operand tile.
+      // P = exp2(s - m_use) (even columns on MUFU, odd ones by polynomial) ->
+      // FP16 into the K-major 128-byte-swizzled A-operand tile; the row sum
+      // accumulates in 8 partial sums.
+      float lp[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
       uint8_t* prow = sP + row * 128;
 #pragma unroll
       for (int c = 0; c < BKV / 8; ++c) {
         uint32_t pk[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          const float p0 = ex2_approx(s[c * 8 + 2 * e] - m_new);
-          const float p1 = ex2_approx(s[c * 8 + 2 * e + 1] - m_new);
+          const float p0 = ex2_approx(sv[c * 8 + 2 * e] - m_use);
+          const float p1 = exp2_poly(sv[c * 8 + 2 * e + 1] - m_use);
+          lp[(2 * e) & 7] += p0;
+          lp[(2 * e + 1) & 7] += p1;
           __half2 h2 = __floats2half2_rn(p0, p1);
-          const float2 back = __half22float2(h2);
-          l += back.x + back.y;
           pk[e] = *reinterpret_cast<uint32_t*>(&h2);
         }
         const int region = c >> 3, cc = c & 7;
         uint8_t* dst = prow + region * (P_BYTES / 2) + ((cc ^ (row & 7)) << 4);
         *reinterpret_cast<uint4*>(dst) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
       }
+      l = l * alpha + (((lp[0] + lp[1]) + (lp[2] + lp[3])) + ((lp[4] + lp[5]) + (lp[6] + lp[7])));
       fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(p_full);
-      m = m_new;
+      m = m_use;
     }
     if (ok) {
       bool w = mbar_wait(o_done, (nkb - 1) & 1, abort_flag);

@@ -33,7 +33,13 @@ ACT_CASES = [(8, 3072, 1024), (4, 12288, 4096), (3, 256, 256), (5, 3584, 512)]
 W_CASES = [(16, 3072), (8, 12288), (16, 256), (4, 64), (4, 3584)]
 SAGE_CASES = [(2, 200), (1, 77), (2, 384)]
 ROPE_CASES = [(8, 8, 8), (128, 128, 256), (166, 166, 256), (256, 256, 512), (7, 9, 5), (64, 64, 64)]
-TINY = dict(H=8, W=8, n_txt=8, t=500.0)
+# Block-0 dumps at 64x64 latent / 64 text tokens (S = 1088).  At sequences shorter than one
+# 64-key block (e.g. 8x8 latent, 8 text tokens: S = 24) the reference's sm80 Sage kernel
+# returns NaN (masked keys multiply stale shared memory), so tiny sizes cannot pin anything
+# past attention.  Only a fixed subsample of rows is stored.
+TINY = dict(H=64, W=64, n_txt=64, t=500.0)
+ROWS_IMG = [0, 1, 63, 64, 127, 200, 333, 511, 512, 700, 777, 901, 1000, 1022, 1023, 640]
+ROWS_TXT = [0, 1, 7, 8, 31, 32, 62, 63]
 
 
 def act_input(M, K, seed):
@@ -111,6 +117,17 @@ def main(out):
               "b0_img_modulated", "b0_img_q_normed", "b0_attn_out_img", "b0_attn_out_txt",
               "b0_img_after_attn", "b0_img_after_mlp", "b0_txt_after_mlp"}
     d = {k: v for k, v in d.items() if k in wanted}
+    n_img = (H // 2) * (W // 2)
+    for k in list(d):
+        a = d[k]
+        if k == "out":
+            continue
+        if a.size == n_img * 3072:
+            d[k] = a.reshape(n_img, 3072)[ROWS_IMG]
+        elif a.size == n_txt * 3072:
+            d[k] = a.reshape(n_txt, 3072)[ROWS_TXT]
+    d["rows_img"] = np.array(ROWS_IMG)
+    d["rows_txt"] = np.array(ROWS_TXT)
     np.savez_compressed(os.path.join(out, "block0.npz"), **d)
     print("wrote", sorted(os.listdir(out)))
 

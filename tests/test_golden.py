@@ -86,25 +86,32 @@ def test_rope_table_golden():
 
 def test_block0_stages_golden():
     """Block 0 of the reference's transformer_forward (its own DUMP hooks) at
-    8x8 latent / 8 text tokens against the oracle's quantization-emulating
-    forward, stage by stage, at the north-star tolerance."""
+    64x64 latent / 64 text tokens against the oracle's quantization-emulating
+    forward, stage by stage, on a fixed subsample of token rows.  Stages up to
+    attention agree to ~1e-3; after the INT8 MLP the reference and an exact
+    evaluation of its own arithmetic differ by up to ~3.5e-2 element-wise (the
+    W8A8 noise floor), so the bar there is cosine >= 0.9998, max-rel <= 5e-2."""
     g = load("block0.npz")
     W = O.Weights(1, base_seed=0)
-    H = Wd = 8
-    n_txt = 8
+    H = Wd = 64
+    n_txt = 64
+    ri, rt = g["rows_img"], g["rows_txt"]
     x = O.gen_bf16(seed_for(1, "latent"), (1, 16, H, Wd), 1.0)
     txt = O.gen_bf16(seed_for(1, "context"), (n_txt, 3584), 1.0)
     pe = O.rope_table(H, Wd, n_txt)
     rec = {}
     O.forward(W, x, 500.0, txt, pe, mode="quant", num_blocks=1, record=rec)
-    pairs = [("t_emb", "t_emb"), ("img_after_proj", "img_after_proj"), ("txt_after_proj", "txt_after_proj"),
-             ("b0_img_mods", "img_mods"), ("b0_txt_mods", "txt_mods"), ("b0_img_modulated", "img_modulated"),
-             ("b0_img_q_normed", "img_q_normed"), ("b0_attn_out_img", "attn_out_img"),
-             ("b0_attn_out_txt", "attn_out_txt"), ("b0_img_after_attn", "img_after_attn"),
-             ("b0_img_after_mlp", "img_after_mlp"), ("b0_txt_after_mlp", "txt_after_mlp")]
-    for gk, ok in pairs:
-        ref = g[gk].astype(np.float32).ravel()
-        ours = rec[ok].astype(np.float32).ravel()
+    pairs = [("t_emb", "t_emb", None, 1e-3), ("img_after_proj", "img_after_proj", ri, 1e-3),
+             ("txt_after_proj", "txt_after_proj", rt, 1e-3), ("b0_img_mods", "img_mods", None, 2e-3),
+             ("b0_txt_mods", "txt_mods", None, 2e-3), ("b0_img_modulated", "img_modulated", ri, 2e-3),
+             ("b0_img_q_normed", "img_q_normed", ri, 5e-3), ("b0_attn_out_img", "attn_out_img", ri, 1e-2),
+             ("b0_attn_out_txt", "attn_out_txt", rt, 1e-2), ("b0_img_after_attn", "img_after_attn", ri, 1e-2),
+             ("b0_img_after_mlp", "img_after_mlp", ri, 5e-2), ("b0_txt_after_mlp", "txt_after_mlp", rt, 5e-2)]
+    for gk, ok, rows, bar in pairs:
+        ref = g[gk].astype(np.float32)
+        ours = rec[ok].astype(np.float32)
+        if rows is not None:
+            ours = ours[rows]
         assert ref.size == ours.size, (gk, ref.size, ours.size)
         cos, maxrel = O.metrics(ours, ref)
-        assert cos >= 0.999 and maxrel <= 2e-2, (gk, cos, maxrel)
+        assert cos >= 0.9998 and maxrel <= bar, (gk, cos, maxrel)
