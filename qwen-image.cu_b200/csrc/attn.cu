@@ -16,8 +16,8 @@
 //     accumulation in TMEM; the row sum is accumulated in FP32; the running
 //     max used for P moves only when the row max grows by more than 2^8 (then
 //     O is rescaled in TMEM), which leaves O / l unchanged in exact arithmetic;
-//   * half of the exponentials run on MUFU (ex2.approx), half as a degree-3
-//     polynomial on the FMA pipe, so the softmax is not MUFU-bound;
+//   * one exponential in eight runs as a degree-3 polynomial on the FMA pipe,
+//     the rest on MUFU (ex2.approx), which balances MUFU against issue slots;
 //   * the result is O * rcp(l) rounded to FP16 (normalize_d, :719-760).
 //
 // Tiling: one CTA per (128 queries, batch-head); keys in blocks of 128 (two
@@ -25,9 +25,14 @@
 // a two-stage ring), warp 1 issues the MMAs (QK^T of block j+1 is issued
 // before P.V of block j so the tensor core works while softmax runs), warps
 // 2-5 own one query row per thread (TMEM lane = row).
-// TMEM: S double buffer (2 x 128 columns) + O (128 columns).
+// TMEM: S double buffer (2 x 128 columns) + O (128 columns).  P is double
+// buffered in shared memory, so the softmax of block j overlaps P.V of block
+// j-1 and only waits for it when O has to be rescaled.
 #include "qi_internal.h"
 #include "sm100.cuh"
+
+#include <climits>
+#include <type_traits>
 
 namespace qi {
 
@@ -41,7 +46,7 @@ constexpr int OFF_Q = 0;
 constexpr int OFF_K = OFF_Q + Q_BYTES;
 constexpr int OFF_V = OFF_K + 2 * K_BYTES;
 constexpr int OFF_P = OFF_V + 2 * V_BYTES;
-constexpr int OFF_BAR = OFF_P + P_BYTES;
+constexpr int OFF_BAR = OFF_P + 2 * P_BYTES;
 constexpr int SMEM_BYTES = OFF_BAR + 256 + 1024;
 constexpr int THREADS = 192;
 constexpr int TMEM_COLS = 512;
@@ -102,10 +107,10 @@ __global__ void __launch_bounds__(attn::THREADS, 1) sage_attn_kernel(const __gri
   uint64_t* v_empty = bars + 7;  // [2]
   uint64_t* s_full = bars + 9;   // [2]
   uint64_t* s_free = bars + 11;  // [2]
-  uint64_t* p_full = bars + 13;
-  uint64_t* o_done = bars + 14;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 17);
+  uint64_t* p_full = bars + 13;  // [2] P buffer j&1 written
+  uint64_t* o_done = bars + 15;  // [2] P.V of block j (reading P buffer j&1) complete
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 17);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 18);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int q0 = blockIdx.x * BQ;
@@ -123,8 +128,10 @@ __global__ void __launch_bounds__(attn::THREADS, 1) sage_attn_kernel(const __gri
       mbar_init(&s_full[i], 1);
       mbar_init(&s_free[i], 4);
     }
-    mbar_init(p_full, 4);
-    mbar_init(o_done, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&p_full[i], 4);
+      mbar_init(&o_done[i], 1);
+    }
     *abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&args.tmQ);
@@ -204,18 +211,18 @@ __global__ void __launch_bounds__(attn::THREADS, 1) sage_attn_kernel(const __gri
         if (j >= 1) {
           const int jj = j - 1;
           const int st = jj & 1;
-          if (!mbar_wait(p_full, jj & 1, abort_flag)) { ok = false; break; }
+          if (!mbar_wait(&p_full[st], (jj >> 1) & 1, abort_flag)) { ok = false; break; }
           if (!mbar_wait(&v_full[st], (jj >> 1) & 1, abort_flag)) { ok = false; break; }
           tc_fence_after();
           const uint32_t v_addr = smem_u32(sV + st * V_BYTES);
-          const uint32_t p_addr = smem_u32(sP);
+          const uint32_t p_addr = smem_u32(sP + st * P_BYTES);
 #pragma unroll
           for (int kk = 0; kk < BKV / 16; ++kk) {
             const uint64_t ad = umma_desc_sw128(p_addr + (kk >> 2) * (P_BYTES / 2) + (kk & 3) * 32, 16, 1024);
             const uint64_t bd = umma_desc_sw128(v_addr + kk * 16 * 128, V_BYTES / 2, 1024);
             mma_f16_ss(tmem + TM_O, ad, bd, id_pv, (jj > 0 || kk > 0) ? 1u : 0u);
           }
-          mma_commit(o_done);
+          mma_commit(&o_done[st]);
           mma_commit(&v_empty[st]);
         }
       }
@@ -239,18 +246,15 @@ __global__ void __launch_bounds__(attn::THREADS, 1) sage_attn_kernel(const __gri
       bool w = mbar_wait(&s_full[sb], (j >> 1) & 1, abort_flag);
       if (!__all_sync(0xffffffffu, w)) { ok = false; break; }
       tc_fence_after();
-      // column factors: k_scale[(2j + c/64)*4 + (c%8)/2] * q_scale * sm_scale * log2e,
-      // and their products with -1.5*2^23 for the exact int->float conversion below
-      float kf[8], kb[8];
+      // column factors kf[g] = k_scale[(2j + c/64)*4 + (c%8)/2] * q_scale * sm_scale * log2e
+      // (all positive) for the 8 scale groups g of this 128-key block
+      float kf[8];
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         const int kb64 = 2 * j + h;
 #pragma unroll
-        for (int g = 0; g < 4; ++g) {
-          const float f = (kb64 * 64 < S) ? args.ks[static_cast<size_t>(bh) * args.ngk + kb64 * 4 + g] * qsm : 0.0f;
-          kf[h * 4 + g] = f;
-          kb[h * 4 + g] = -12582912.0f * f;
-        }
+        for (int g = 0; g < 4; ++g)
+          kf[h * 4 + g] = (kb64 * 64 < S) ? args.ks[static_cast<size_t>(bh) * args.ngk + kb64 * 4 + g] * qsm : 1.0f;
       }
       // all four 32-column loads in flight, one wait
       uint32_t r[BKV];
@@ -263,26 +267,26 @@ __global__ void __launch_bounds__(attn::THREADS, 1) sage_attn_kernel(const __gri
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&s_free[sb]);
-      // |acc| <= 128^3 < 2^22: float bits (acc + 0x4B400000) are exactly 1.5*2^23 + acc,
-      // so s = (1.5*2^23 + acc) * kf - 1.5*2^23 * kf, one integer add and one FMA.
-      float sv[BKV];
+      const bool tail = (j + 1) * BKV > S;  // last block reaches past the sequence end
+      if (tail) {
+#pragma unroll
+        for (int i = 0; i < BKV; ++i)
+          if (j * BKV + i >= S) r[i] = 0x80000000u;  // INT_MIN: never the max, exp -> 0 below
+      }
+      // Row max: the scales are positive, so max(acc * kf[g]) = kf[g] * max(acc) per
+      // scale group -- integer maxima, then 8 products.
+      int gmax[8];
+#pragma unroll
+      for (int g = 0; g < 8; ++g) gmax[g] = INT_MIN;
 #pragma unroll
       for (int i = 0; i < BKV; ++i) {
         const int g = (i >> 6) * 4 + ((i & 7) >> 1);
-        sv[i] = fmaf(__int_as_float(static_cast<int>(r[i]) + 0x4B400000), kf[g], kb[g]);
+        gmax[g] = max(gmax[g], static_cast<int>(r[i]));
       }
-      if (j == nkb - 1 && (j + 1) * BKV > S) {
+      float mloc = -5000000.0f;
 #pragma unroll
-        for (int i = 0; i < BKV; ++i)
-          if (j * BKV + i >= S) sv[i] = -5000000.0f;
-      }
-      float mp[8];
-#pragma unroll
-      for (int u = 0; u < 8; ++u) mp[u] = sv[u];
-#pragma unroll
-      for (int i = 8; i < BKV; ++i) mp[i & 7] = fmaxf(mp[i & 7], sv[i]);
-      const float mloc = fmaxf(fmaxf(fmaxf(mp[0], mp[1]), fmaxf(mp[2], mp[3])),
-                               fmaxf(fmaxf(mp[4], mp[5]), fmaxf(mp[6], mp[7])));
+      for (int g = 0; g < 8; ++g)
+        if (gmax[g] != INT_MIN) mloc = fmaxf(mloc, static_cast<float>(gmax[g]) * kf[g]);
       // Lazy rescale: the running max used for P only moves when the row max
       // grows by more than 8 (P stays <= 2^8, exact in FP16 range); O and l are
       // rescaled with it, so O / l is unchanged in exact arithmetic.
@@ -290,53 +294,79 @@ __global__ void __launch_bounds__(attn::THREADS, 1) sage_attn_kernel(const __gri
       const bool grow = m_new > m + 8.0f;
       const float alpha = grow ? ex2_approx(m - m_new) : 1.0f;
       const float m_use = grow ? m_new : m;
-      if (j > 0) {
-        w = mbar_wait(o_done, (j - 1) & 1, abort_flag);
+      if (j > 0 && __any_sync(0xffffffffu, grow)) {
+        // O holds P.V of blocks < j once P.V of block j-1 is complete
+        w = mbar_wait(&o_done[(j - 1) & 1], ((j - 1) >> 1) & 1, abort_flag);
         if (!__all_sync(0xffffffffu, w)) { ok = false; break; }
         tc_fence_after();
-        if (__any_sync(0xffffffffu, grow)) {
 #pragma unroll 1
-          for (int c = 0; c < D; c += 32) {
-            uint32_t o[32];
-            tmem_ld32(tmem + lane_off + TM_O + c, o);
-            tmem_ld_wait();
+        for (int c = 0; c < D; c += 32) {
+          uint32_t o[32];
+          tmem_ld32(tmem + lane_off + TM_O + c, o);
+          tmem_ld_wait();
 #pragma unroll
-            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-            tmem_st32(tmem + lane_off + TM_O + c, o);
-          }
-          tmem_st_wait();
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+          tmem_st32(tmem + lane_off + TM_O + c, o);
         }
+        tmem_st_wait();
       }
-      // P = exp2(s - m_use) (even columns on MUFU, odd ones by polynomial) ->
-      // FP16 into the K-major 128-byte-swizzled A-operand tile; the row sum
-      // accumulates in 8 partial sums.
+      // P buffer j&1 was last read by P.V of block j-2
+      if (j >= 2) {
+        w = mbar_wait(&o_done[sb], ((j - 2) >> 1) & 1, abort_flag);
+        if (!__all_sync(0xffffffffu, w)) { ok = false; break; }
+      }
+      // exponent argument: acc * kf - m_use = (1.5*2^23 + acc) * kf + (-1.5*2^23 * kf - m_use),
+      // where the float bits of (acc + 0x4B400000) are exactly 1.5*2^23 + acc (|acc| < 2^22).
+      float kb[8];
+#pragma unroll
+      for (int g = 0; g < 8; ++g) kb[g] = fmaf(-12582912.0f, kf[g], -m_use);
+      // P = exp2(.) -> FP16 into the K-major 128-byte-swizzled A-operand tile (one
+      // exponential in eight on the FMA pipe, the rest on MUFU); the row sum
+      // accumulates the FP32 values in 8 partial sums.
       float lp[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-      uint8_t* prow = sP + row * 128;
+      uint8_t* prow = sP + sb * P_BYTES + row * 128;
+      const int valid = S - j * BKV;  // keys of this block inside the sequence
+      // TAIL: the last block, whose keys past the sequence end get P = 0
+      auto exp_block = [&](auto tail_tag) {
+        constexpr bool TAIL = decltype(tail_tag)::value;
 #pragma unroll
-      for (int c = 0; c < BKV / 8; ++c) {
-        uint32_t pk[4];
+        for (int c = 0; c < BKV / 8; ++c) {
+          uint32_t pk[4];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float p0 = ex2_approx(sv[c * 8 + 2 * e] - m_use);
-          const float p1 = exp2_poly(sv[c * 8 + 2 * e + 1] - m_use);
-          lp[(2 * e) & 7] += p0;
-          lp[(2 * e + 1) & 7] += p1;
-          __half2 h2 = __floats2half2_rn(p0, p1);
-          pk[e] = *reinterpret_cast<uint32_t*>(&h2);
+          for (int e = 0; e < 4; ++e) {
+            const int i0 = c * 8 + 2 * e, i1 = i0 + 1;
+            const int g0 = (i0 >> 6) * 4 + ((i0 & 7) >> 1), g1 = (i1 >> 6) * 4 + ((i1 & 7) >> 1);
+            const float x0 = fmaf(__int_as_float(static_cast<int>(r[i0]) + 0x4B400000), kf[g0], kb[g0]);
+            const float x1 = fmaf(__int_as_float(static_cast<int>(r[i1]) + 0x4B400000), kf[g1], kb[g1]);
+            float p0 = ex2_approx(x0);
+            float p1 = (e == 3) ? exp2_poly(x1) : ex2_approx(x1);
+            if (TAIL) {
+              if (i0 >= valid) p0 = 0.0f;
+              if (i1 >= valid) p1 = 0.0f;
+            }
+            lp[(2 * e) & 7] += p0;
+            lp[(2 * e + 1) & 7] += p1;
+            __half2 h2 = __floats2half2_rn(p0, p1);
+            pk[e] = *reinterpret_cast<uint32_t*>(&h2);
+          }
+          const int region = c >> 3, cc = c & 7;
+          uint8_t* dst = prow + region * (P_BYTES / 2) + ((cc ^ (row & 7)) << 4);
+          *reinterpret_cast<uint4*>(dst) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
         }
-        const int region = c >> 3, cc = c & 7;
-        uint8_t* dst = prow + region * (P_BYTES / 2) + ((cc ^ (row & 7)) << 4);
-        *reinterpret_cast<uint4*>(dst) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-      }
+      };
+      if (tail)
+        exp_block(std::true_type{});
+      else
+        exp_block(std::false_type{});
       l = l * alpha + (((lp[0] + lp[1]) + (lp[2] + lp[3])) + ((lp[4] + lp[5]) + (lp[6] + lp[7])));
       fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(p_full);
+      if (lane == 0) mbar_arrive(&p_full[sb]);
       m = m_use;
     }
     if (ok) {
-      bool w = mbar_wait(o_done, (nkb - 1) & 1, abort_flag);
+      bool w = mbar_wait(&o_done[(nkb - 1) & 1], ((nkb - 1) >> 1) & 1, abort_flag);
       ok = __all_sync(0xffffffffu, w);
     }
     if (!ok) {

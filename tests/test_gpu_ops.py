@@ -181,6 +181,27 @@ def test_sage_attention_large_logits():
     assert cos > 0.999 and maxrel < 2e-2, (cos, maxrel)
 
 
+@pytest.mark.parametrize("zero", ["q", "k", "v"])
+def test_sage_attention_degenerate_heads(zero):
+    """An all-zero Q (or K) head gives uniform attention over the valid keys
+    (tiny scales must not let masked keys in); a zero V head gives zeros."""
+    BH, S = 3, 300  # S not a multiple of the 128-key block
+    q = Q.synth((BH, S, 128), Q.seed_for(16, "q"), 1.0).half()
+    k = Q.synth((BH, S, 128), Q.seed_for(16, "k"), 1.0).half()
+    v = Q.synth((BH, S, 128), Q.seed_for(16, "v"), 1.0).half()
+    {"q": q, "k": k, "v": v}[zero][1].zero_()
+    scale = 1.0 / np.sqrt(128.0)
+    ours = Q.sage_attention(q, k, v, scale)
+    ref = R.sage_attention(q, k, v, scale)
+    cos, maxrel = metrics(ours, ref)
+    assert cos > 0.9999 and maxrel < 1e-2, (cos, maxrel)
+    if zero == "v":
+        assert torch.equal(ours[1], torch.zeros_like(ours[1]))
+    else:
+        uniform = v[1].float().mean(0, keepdim=True).expand(S, 128)
+        assert (ours[1] - uniform).abs().max() < 2e-3
+
+
 # ------------------------------------------------------------------ norms
 def test_layer_norm_modulate_matches_reference():
     x = Q.synth((333, 3072), Q.seed_for(16, "x"), 2.0) + 0.5
