@@ -606,13 +606,9 @@ int attention_launch(const AttnArgs& a, cudaStream_t stream, int* err_dev) {
   if ((reinterpret_cast<uintptr_t>(a.qc) & 15) || (reinterpret_cast<uintptr_t>(a.kc) & 15) ||
       (reinterpret_cast<uintptr_t>(a.v) & 15) || (reinterpret_cast<uintptr_t>(a.out) & 15))
     return QI_ERR_ALIGN;
-  static bool attr = false;
-  if (!attr) {
-    if (cudaFuncSetAttribute(sage_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, attn::SMEM_BYTES) !=
-        cudaSuccess)
-      return QI_ERR_CUDA;
-    attr = true;
-  }
+  static unsigned long long attr_done = 0;
+  if (smem_optin(reinterpret_cast<const void*>(sage_attn_kernel), attn::SMEM_BYTES, &attr_done) != QI_OK)
+    return QI_ERR_CUDA;
   AttnArgsDev d;
   memset(&d, 0, sizeof(d));
   if (encode_3d(&d.tmQ, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a.qc, a.S, a.BH, 128) != QI_OK) return QI_ERR_CUDA;

@@ -403,13 +403,9 @@ static int encode_kmajor(CUtensorMap* tm, const void* base, int rows, int K, int
 
 template <bool BF16>
 static int launch_args(GemmArgsDev& args, cudaStream_t stream, int num_sms) {
-  static bool attr_set = false;
-  if (!attr_set) {
-    if (cudaFuncSetAttribute(gemm_kernel<BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, gemm::SMEM_BYTES) !=
-        cudaSuccess)
-      return QI_ERR_CUDA;
-    attr_set = true;
-  }
+  static unsigned long long attr_done = 0;
+  if (smem_optin(reinterpret_cast<const void*>(gemm_kernel<BF16>), gemm::SMEM_BYTES, &attr_done) != QI_OK)
+    return QI_ERR_CUDA;
   int grid = args.total_tiles < num_sms ? args.total_tiles : num_sms;
   gemm_kernel<BF16><<<grid, gemm::THREADS, gemm::SMEM_BYTES, stream>>>(args);
   return cudaGetLastError() == cudaSuccess ? QI_OK : QI_ERR_CUDA;

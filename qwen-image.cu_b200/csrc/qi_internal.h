@@ -20,6 +20,20 @@ constexpr int kOutCh = 16;
 
 enum Epilogue { kEpiStore = 0, kEpiGelu = 1, kEpiResidual = 2 };
 
+// Raises a kernel's dynamic shared-memory limit on the current device, once
+// per device: the attribute belongs to the device, so a process that drives
+// several GPUs has to set it on each.  `done` is the caller's per-kernel
+// bit mask of devices already set (devices 0..63).
+inline int smem_optin(const void* fn, int bytes, unsigned long long* done) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return QI_ERR_CUDA;
+  const unsigned long long bit = 1ull << dev;
+  if (__atomic_load_n(done, __ATOMIC_ACQUIRE) & bit) return QI_OK;
+  if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess) return QI_ERR_CUDA;
+  __atomic_fetch_or(done, bit, __ATOMIC_ACQ_REL);
+  return QI_OK;
+}
+
 // ---------------------------------------------------------------- GEMMs
 // INT8: out = acc * sa[m] * sw[n] + bias[n] (+ epilogue).  a [M,K], w [N,K].
 struct GemmDesc {

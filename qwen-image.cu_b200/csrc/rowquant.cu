@@ -223,6 +223,125 @@ __global__ void __launch_bounds__(NW * 32) rowquant_warp_kernel(RowSegs segs, in
   }
 }
 
+// K = 12288, block 4096: one warp per 4096-block, lane l holding float4 j at
+// element 128j + 4l (coalesced loads and stores).  Element-index bits 0-1 are
+// the float4 components, bits 2-6 the lane, bits 7-11 the register index.
+// Instead of 5 shuffle stages over 128 values per lane, the warp transposes
+// its block through a private, XOR-swizzled 16 KB shared-memory tile so that
+// bits 2-6 become register bits (lane L then holds elements 128L .. 128L+127),
+// runs those stages in registers, and transposes back for bits 7-11; the
+// stage order (half = 1, 2, 4, ..., 2048) and every butterfly's operands are
+// those of the reference.
+__global__ void __launch_bounds__(96) rowquant_b4096_kernel(RowSegs segs, int had_block, int8_t* __restrict__ codes,
+                                                            float* __restrict__ scales) {
+  constexpr int K = 12288, NW = 3, J = 32;
+  extern __shared__ float4 tile4[];  // [NW][32 rows][32 float4], swizzled: (row, col) at row*32 + (col ^ row)
+  __shared__ float red[NW];
+  const int row = blockIdx.x;
+  const bool second = segs.nseg > 1 && row >= segs.s[0].rows;
+  const void* in = second ? segs.s[1].in : segs.s[0].in;
+  const long long ld = second ? segs.s[1].ld : segs.s[0].ld;
+  const int local = second ? row - segs.s[0].rows : row;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int base = warp * 4096 + 4 * lane;
+  float4* tw = tile4 + warp * 1024;
+
+  float v[J][4];
+  {
+    const float* src = reinterpret_cast<const float*>(in) + static_cast<long long>(local) * ld + base;
+#pragma unroll
+    for (int j = 0; j < J; ++j) {
+      const float4 f = *reinterpret_cast<const float4*>(src + 128 * j);
+      v[j][0] = f.x;
+      v[j][1] = f.y;
+      v[j][2] = f.z;
+      v[j][3] = f.w;
+    }
+  }
+  auto stage_components = [&]() {
+#pragma unroll
+    for (int j = 0; j < J; ++j) {
+      float a = v[j][0], b = v[j][1];
+      v[j][0] = a + b;
+      v[j][1] = a - b;
+      a = v[j][2];
+      b = v[j][3];
+      v[j][2] = a + b;
+      v[j][3] = a - b;
+    }
+#pragma unroll
+    for (int j = 0; j < J; ++j) {
+      float a = v[j][0], b = v[j][2];
+      v[j][0] = a + b;
+      v[j][2] = a - b;
+      a = v[j][1];
+      b = v[j][3];
+      v[j][1] = a + b;
+      v[j][3] = a - b;
+    }
+  };
+  auto stages_registers = [&]() {  // register-index bits, lowest first
+#pragma unroll
+    for (int jm = 1; jm < J; jm <<= 1)
+#pragma unroll
+      for (int j = 0; j < J; ++j) {
+        if (j & jm) continue;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float a = v[j][e], b = v[j | jm][e];
+          v[j][e] = a + b;
+          v[j | jm][e] = a - b;
+        }
+      }
+  };
+  // transpose: (row j, col lane) <-> (row lane, col j) of the 32 x 32 float4 grid
+  auto transpose = [&]() {
+#pragma unroll
+    for (int j = 0; j < J; ++j) tw[j * 32 + (lane ^ j)] = make_float4(v[j][0], v[j][1], v[j][2], v[j][3]);
+    __syncwarp();
+#pragma unroll
+    for (int c = 0; c < J; ++c) {
+      const float4 f = tw[lane * 32 + (c ^ lane)];
+      v[c][0] = f.x;
+      v[c][1] = f.y;
+      v[c][2] = f.z;
+      v[c][3] = f.w;
+    }
+    __syncwarp();
+  };
+  stage_components();  // half = 1, 2
+  transpose();         // lane <- bits 7-11, register <- bits 2-6
+  stages_registers();  // half = 4 .. 64
+  transpose();         // back: lane <- bits 2-6, register <- bits 7-11
+  stages_registers();  // half = 128 .. 2048
+
+  const float norm = rsqrtf(static_cast<float>(had_block));  // had_block == 4096, evaluated at run time
+  float mx = 0.0f;
+#pragma unroll
+  for (int j = 0; j < J; ++j)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      v[j][e] *= norm;
+      mx = fmaxf(mx, fabsf(v[j][e]));
+    }
+  mx = warp_max(mx);
+  if (lane == 0) red[warp] = mx;
+  __syncthreads();
+  mx = fmaxf(fmaxf(red[0], red[1]), red[2]);
+  if (threadIdx.x == 0) scales[row] = mx / 127.0f;
+  const float inv = (mx > 0.0f) ? 127.0f / mx : 0.0f;
+  int8_t* dst = codes + static_cast<long long>(row) * K + base;
+#pragma unroll
+  for (int j = 0; j < J; ++j) {
+    char4 q;
+    q.x = static_cast<signed char>(max(-128, min(127, __float2int_rn(v[j][0] * inv))));
+    q.y = static_cast<signed char>(max(-128, min(127, __float2int_rn(v[j][1] * inv))));
+    q.z = static_cast<signed char>(max(-128, min(127, __float2int_rn(v[j][2] * inv))));
+    q.w = static_cast<signed char>(max(-128, min(127, __float2int_rn(v[j][3] * inv))));
+    *reinterpret_cast<char4*>(dst + 128 * j) = q;
+  }
+}
+
 // Generic version: the whole row in shared memory, every stage over all
 // pairs (the structure of fwht_quantize_kernel / fwht_inplace_kernel).
 __global__ void fwht_quant_generic_kernel(const void* __restrict__ in, int in_bf16, int K, int had_block,
@@ -310,6 +429,14 @@ int rowquant_launch(int src, int K, int had_block, const RowSeg* segs, int nseg,
   if (K == 3072 && src == kSrcF16) return launch_warp<3072, 3, kSrcF16>(s, rows, had_block, codes, scales, eps, stream);
   if (K == 3072 && src == kSrcLnMod)
     return launch_warp<3072, 3, kSrcLnMod>(s, rows, had_block, codes, scales, eps, stream);
+  if (K == 12288 && src == kSrcF32 && had_block == 4096) {
+    const int smem = 3 * 1024 * 16;  // three 16 KB warp tiles
+    static unsigned long long attr_done = 0;
+    if (smem_optin(reinterpret_cast<const void*>(rowquant_b4096_kernel), smem, &attr_done) != QI_OK)
+      return QI_ERR_CUDA;
+    rowquant_b4096_kernel<<<rows, 96, smem, stream>>>(s, had_block, codes, scales);
+    return cudaGetLastError() == cudaSuccess ? QI_OK : QI_ERR_CUDA;
+  }
   if (K == 12288 && src == kSrcF32)
     return launch_warp<12288, 3, kSrcF32>(s, rows, had_block, codes, scales, eps, stream);
   if (K == 256 && src == kSrcF32) return launch_warp<256, 1, kSrcF32>(s, rows, had_block, codes, scales, eps, stream);
@@ -322,13 +449,9 @@ int fwht_quant_generic(const void* in, int in_bf16, int M, int K, int had_block,
   if (had_block < 1 || (had_block & (had_block - 1)) || K % had_block) return QI_ERR_ARG;
   if (M == 0) return QI_OK;
   const int smem = (K + 32) * static_cast<int>(sizeof(float));
-  static bool attr = false;
-  if (!attr) {
-    if (cudaFuncSetAttribute(fwht_quant_generic_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (12288 + 32) * 4) != cudaSuccess)
-      return QI_ERR_CUDA;
-    attr = true;
-  }
+  static unsigned long long attr_done = 0;
+  if (smem_optin(reinterpret_cast<const void*>(fwht_quant_generic_kernel), (12288 + 32) * 4, &attr_done) != QI_OK)
+    return QI_ERR_CUDA;
   int threads = K < 1024 ? ((K + 31) / 32) * 32 : 1024;
   fwht_quant_generic_kernel<<<M, threads, smem, stream>>>(in, in_bf16, K, had_block, codes, scales);
   return cudaGetLastError() == cudaSuccess ? QI_OK : QI_ERR_CUDA;
