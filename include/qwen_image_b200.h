@@ -71,6 +71,27 @@ int qi_linear_i8(const int8_t* act, const float* act_scales, int M, int K, const
 int qi_linear_i8_f32in(const float* x, int M, int K, const int8_t* w, const float* w_scales, int N,
                        const void* bias_bf16, int apply_gelu, float* out, void* stream);
 
+/* qi_linear_i8_f32in without any device allocation: same arguments, same
+ * kernels, same results.  No counterpart in the reference.
+ * For callers that must not allocate device memory once running (a server
+ * whose memory pool owns all of HBM, so cudaMalloc would fail; a step loop
+ * that cannot take cudaMalloc's implicit device synchronisation).  The
+ * quantised activations live in a fixed scratch array compiled into the
+ * library (about 4 MiB per device), so:
+ *   - M <= QI_NOALLOC_MAX_ROWS and M * K <= QI_NOALLOC_MAX_CODES, else the
+ *     call returns QI_ERR_UNSUPPORTED and launches nothing;
+ *   - the first call on a device does one-time setup (looks up the scratch
+ *     address with that device current): make it before any stream capture;
+ *   - the scratch is shared by all calls on a device: calls that can overlap
+ *     (different streams or host threads without ordering between them)
+ *     race and corrupt each other's results; serialise them.
+ * Only the scratch's error word must be zero when the kernels start; the call
+ * clears it on `stream` itself.  Codes and scales are fully overwritten.     */
+#define QI_NOALLOC_MAX_ROWS 4096
+#define QI_NOALLOC_MAX_CODES (4 * 1024 * 1024)
+int qi_linear_i8_f32in_noalloc(const float* x, int M, int K, const int8_t* w, const float* w_scales, int N,
+                               const void* bias_bf16, int apply_gelu, float* out, void* stream);
+
 /* SageAttention on FP16 Q, K, V laid out [BH, S, 128] (head-major):
  * K mean smoothing, per-thread INT8 Q/K quantisation, INT8 QK^T, FP16 P.V,
  * online base-2 softmax; output FP32 [BH, S, 128] (each value an FP16

@@ -76,6 +76,7 @@ def lib():
             "qi_fwht_quantize": ([vp, i, i, i, vp, vp, vp], i),
             "qi_linear_i8": ([vp, vp, i, i, vp, vp, i, vp, i, vp, vp, i, vp], i),
             "qi_linear_i8_f32in": ([vp, i, i, vp, vp, i, vp, i, vp, vp], i),
+            "qi_linear_i8_f32in_noalloc": ([vp, i, i, vp, vp, i, vp, i, vp, vp], i),
             "qi_sage_attention": ([vp, vp, vp, vp, f, i, i, i, vp], i),
             "qi_sage_quantize": ([vp, vp, i, i, vp, vp, vp, vp, vp, vp], i),
             "qi_layer_norm_modulate": ([vp, vp, vp, vp, i, i, f, vp], i),
