@@ -16,18 +16,21 @@
 //     accumulation in TMEM; the row sum is accumulated in FP32; the running
 //     max used for P moves only when the row max grows by more than 2^8 (then
 //     O is rescaled in TMEM), which leaves O / l unchanged in exact arithmetic;
-//   * one exponential in eight runs as a degree-3 polynomial on the FMA pipe,
-//     the rest on MUFU (ex2.approx), which balances MUFU against issue slots;
+//   * exponentials on MUFU (ex2.approx); a degree-3 polynomial on the FMA
+//     pipe can take a share of them (compile-time option, off by default);
 //   * the result is O * rcp(l) rounded to FP16 (normalize_d, :719-760).
 //
-// Tiling: one CTA per (128 queries, batch-head); keys in blocks of 128 (two
-// of the reference's 64-key scale blocks).  Warp 0 issues TMA (Q once, K/V in
-// a two-stage ring), warp 1 issues the MMAs (QK^T of block j+1 is issued
-// before P.V of block j so the tensor core works while softmax runs), warps
-// 2-5 own one query row per thread (TMEM lane = row).
-// TMEM: S double buffer (2 x 128 columns) + O (128 columns).  P is double
-// buffered in shared memory, so the softmax of block j overlaps P.V of block
-// j-1 and only waits for it when O has to be rescaled.
+// Tiling: one CTA per (256 queries, batch-head) = two 128-query tiles that
+// share one K/V stream (keys in blocks of 128, two of the reference's 64-key
+// scale blocks; a three-stage TMA ring).  Warp 0 issues TMA, warp 1 the MMAs,
+// warps 4-7 run the softmax of tile 0 and warps 8-11 that of tile 1 (one query
+// row per thread, TMEM lane = row); the softmax warpgroups take the registers
+// warpgroup 0 does not need (setmaxnreg).  TMEM holds, per tile, S (128 columns)
+// and O (128 columns); the softmax writes P as packed FP16 over the first 64
+// columns of its S, and P.V reads it from TMEM as the A operand.  Per tile the
+// chain is QK(j) -> softmax(j) -> PV(j) -> QK(j+1); the two tiles' chains are
+// interleaved so the tensor core runs one tile's MMAs while the other tile's
+// softmax runs.
 #include "qi_internal.h"
 #include "sm100.cuh"
 
@@ -38,19 +41,34 @@ namespace qi {
 
 namespace attn {
 constexpr int BQ = 128, BKV = 128, D = 128;
-constexpr int Q_BYTES = BQ * D;        // int8
-constexpr int K_BYTES = BKV * D;       // int8
-constexpr int V_BYTES = BKV * D * 2;   // fp16
-constexpr int P_BYTES = BQ * BKV * 2;  // fp16
+constexpr int NT = 2;                 // query tiles per CTA
+constexpr int STAGES = 3;             // K/V ring depth
+constexpr int Q_BYTES = BQ * D;       // int8, one tile
+constexpr int K_BYTES = BKV * D;      // int8
+constexpr int V_BYTES = BKV * D * 2;  // fp16
 constexpr int OFF_Q = 0;
-constexpr int OFF_K = OFF_Q + Q_BYTES;
-constexpr int OFF_V = OFF_K + 2 * K_BYTES;
-constexpr int OFF_P = OFF_V + 2 * V_BYTES;
-constexpr int OFF_BAR = OFF_P + 2 * P_BYTES;
-constexpr int SMEM_BYTES = OFF_BAR + 256 + 1024;
-constexpr int THREADS = 192;
+constexpr int OFF_K = OFF_Q + NT * Q_BYTES;
+constexpr int OFF_V = OFF_K + STAGES * K_BYTES;
+constexpr int OFF_BAR = OFF_V + STAGES * V_BYTES;
+constexpr int OFF_KS = OFF_BAR + 256;  // this batch-head's K scales (FP32), loaded once
+constexpr int MAX_S = 131072;          // K scales of up to 8192 64-key blocks fit in shared memory
+constexpr int smem_bytes(int ngk) { return OFF_KS + ngk * 4 + 1024; }
+constexpr int THREADS = 384;  // warpgroup 0: TMA warp, MMA warp, 2 idle; warpgroups 1, 2: softmax of tiles 0, 1
+// Register split (setmaxnreg): launched at 168 per thread (384 x 168 = 64512);
+// warpgroup 0 gives up to 56, the two softmax warpgroups take 224:
+// 128 x 56 + 256 x 224 = 64512.
+constexpr int LAUNCH_REGS = 168, PRODUCER_REGS = 56, SOFTMAX_REGS = 224;
+static_assert(128 * PRODUCER_REGS + 256 * SOFTMAX_REGS <= THREADS * LAUNCH_REGS, "register split exceeds the launch");
 constexpr int TMEM_COLS = 512;
-constexpr int TM_S0 = 0, TM_S1 = 128, TM_O = 256;
+constexpr int TM_S = 0;    // S / P of tile t at column 128 t
+constexpr int TM_O = 256;  // O of tile t at column 256 + 128 t
+// Optional: every POLY_EVERY-th odd key's exponential on the FMA pipe
+// (exp2_poly) instead of MUFU.  Off by default: measured on B200, the softmax
+// is not MUFU-bound at this tiling and the extra instructions cost time.
+#ifndef QI_ATTN_POLY_EVERY
+#define QI_ATTN_POLY_EVERY 0
+#endif
+constexpr int POLY_EVERY = QI_ATTN_POLY_EVERY;
 }  // namespace attn
 
 struct alignas(64) AttnArgsDev {
@@ -63,13 +81,14 @@ struct alignas(64) AttnArgsDev {
   int* err;
 };
 
+// Not volatile: a pure function of its input, so the compiler may schedule
+// the exponentials freely among the surrounding arithmetic.
 __device__ __forceinline__ float ex2_approx(float x) {
   float y;
-  asm volatile("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
-// 2^x for x <= 0 on the FMA/ALU pipes (half of the softmax exponentials go
-// here, half to MUFU ex2, so neither pipe limits the softmax): x = n + f with
+// 2^x for x <= 0 on the FMA/ALU pipes (the POLY_EVERY option): x = n + f with
 // n = round(x), |f| <= 1/2; 2^f by a degree-3 polynomial fitted on [-1/2, 1/2]
 // (max relative error 7.5e-5, under FP16's 4.9e-4 half ulp); 2^n is added to
 // the exponent field.  x is clamped at -125 so the exponent cannot underflow
@@ -87,8 +106,17 @@ __device__ __forceinline__ float exp2_poly(float x) {
 
 __device__ __forceinline__ float rcp_approx(float x) {
   float y;
-  asm volatile("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+
+// Bounded wait that ignores the abort flag (used to drain work this thread
+// itself issued before it tears down).
+__device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity) {
+  const uint64_t t0 = global_timer_ns();
+  while (!mbar_try_wait(bar, parity) && global_timer_ns() - t0 < kWaitLimitNs / 4) {
+  }
 }
 
 __global__ void __launch_bounds__(attn::THREADS, 1) sage_attn_kernel(const __grid_constant__ AttnArgsDev args) {
@@ -98,40 +126,41 @@ __global__ void __launch_bounds__(attn::THREADS, 1) sage_attn_kernel(const __gri
   uint8_t* sQ = smem + OFF_Q;
   uint8_t* sK = smem + OFF_K;
   uint8_t* sV = smem + OFF_V;
-  uint8_t* sP = smem + OFF_P;
+  float* sKS = reinterpret_cast<float*>(smem + OFF_KS);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
   uint64_t* q_full = bars + 0;
-  uint64_t* k_full = bars + 1;   // [2]
-  uint64_t* k_empty = bars + 3;  // [2]
-  uint64_t* v_full = bars + 5;   // [2]
-  uint64_t* v_empty = bars + 7;  // [2]
-  uint64_t* s_full = bars + 9;   // [2]
-  uint64_t* s_free = bars + 11;  // [2]
-  uint64_t* p_full = bars + 13;  // [2] P buffer j&1 written
-  uint64_t* o_done = bars + 15;  // [2] P.V of block j (reading P buffer j&1) complete
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 17);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 18);
+  uint64_t* k_full = bars + 1;                // [STAGES]
+  uint64_t* k_empty = k_full + STAGES;        // [STAGES]
+  uint64_t* v_full = k_empty + STAGES;        // [STAGES]
+  uint64_t* v_empty = v_full + STAGES;        // [STAGES]
+  uint64_t* s_full = v_empty + STAGES;        // [NT] QK of the tile's current block complete
+  uint64_t* p_half = s_full + NT;             // [NT][2] half h of the tile's P written to TMEM (4 warps)
+  uint64_t* o_final = p_half + 2 * NT;        // [NT] the tile's last PV complete (single use)
+  uint64_t* drain = o_final + NT;             // MMA teardown
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(drain + 2);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int q0 = blockIdx.x * BQ;
+  const int q0 = blockIdx.x * (NT * BQ);
   const int bh = blockIdx.y;
   const int S = args.S;
   const int nkb = (S + BKV - 1) / BKV;
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < STAGES; ++i) {
       mbar_init(&k_full[i], 1);
       mbar_init(&k_empty[i], 1);
       mbar_init(&v_full[i], 1);
       mbar_init(&v_empty[i], 1);
-      mbar_init(&s_full[i], 1);
-      mbar_init(&s_free[i], 4);
     }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&p_full[i], 4);
-      mbar_init(&o_done[i], 1);
+    for (int t = 0; t < NT; ++t) {
+      mbar_init(&s_full[t], 1);
+      mbar_init(&p_half[2 * t], 4);
+      mbar_init(&p_half[2 * t + 1], 4);
+      mbar_init(&o_final[t], 1);
     }
+    mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&args.tmQ);
@@ -142,110 +171,141 @@ __global__ void __launch_bounds__(attn::THREADS, 1) sage_attn_kernel(const __gri
     tmem_alloc(tmem_slot, TMEM_COLS);
     tmem_relinquish();
   }
+  if (warp >= 4) {  // K scales of this batch-head into shared memory
+    const float* ks = args.ks + static_cast<size_t>(bh) * args.ngk;
+    for (int i = threadIdx.x - 128; i < args.ngk; i += THREADS - 128) sKS[i] = ks[i];
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 0) {
-    if (lane == 0) {
-      bool ok = true;
-      uint32_t kmask = 0, kpar = 0, vmask = 0, vpar = 0;
-      mbar_expect_tx(q_full, Q_BYTES);
-      tma_load_3d(sQ, &args.tmQ, 0, q0, bh, q_full);
-      for (int j = 0; j < nkb && ok; ++j) {
-        const int st = j & 1;
-        const uint32_t ph = (j >> 1) & 1;
-        if (!mbar_wait(&k_empty[st], ph ^ 1u, abort_flag)) { ok = false; break; }
-        mbar_expect_tx(&k_full[st], K_BYTES);
-        tma_load_3d(sK + st * K_BYTES, &args.tmK, 0, j * BKV, bh, &k_full[st]);
-        kmask |= 1u << st;
-        kpar = (kpar & ~(1u << st)) | (ph << st);
-        if (!mbar_wait(&v_empty[st], ph ^ 1u, abort_flag)) { ok = false; break; }
-        mbar_expect_tx(&v_full[st], V_BYTES);
-        tma_load_3d(sV + st * V_BYTES, &args.tmV, 0, j * BKV, bh, &v_full[st]);
-        tma_load_3d(sV + st * V_BYTES + V_BYTES / 2, &args.tmV, 64, j * BKV, bh, &v_full[st]);
-        vmask |= 1u << st;
-        vpar = (vpar & ~(1u << st)) | (ph << st);
-      }
-      if (!ok) {
-        *abort_flag = 1;
-        atomicCAS(args.err, 0, kErrTimeoutProducer);
-        uint64_t t0 = global_timer_ns();
-        while (!mbar_try_wait(q_full, 0) && global_timer_ns() - t0 < kWaitLimitNs / 4) {
+  if (warp < 4) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(PRODUCER_REGS));
+    if (warp == 0) {
+      if (lane == 0) {
+        bool ok = true;
+        uint32_t kmask = 0, kpar = 0, vmask = 0, vpar = 0;
+        mbar_expect_tx(q_full, NT * Q_BYTES);
+        for (int t = 0; t < NT; ++t) tma_load_3d(sQ + t * Q_BYTES, &args.tmQ, 0, q0 + t * BQ, bh, q_full);
+        for (int j = 0; j < nkb && ok; ++j) {
+          const int st = j % STAGES;
+          const uint32_t ph = (j / STAGES) & 1;
+          if (!mbar_wait(&k_empty[st], ph ^ 1u, abort_flag)) { ok = false; break; }
+          mbar_expect_tx(&k_full[st], K_BYTES);
+          tma_load_3d(sK + st * K_BYTES, &args.tmK, 0, j * BKV, bh, &k_full[st]);
+          kmask |= 1u << st;
+          kpar = (kpar & ~(1u << st)) | (ph << st);
+          if (!mbar_wait(&v_empty[st], ph ^ 1u, abort_flag)) { ok = false; break; }
+          mbar_expect_tx(&v_full[st], V_BYTES);
+          tma_load_3d(sV + st * V_BYTES, &args.tmV, 0, j * BKV, bh, &v_full[st]);
+          tma_load_3d(sV + st * V_BYTES + V_BYTES / 2, &args.tmV, 64, j * BKV, bh, &v_full[st]);
+          vmask |= 1u << st;
+          vpar = (vpar & ~(1u << st)) | (ph << st);
         }
-        for (int s = 0; s < 2; ++s) {
-          t0 = global_timer_ns();
-          if (kmask & (1u << s))
-            while (!mbar_try_wait(&k_full[s], (kpar >> s) & 1u) && global_timer_ns() - t0 < kWaitLimitNs / 4) {
-            }
-          t0 = global_timer_ns();
-          if (vmask & (1u << s))
-            while (!mbar_try_wait(&v_full[s], (vpar >> s) & 1u) && global_timer_ns() - t0 < kWaitLimitNs / 4) {
-            }
-        }
-      }
-    }
-  } else if (warp == 1) {
-    if (lane == 0) {
-      bool ok = mbar_wait(q_full, 0, abort_flag);
-      const uint32_t id_qk = idesc_i8(BQ, BKV);
-      const uint32_t id_pv = idesc_f16(BQ, D, false, true);
-      const uint32_t q_addr = smem_u32(sQ);
-      for (int j = 0; j <= nkb && ok; ++j) {
-        if (j < nkb) {
-          const int st = j & 1;
-          const uint32_t ph = (j >> 1) & 1;
-          if (!mbar_wait(&k_full[st], ph, abort_flag)) { ok = false; break; }
-          if (!mbar_wait(&s_free[st], ph ^ 1u, abort_flag)) { ok = false; break; }
-          tc_fence_after();
-          const uint32_t k_addr = smem_u32(sK + st * K_BYTES);
-          const uint32_t d_s = tmem + (st ? TM_S1 : TM_S0);
-#pragma unroll
-          for (int k = 0; k < D / 32; ++k)
-            mma_i8_ss(d_s, umma_desc_sw128(q_addr + k * 32, 16, 1024), umma_desc_sw128(k_addr + k * 32, 16, 1024),
-                      id_qk, k > 0 ? 1u : 0u);
-          mma_commit(&s_full[st]);
-          mma_commit(&k_empty[st]);
-        }
-        if (j >= 1) {
-          const int jj = j - 1;
-          const int st = jj & 1;
-          if (!mbar_wait(&p_full[st], (jj >> 1) & 1, abort_flag)) { ok = false; break; }
-          if (!mbar_wait(&v_full[st], (jj >> 1) & 1, abort_flag)) { ok = false; break; }
-          tc_fence_after();
-          const uint32_t v_addr = smem_u32(sV + st * V_BYTES);
-          const uint32_t p_addr = smem_u32(sP + st * P_BYTES);
-#pragma unroll
-          for (int kk = 0; kk < BKV / 16; ++kk) {
-            const uint64_t ad = umma_desc_sw128(p_addr + (kk >> 2) * (P_BYTES / 2) + (kk & 3) * 32, 16, 1024);
-            const uint64_t bd = umma_desc_sw128(v_addr + kk * 16 * 128, V_BYTES / 2, 1024);
-            mma_f16_ss(tmem + TM_O, ad, bd, id_pv, (jj > 0 || kk > 0) ? 1u : 0u);
+        if (!ok) {  // let the copies already issued land before the CTA exits
+          *abort_flag = 1;
+          atomicCAS(args.err, 0, kErrTimeoutProducer);
+          drain_wait(q_full, 0);
+          for (int s = 0; s < STAGES; ++s) {
+            if (kmask & (1u << s)) drain_wait(&k_full[s], (kpar >> s) & 1u);
+            if (vmask & (1u << s)) drain_wait(&v_full[s], (vpar >> s) & 1u);
           }
-          mma_commit(&o_done[st]);
-          mma_commit(&v_empty[st]);
         }
       }
-      if (!ok) {
-        *abort_flag = 1;
-        atomicCAS(args.err, 0, kErrTimeoutMma);
+    } else if (warp == 1) {
+      if (lane == 0) {
+        bool ok = mbar_wait(q_full, 0, abort_flag);
+        const uint32_t id_qk = idesc_i8(BQ, BKV);
+        const uint32_t id_pv = idesc_f16(BQ, D, false, true);
+        const uint32_t q_addr = smem_u32(sQ);
+        // S_t = Q_t . K^T for the block in stage st
+        auto qk = [&](int t, int st) {
+          const uint32_t k_addr = smem_u32(sK + st * K_BYTES);
+          const uint32_t qa = q_addr + t * Q_BYTES;
+  #pragma unroll
+          for (int k = 0; k < D / 32; ++k)
+            mma_i8_ss(tmem + TM_S + 128 * t, umma_desc_sw128(qa + k * 32, 16, 1024),
+                      umma_desc_sw128(k_addr + k * 32, 16, 1024), id_qk, k > 0 ? 1u : 0u);
+          mma_commit(&s_full[t]);
+        };
+        // O_t += P_t . V over keys 64h .. 64h+63 of the block in stage st; P_t is read from TMEM
+        auto pv_half = [&](int t, int st, int j, int h) {
+          const uint32_t v_addr = smem_u32(sV + st * V_BYTES);
+  #pragma unroll
+          for (int k4 = 0; k4 < BKV / 32; ++k4) {
+            const int kk = h * (BKV / 32) + k4;
+            mma_f16_ts(tmem + TM_O + 128 * t, tmem + TM_S + 128 * t + kk * 8,
+                       umma_desc_sw128(v_addr + kk * 16 * 128, V_BYTES / 2, 1024), id_pv, (j > 0 || kk > 0) ? 1u : 0u);
+          }
+        };
+        if (ok) ok = mbar_wait(&k_full[0], 0, abort_flag);
+        if (ok) {
+          tc_fence_after();
+          for (int t = 0; t < NT; ++t) qk(t, 0);
+          mma_commit(&k_empty[0]);
+        }
+        for (int j = 0; j < nkb && ok; ++j) {
+          const int st = j % STAGES, nst = (j + 1) % STAGES;
+          const uint32_t ph = (j / STAGES) & 1, nph = ((j + 1) / STAGES) & 1;
+          const bool more = j + 1 < nkb;
+          for (int t = 0; t < NT && ok; ++t) {
+            // each half of P_t . V starts as soon as that half of P_t is in TMEM
+            if (!mbar_wait(&p_half[2 * t], j & 1, abort_flag)) { ok = false; break; }
+            if (t == 0 && !mbar_wait(&v_full[st], ph, abort_flag)) { ok = false; break; }
+            tc_fence_after();
+            pv_half(t, st, j, 0);
+            if (!mbar_wait(&p_half[2 * t + 1], j & 1, abort_flag)) { ok = false; break; }
+            tc_fence_after();
+            pv_half(t, st, j, 1);
+            if (j == nkb - 1) mma_commit(&o_final[t]);
+            if (t == NT - 1) mma_commit(&v_empty[st]);
+            if (more) {
+              if (t == 0 && !mbar_wait(&k_full[nst], nph, abort_flag)) { ok = false; break; }
+              // QK(j+1) overwrites the S_t / P_t columns that P_t . V of block j
+              // reads; the tensor pipe runs one CTA's MMAs in issue order, so it
+              // is issued right behind it.
+              tc_fence_after();
+              qk(t, nst);
+              if (t == NT - 1) mma_commit(&k_empty[nst]);
+            }
+          }
+        }
+        if (!ok) {
+          *abort_flag = 1;
+          atomicCAS(args.err, 0, kErrTimeoutMma);
+        }
+        // every MMA this thread issued has completed before TMEM is released
+        mma_commit(drain);
+        drain_wait(drain, 0);
       }
     }
   } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(SOFTMAX_REGS));
     // -------------------------------------------------------------- softmax
+    const int t = (warp - 4) >> 2;
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;
-    const int qrow = q0 + row;
+    const int qrow = q0 + t * BQ + row;
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
+    const uint32_t s_tm = tmem + lane_off + TM_S + 128 * t;
+    const uint32_t o_tm = tmem + lane_off + TM_O + 128 * t;
     const int gq = (qrow / 128) * 32 + ((qrow % 128) / 32) * 8 + (qrow % 8);
     const float qsm = (qrow < S) ? args.qs[static_cast<size_t>(bh) * args.ngq + gq] * args.qk_scale : 0.0f;
     float m = -5000000.0f, l = 0.0f;
     bool ok = true;
     for (int j = 0; j < nkb; ++j) {
-      const int sb = j & 1;
-      bool w = mbar_wait(&s_full[sb], (j >> 1) & 1, abort_flag);
+      // S_t of block j is in TMEM; P_t . V of block j-1 has completed (both
+      // were issued before the commit that completes this phase), so O_t is
+      // stable and the P_t columns are free
+      bool w = mbar_wait(&s_full[t], j & 1, abort_flag);
       if (!__all_sync(0xffffffffu, w)) { ok = false; break; }
       tc_fence_after();
+      uint32_t r[BKV];
+      tmem_ld32(s_tm + 0, *reinterpret_cast<uint32_t(*)[32]>(r + 0));
+      tmem_ld32(s_tm + 32, *reinterpret_cast<uint32_t(*)[32]>(r + 32));
+      tmem_ld32(s_tm + 64, *reinterpret_cast<uint32_t(*)[32]>(r + 64));
+      tmem_ld32(s_tm + 96, *reinterpret_cast<uint32_t(*)[32]>(r + 96));
       // column factors kf[g] = k_scale[(2j + c/64)*4 + (c%8)/2] * q_scale * sm_scale * log2e
       // (all positive) for the 8 scale groups g of this 128-key block
       float kf[8];
@@ -253,20 +313,9 @@ __global__ void __launch_bounds__(attn::THREADS, 1) sage_attn_kernel(const __gri
       for (int h = 0; h < 2; ++h) {
         const int kb64 = 2 * j + h;
 #pragma unroll
-        for (int g = 0; g < 4; ++g)
-          kf[h * 4 + g] = (kb64 * 64 < S) ? args.ks[static_cast<size_t>(bh) * args.ngk + kb64 * 4 + g] * qsm : 1.0f;
+        for (int g = 0; g < 4; ++g) kf[h * 4 + g] = (kb64 * 64 < S) ? sKS[kb64 * 4 + g] * qsm : 1.0f;
       }
-      // all four 32-column loads in flight, one wait
-      uint32_t r[BKV];
-      const uint32_t s_addr = tmem + lane_off + (sb ? TM_S1 : TM_S0);
-      tmem_ld32(s_addr + 0, *reinterpret_cast<uint32_t(*)[32]>(r + 0));
-      tmem_ld32(s_addr + 32, *reinterpret_cast<uint32_t(*)[32]>(r + 32));
-      tmem_ld32(s_addr + 64, *reinterpret_cast<uint32_t(*)[32]>(r + 64));
-      tmem_ld32(s_addr + 96, *reinterpret_cast<uint32_t(*)[32]>(r + 96));
       tmem_ld_wait();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&s_free[sb]);
       const bool tail = (j + 1) * BKV > S;  // last block reaches past the sequence end
       if (tail) {
 #pragma unroll
@@ -295,78 +344,68 @@ __global__ void __launch_bounds__(attn::THREADS, 1) sage_attn_kernel(const __gri
       const float alpha = grow ? ex2_approx(m - m_new) : 1.0f;
       const float m_use = grow ? m_new : m;
       if (j > 0 && __any_sync(0xffffffffu, grow)) {
-        // O holds P.V of blocks < j once P.V of block j-1 is complete
-        w = mbar_wait(&o_done[(j - 1) & 1], ((j - 1) >> 1) & 1, abort_flag);
-        if (!__all_sync(0xffffffffu, w)) { ok = false; break; }
-        tc_fence_after();
 #pragma unroll 1
         for (int c = 0; c < D; c += 32) {
           uint32_t o[32];
-          tmem_ld32(tmem + lane_off + TM_O + c, o);
+          tmem_ld32(o_tm + c, o);
           tmem_ld_wait();
 #pragma unroll
           for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-          tmem_st32(tmem + lane_off + TM_O + c, o);
+          tmem_st32(o_tm + c, o);
         }
-        tmem_st_wait();
-      }
-      // P buffer j&1 was last read by P.V of block j-2
-      if (j >= 2) {
-        w = mbar_wait(&o_done[sb], ((j - 2) >> 1) & 1, abort_flag);
-        if (!__all_sync(0xffffffffu, w)) { ok = false; break; }
       }
       // exponent argument: acc * kf - m_use = (1.5*2^23 + acc) * kf + (-1.5*2^23 * kf - m_use),
       // where the float bits of (acc + 0x4B400000) are exactly 1.5*2^23 + acc (|acc| < 2^22).
       float kb[8];
 #pragma unroll
       for (int g = 0; g < 8; ++g) kb[g] = fmaf(-12582912.0f, kf[g], -m_use);
-      // P = exp2(.) -> FP16 into the K-major 128-byte-swizzled A-operand tile (one
-      // exponential in eight on the FMA pipe, the rest on MUFU); the row sum
-      // accumulates the FP32 values in 8 partial sums.
+      // P = exp2(.) -> packed FP16 pairs over columns 0-63 of S_t (one odd key in
+      // POLY_EVERY on the FMA pipe, the rest on MUFU); the row sum accumulates
+      // the FP32 values in 8 partial sums.
       float lp[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-      uint8_t* prow = sP + sb * P_BYTES + row * 128;
       const int valid = S - j * BKV;  // keys of this block inside the sequence
       // TAIL: the last block, whose keys past the sequence end get P = 0
-      auto exp_block = [&](auto tail_tag) {
+      auto exp_half = [&](auto tail_tag, int h) {
+        const int hbase = 64 * h;
         constexpr bool TAIL = decltype(tail_tag)::value;
+        uint32_t pk[32];
 #pragma unroll
-        for (int c = 0; c < BKV / 8; ++c) {
-          uint32_t pk[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int i0 = c * 8 + 2 * e, i1 = i0 + 1;
-            const int g0 = (i0 >> 6) * 4 + ((i0 & 7) >> 1), g1 = (i1 >> 6) * 4 + ((i1 & 7) >> 1);
-            const float x0 = fmaf(__int_as_float(static_cast<int>(r[i0]) + 0x4B400000), kf[g0], kb[g0]);
-            const float x1 = fmaf(__int_as_float(static_cast<int>(r[i1]) + 0x4B400000), kf[g1], kb[g1]);
-            float p0 = ex2_approx(x0);
-            float p1 = (e == 3) ? exp2_poly(x1) : ex2_approx(x1);
-            if (TAIL) {
-              if (i0 >= valid) p0 = 0.0f;
-              if (i1 >= valid) p1 = 0.0f;
-            }
-            lp[(2 * e) & 7] += p0;
-            lp[(2 * e + 1) & 7] += p1;
-            __half2 h2 = __floats2half2_rn(p0, p1);
-            pk[e] = *reinterpret_cast<uint32_t*>(&h2);
+        for (int c = 0; c < 32; ++c) {
+          const int i0 = hbase + 2 * c, i1 = i0 + 1;
+          const int g0 = (i0 >> 6) * 4 + ((i0 & 7) >> 1), g1 = (i1 >> 6) * 4 + ((i1 & 7) >> 1);
+          const float x0 = fmaf(__int_as_float(static_cast<int>(r[i0]) + 0x4B400000), kf[g0], kb[g0]);
+          const float x1 = fmaf(__int_as_float(static_cast<int>(r[i1]) + 0x4B400000), kf[g1], kb[g1]);
+          float p0 = ex2_approx(x0);
+          float p1 = (POLY_EVERY > 0 && c % (POLY_EVERY > 0 ? POLY_EVERY : 1) == POLY_EVERY - 1) ? exp2_poly(x1)
+                                                                                           : ex2_approx(x1);
+          if (TAIL) {
+            if (i0 >= valid) p0 = 0.0f;
+            if (i1 >= valid) p1 = 0.0f;
           }
-          const int region = c >> 3, cc = c & 7;
-          uint8_t* dst = prow + region * (P_BYTES / 2) + ((cc ^ (row & 7)) << 4);
-          *reinterpret_cast<uint4*>(dst) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+          lp[(2 * c) & 7] += p0;
+          lp[(2 * c + 1) & 7] += p1;
+          __half2 h2 = __floats2half2_rn(p0, p1);
+          pk[c] = *reinterpret_cast<uint32_t*>(&h2);
         }
+        tmem_st32(s_tm + hbase / 2, pk);
+        // publish this half (and, for h = 0, the rescaled O) to the MMA warp
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&p_half[2 * t + h]);
       };
-      if (tail)
-        exp_block(std::true_type{});
-      else
-        exp_block(std::false_type{});
+      if (tail) {
+        exp_half(std::true_type{}, 0);
+        exp_half(std::true_type{}, 1);
+      } else {
+        exp_half(std::false_type{}, 0);
+        exp_half(std::false_type{}, 1);
+      }
       l = l * alpha + (((lp[0] + lp[1]) + (lp[2] + lp[3])) + ((lp[4] + lp[5]) + (lp[6] + lp[7])));
-      fence_proxy_async_smem();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full[sb]);
       m = m_use;
     }
     if (ok) {
-      bool w = mbar_wait(&o_done[(nkb - 1) & 1], ((nkb - 1) >> 1) & 1, abort_flag);
+      bool w = mbar_wait(&o_final[t], 0, abort_flag);
       ok = __all_sync(0xffffffffu, w);
     }
     if (!ok) {
@@ -382,7 +421,7 @@ __global__ void __launch_bounds__(attn::THREADS, 1) sage_attn_kernel(const __gri
 #pragma unroll 1
       for (int c = 0; c < D; c += 32) {
         uint32_t r[32];
-        tmem_ld32(tmem + lane_off + TM_O + c, r);
+        tmem_ld32(o_tm + c, r);
         tmem_ld_wait();
         if (!valid) continue;
         if (args.out_mode == 0) {
@@ -606,8 +645,20 @@ int attention_launch(const AttnArgs& a, cudaStream_t stream, int* err_dev) {
   if ((reinterpret_cast<uintptr_t>(a.qc) & 15) || (reinterpret_cast<uintptr_t>(a.kc) & 15) ||
       (reinterpret_cast<uintptr_t>(a.v) & 15) || (reinterpret_cast<uintptr_t>(a.out) & 15))
     return QI_ERR_ALIGN;
+  if (a.S > attn::MAX_S) return QI_ERR_UNSUPPORTED;
+  // The setmaxnreg split assumes the kernel was built for exactly LAUNCH_REGS
+  // registers per thread; with fewer, the softmax warpgroups' increase could
+  // never be granted.  Refuse to launch rather than risk that.
+  static int regs_checked = 0;
+  if (!regs_checked) {
+    cudaFuncAttributes fa;
+    if (cudaFuncGetAttributes(&fa, sage_attn_kernel) != cudaSuccess) return QI_ERR_CUDA;
+    if (fa.numRegs != attn::LAUNCH_REGS) return QI_ERR_UNSUPPORTED;
+    regs_checked = 1;
+  }
   static unsigned long long attr_done = 0;
-  if (smem_optin(reinterpret_cast<const void*>(sage_attn_kernel), attn::SMEM_BYTES, &attr_done) != QI_OK)
+  if (smem_optin(reinterpret_cast<const void*>(sage_attn_kernel), attn::smem_bytes(((attn::MAX_S + 63) / 64) * 4),
+                 &attr_done) != QI_OK)
     return QI_ERR_CUDA;
   AttnArgsDev d;
   memset(&d, 0, sizeof(d));
@@ -628,8 +679,8 @@ int attention_launch(const AttnArgs& a, cudaStream_t stream, int* err_dev) {
   d.ngk = ((a.S + 63) / 64) * 4;
   d.qk_scale = a.sm_scale * 1.44269504088896340736f;
   d.err = err_dev;
-  dim3 grid((a.S + attn::BQ - 1) / attn::BQ, a.BH);
-  sage_attn_kernel<<<grid, attn::THREADS, attn::SMEM_BYTES, stream>>>(d);
+  dim3 grid((a.S + attn::NT * attn::BQ - 1) / (attn::NT * attn::BQ), a.BH);
+  sage_attn_kernel<<<grid, attn::THREADS, attn::smem_bytes(d.ngk), stream>>>(d);
   return cudaGetLastError() == cudaSuccess ? QI_OK : QI_ERR_CUDA;
 }
 
