@@ -10,9 +10,11 @@ checkpoint or dataset is available): latents and text states ~ N(0, 1).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-N > 1 (torchrun, one process per GPU): ranks form CFG pairs; rank 2p runs the
-cond half and rank 2p+1 the uncond half of one denoising job with one NCCL
-all-gather of the velocities per step; pairs are independent jobs.
+N > 1 (torchrun, one process per GPU), one denoising job (strong scaling):
+the cond and uncond halves go to two groups of N/2 ranks; within a half the
+forward is head-parallel (Ulysses) over the N/2 ranks when N/2 > 1 (two NCCL
+all-to-alls per block inside the library); one NCCL all-gather of the two
+halves' velocities per step, then every rank runs the same Euler step.
 
 Prints one JSON line (rank 0).  `value` is seconds per step on the device
 with inputs resident in HBM (CUDA events, max over ranks); `e2e` is the same
@@ -153,20 +155,34 @@ def max_over_ranks(v, world):
 # ------------------------------------------------------------------ our arm
 def run_ours(args):
     import qib200 as Q
+    import topology as T
 
     rank, world, local = dist_env()
     init_dist(world, local)
-    pair = world > 1
-    half = rank % 2 if pair else None  # CFG half of this rank
+    pair, P = T.layout(world)  # CFG split over two rank groups; head-parallel size P within a half
+    role = T.roles(rank, world)
+    half = role["half"]  # CFG half of this rank (None: both halves batched here)
     nb = 1 if pair else 2
     g, blocks = Q.make_weight_table(BLOCKS, base_seed=0)
     ctx = Q.Context(local)
     model = Q.Model(ctx, g, blocks)
     del g, blocks
     torch.cuda.empty_cache()
+    group = None
+    if pair:
+        # every rank creates every group, in the same order
+        ugroups = [torch.distributed.new_group([h * P + u for u in range(P)]) for h in range(2)] if P > 1 else None
+        pairs = [torch.distributed.new_group([u, P + u]) for u in range(P)]
+        group = pairs[role["urank"]]
+        if P > 1:  # the library's NCCL communicator for this half's head-parallel group
+            uid = torch.zeros(Q.COMM_ID_BYTES, dtype=torch.uint8, device="cuda")
+            if role["urank"] == 0:
+                uid.copy_(torch.frombuffer(bytearray(Q.comm_unique_id()), dtype=torch.uint8))
+            torch.distributed.broadcast(uid, src=half * P, group=ugroups[half])
+            ctx.set_comm(bytes(uid.cpu().numpy()), role["urank"], P)
 
     sig = sigmas_fixed_shift(SCHED_STEPS, SHIFT)
-    job = rank // 2 if pair else rank
+    job = 0  # one denoising job over all ranks
     latent = Q.synth((1, 16, H_LAT, W_LAT), Q.seed_for(100 + job, "noise"), sig[0])
     lat_bf = latent.to(torch.bfloat16)
     ctxs = torch.stack([Q.synth((N_TXT, 3584), Q.seed_for(100 + job, f"context_{b}"), 1.0, dtype=torch.bfloat16)
@@ -176,10 +192,6 @@ def run_ours(args):
     my_ctx = ctxs if nb == 2 else ctxs[half:half + 1].contiguous()
     vel = torch.empty(nb, 16, H_LAT, W_LAT, dtype=torch.bfloat16, device="cuda")
     gathered = torch.empty(2, 16, H_LAT, W_LAT, dtype=torch.bfloat16, device="cuda")
-    group = None
-    if pair:
-        pairs = [torch.distributed.new_group([2 * p, 2 * p + 1]) for p in range(world // 2)]
-        group = pairs[rank // 2]
     stream = torch.cuda.current_stream()
 
     def step(i):
@@ -208,7 +220,7 @@ def run_ours(args):
         barrier(world)
     ms = e0.elapsed_time(e1) / args.steps
     ms = max_over_ranks(ms, world)
-    nprof = 12
+    nprof = 13
     import ctypes
     pl = (ctypes.c_int * nprof)()
     pm = (ctypes.c_float * nprof)()
@@ -256,13 +268,14 @@ def run_ours(args):
     gemm_stages = [2, 7, 8, 10]  # QI_PROF_GEMM_QKV, _OUT, _FC1, _FC2
     gemm_ms = sum(pm[i] for i in gemm_stages)
     gemm_n = sum(pl[i] for i in gemm_stages)
-    gemm_flops_total = lin_f * nb * args.steps  # every INT8 linear of the blocks runs in these launches
+    # every INT8 linear of this rank's tokens runs in these launches (1/P of the tokens)
+    gemm_flops_total = lin_f * nb * args.steps / P
     avg_launch_ms = gemm_ms / max(gemm_n, 1)
     achieved = gemm_flops_total / gemm_n / (avg_launch_ms * 1e-3) / 1e12 if gemm_n else None
     attn_ms = pm[5]
-    attn_tflops = attn_f * nb * args.steps / (attn_ms * 1e-3) / 1e12 if attn_ms > 0 else None
+    attn_tflops = attn_f * nb * args.steps / P / (attn_ms * 1e-3) / 1e12 if attn_ms > 0 else None
     stage_names = ["pre", "quant_ln", "gemm_qkv", "qkv_post", "sage_quant", "attention", "quant_o", "gemm_out",
-                   "gemm_fc1", "quant_h", "gemm_fc2", "post"]
+                   "gemm_fc1", "quant_h", "gemm_fc2", "post", "exchange"]
     stages = {n: {"launches": int(pl[i]), "ms_per_step": round(pm[i] / args.steps, 3)}
               for i, n in enumerate(stage_names)}
 
@@ -281,15 +294,15 @@ def run_ours(args):
         "warmup": args.warmup,
         "ms_per_step": round(ms, 3),
         "higher_is_better": False,
-        "scaling": "strong" if world <= 2 else "weak",
+        "scaling": "strong",
         "vs_baseline": None,
         "dtype": "int8",
         "data": "synthetic (seeded N(0,1) latents/text states; random-init N(0,0.02^2) weights quantized to INT8)",
         "config": {"workload": "C4: 1328x1328, 6889 img + 256 txt tokens, CFG cond+uncond, 60 blocks, W8A8 + "
                                "SageAttention (INT8 QK, FP16 PV)",
                    "latent": [16, H_LAT, W_LAT], "n_img": N_IMG, "n_txt": N_TXT, "blocks": BLOCKS,
-                   "cfg": "batched (nb=2) on 1 GPU" if world == 1 else "cond/uncond split over rank pairs",
-                   "parallelism": "single" if world == 1 else f"cfg2 x {world // 2} jobs",
+                   "cfg": "batched (nb=2) on 1 GPU" if world == 1 else "cond/uncond on two rank groups",
+                   "parallelism": "single" if world == 1 else ("cfg2" if P == 1 else f"cfg2 x ulysses{P}"),
                    "l2": "no flush: 20.4 GB of INT8 weights streamed per step >> 126 MB L2"},
         "e2e": {"value": round(e2e_ms / 1000.0, 5), "unit": "s/step", "h2d_bytes_per_step": bi,
                 "d2h_bytes_per_step": bo},

@@ -129,6 +129,26 @@ int qi_ctx_destroy(qi_ctx* ctx);
  * any kernel gave up a bounded wait since the last call.  Synchronous.      */
 int qi_ctx_check(qi_ctx* ctx);
 
+/* Head-parallel (Ulysses) group.  New: the reference runs on one GPU
+ * (its main.cu:761-773 calls transformer_forward for cond and uncond in
+ * turn).  One process (or context) per GPU; rank 0 makes the id and the
+ * caller hands it to the others (any channel); every rank then calls
+ * qi_ctx_set_comm with its rank (a collective: it returns when all nranks
+ * have joined).  nranks divides the 24 heads and is at most 8; nranks = 1
+ * leaves the context single-GPU.  With a group set, qi_forward takes the same
+ * full inputs on every rank, runs each linear on 1/nranks of the tokens and
+ * attention on 24/nranks heads (two all-to-all exchanges per block), and
+ * returns the full output on every rank.                                     */
+#define QI_COMM_ID_BYTES 128
+int qi_comm_unique_id(void* id_out);
+int qi_ctx_set_comm(qi_ctx* ctx, const void* id, int rank, int nranks);
+/* The per-peer byte offsets and sizes a rank uses in the two all-to-all
+ * exchanges of a head-parallel block (which = 0: Q/K/V before attention,
+ * which = 1: attention output after it), for a joint sequence of n_txt text
+ * and n_img image tokens per batch entry.  Host only; arrays of nranks. */
+int qi_exchange_plan(int which, int nb, int n_txt, int n_img, int nranks, int rank, long long* send_off,
+                     long long* send_bytes, long long* recv_off, long long* recv_bytes);
+
 /* Weight table in quantize.cu's format, one device pointer per tensor,
  * indexed by the enums below.  INT8 linears: codes I8 [N,K], scales F32 [N],
  * bias BF16 [N].  Boundary linears (img_in, txt_in, norm_out, proj_out):
@@ -218,6 +238,7 @@ enum {
   QI_PROF_QUANT_H,       /* fc2 input FWHT(4096) + INT8                         */
   QI_PROF_GEMM_FC2,      /* fc2 INT8 GEMM + gated residual                      */
   QI_PROF_POST,          /* output AdaLN, proj_out, unpatchify                  */
+  QI_PROF_EXCHANGE,      /* head-parallel all-to-all exchanges + reorders       */
   QI_PROF_COUNT
 };
 int qi_ctx_set_profiling(qi_ctx* ctx, int enable);

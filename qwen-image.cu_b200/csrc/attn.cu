@@ -79,6 +79,7 @@ struct alignas(64) AttnArgsDev {
   int BH, S, heads, out_mode, nb, n_img, n_txt, ngq, ngk;
   float qk_scale;  // sm_scale * log2(e)
   int* err;
+  ShardMap map;
 };
 
 // Not volatile: a pure function of its input, so the compiler may schedule
@@ -418,6 +419,22 @@ __global__ void __launch_bounds__(attn::THREADS, 1) sage_attn_kernel(const __gri
       const float rl = rcp_approx(l);
       const bool valid = qrow < S;
       const int b = bh / args.heads, h = bh % args.heads;
+      // out_mode 2: this row's slot in the send buffer of the rank that owns it
+      long long dst_off = 0;
+      if (args.out_mode == 2 && valid) {
+        const ShardMap& mp = args.map;
+        int dr = 0, lpos;
+        if (qrow < args.n_txt) {
+          while (dr + 1 < mp.P && mp.txt_lo[dr + 1] <= qrow) ++dr;
+          lpos = qrow - mp.txt_lo[dr];
+        } else {
+          const int gi = qrow - args.n_txt;
+          while (dr + 1 < mp.P && mp.img_lo[dr + 1] <= gi) ++dr;
+          lpos = mp.n_txt_l(dr) + gi - mp.img_lo[dr];
+        }
+        for (int q = 0; q < dr; ++q) dst_off += static_cast<long long>(args.nb) * mp.len(q) * args.heads * D;
+        dst_off += ((static_cast<long long>(b) * mp.len(dr) + lpos) * args.heads + h) * D;
+      }
 #pragma unroll 1
       for (int c = 0; c < D; c += 32) {
         uint32_t r[32];
@@ -434,6 +451,18 @@ __global__ void __launch_bounds__(attn::THREADS, 1) sage_attn_kernel(const __gri
             o.z = __half2float(__float2half_rn(__uint_as_float(r[i + 2]) * rl));
             o.w = __half2float(__float2half_rn(__uint_as_float(r[i + 3]) * rl));
             *reinterpret_cast<float4*>(dst + i) = o;
+          }
+        } else if (args.out_mode == 2) {
+          __half* dst = reinterpret_cast<__half*>(args.out) + dst_off + c;
+#pragma unroll
+          for (int i = 0; i < 32; i += 8) {
+            uint32_t pk[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              __half2 h2 = __floats2half2_rn(__uint_as_float(r[i + 2 * e]) * rl, __uint_as_float(r[i + 2 * e + 1]) * rl);
+              pk[e] = *reinterpret_cast<uint32_t*>(&h2);
+            }
+            *reinterpret_cast<uint4*>(dst + i) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
           }
         } else {
           const long long orow = (qrow < args.n_txt)
@@ -679,6 +708,8 @@ int attention_launch(const AttnArgs& a, cudaStream_t stream, int* err_dev) {
   d.ngk = ((a.S + 63) / 64) * 4;
   d.qk_scale = a.sm_scale * 1.44269504088896340736f;
   d.err = err_dev;
+  d.map = a.map;
+  if (a.out_mode == 2 && (a.map.P < 1 || a.map.P > kMaxRanks)) return QI_ERR_ARG;
   dim3 grid((a.S + attn::NT * attn::BQ - 1) / (attn::NT * attn::BQ), a.BH);
   sage_attn_kernel<<<grid, attn::THREADS, attn::smem_bytes(d.ngk), stream>>>(d);
   return cudaGetLastError() == cudaSuccess ? QI_OK : QI_ERR_CUDA;

@@ -15,10 +15,18 @@
 // The 120 modulation linears of a forward depend only on the timestep
 // (transformer.cu:506-515) and run as one GEMV over the stacked weights.
 // `nb` batch elements (CFG cond/uncond) share every launch.
+//
+// Head-parallel (Ulysses) forward over the P ranks of a communicator
+// (qi_ctx_set_comm): every rank runs the linears and norms of its share of
+// the text and image tokens; before attention the Q/K/V rows are exchanged
+// all-to-all so that each rank holds every token of 24/P heads, and the
+// attention output goes back the same way.  The exchanges are NCCL
+// point-to-point groups on the forward's stream.
 #include "qi_internal.h"
 #include "sm100.cuh"
 
 #include <cuda_bf16.h>
+#include <nccl.h>
 
 #include <map>
 #include <mutex>
@@ -70,13 +78,16 @@ static inline cudaStream_t S_(void* s) { return reinterpret_cast<cudaStream_t>(s
 // ------------------------------------------------------------------ context
 enum BufId {
   B_PATCH, B_TEMB256, B_TACT, B_TACT_S, B_T1, B_TEMB, B_TSILU, B_MODS, B_ADA, B_X, B_TXTN, B_ACT, B_ACT_S, B_QKV,
-  B_QH, B_KH, B_VH, B_QC, B_KC, B_QS, B_KS, B_KMEAN, B_O, B_H, B_FIN, B_PROJ, B_COUNT
+  B_QKVH, B_QC, B_KC, B_QS, B_KS, B_KMEAN, B_O, B_H, B_FIN, B_PROJ, B_SEND1, B_RECV1, B_SEND2, B_RECV2,
+  B_PROJF, B_COUNT
 };
 
 struct qi_ctx {
   int device = 0;
   int num_sms = 148;
   int* err = nullptr;  // device error word
+  ncclComm_t comm = nullptr;  // head-parallel group (qi_ctx_set_comm)
+  int urank = 0, usize = 1;
   void* buf[B_COUNT] = {};
   size_t cap[B_COUNT] = {};
   int launches = 0;
@@ -192,7 +203,39 @@ int qi_ctx_destroy(qi_ctx* c) {
   for (int i = 0; i < B_COUNT; ++i)
     if (c->buf[i]) cudaFree(c->buf[i]);
   if (c->err) cudaFree(c->err);
+  if (c->comm) ncclCommDestroy(c->comm);
   delete c;
+  return QI_OK;
+}
+
+int qi_comm_unique_id(void* id_out) {
+  if (!id_out) return QI_ERR_ARG;
+  static_assert(sizeof(ncclUniqueId) == QI_COMM_ID_BYTES, "NCCL unique id size");
+  ncclUniqueId id;
+  if (ncclGetUniqueId(&id) != ncclSuccess) return QI_ERR_NCCL;
+  memcpy(id_out, &id, sizeof(id));
+  return QI_OK;
+}
+
+int qi_ctx_set_comm(qi_ctx* c, const void* id, int rank, int nranks) {
+  if (!c || nranks < 1 || nranks > kMaxRanks || kHeads % nranks || rank < 0 || rank >= nranks) return QI_ERR_ARG;
+  if (c->comm) {
+    ncclCommDestroy(c->comm);
+    c->comm = nullptr;
+  }
+  c->urank = 0;
+  c->usize = 1;
+  if (nranks == 1) return QI_OK;
+  if (!id) return QI_ERR_ARG;
+  if (cudaSetDevice(c->device) != cudaSuccess) return QI_ERR_CUDA;
+  ncclUniqueId uid;
+  memcpy(&uid, id, sizeof(uid));
+  if (ncclCommInitRank(&c->comm, nranks, uid, rank) != ncclSuccess) {
+    c->comm = nullptr;
+    return QI_ERR_NCCL;
+  }
+  c->urank = rank;
+  c->usize = nranks;
   return QI_OK;
 }
 
@@ -487,14 +530,73 @@ extern "C" int qi_model_create(qi_ctx* ctx, int num_blocks, const void* const* g
 }
 
 // ------------------------------------------------------------------ forward
-// Shapes and workspace views of one forward; the stages below share it.
 namespace {
+// Even split of the text and of the image tokens over P ranks.
+ShardMap make_map(int P, int n_txt, int n_img) {
+  ShardMap mp;
+  memset(&mp, 0, sizeof(mp));
+  mp.P = P;
+  for (int r = 0; r <= P; ++r) {
+    mp.txt_lo[r] = static_cast<int>(static_cast<long long>(r) * n_txt / P);
+    mp.img_lo[r] = static_cast<int>(static_cast<long long>(r) * n_img / P);
+  }
+  return mp;
+}
+
+// Byte offsets and sizes, per peer, of the two all-to-all exchanges of a
+// head-parallel block (FP16 rows of 128):
+//   which 0 (Q/K/V): rank r sends peer q [3][nb][Hl][len(r)][128] from offset
+//     q * that size, and receives [3][nb][Hl][len(q)][128] packed by q;
+//   which 1 (attention output): rank r sends peer q [nb][len(q)][Hl][128],
+//     packed by q, and receives [nb][len(r)][Hl][128] at offset q * that size.
+void exchange_plan(int which, int nb, const ShardMap& mp, int rank, long long* soff, long long* sbytes,
+                   long long* roff, long long* rbytes) {
+  const long long Hl = kHeads / mp.P, row = kHeadDim * 2;
+  long long so = 0, ro = 0;
+  for (int q = 0; q < mp.P; ++q) {
+    if (which == 0) {
+      sbytes[q] = 3LL * nb * Hl * mp.len(rank) * row;
+      rbytes[q] = 3LL * nb * Hl * mp.len(q) * row;
+    } else {
+      sbytes[q] = static_cast<long long>(nb) * mp.len(q) * Hl * row;
+      rbytes[q] = static_cast<long long>(nb) * mp.len(rank) * Hl * row;
+    }
+    soff[q] = so;
+    roff[q] = ro;
+    so += sbytes[q];
+    ro += rbytes[q];
+  }
+}
+
+// All-to-all with per-peer sizes on `s`: NCCL send/recv pairs in one group,
+// the rank's own chunk as a device copy.
+int exchange(qi_ctx* c, int which, int nb, const ShardMap& mp, const void* send, void* recv, cudaStream_t s) {
+  long long so[kMaxRanks], sb[kMaxRanks], ro[kMaxRanks], rb[kMaxRanks];
+  exchange_plan(which, nb, mp, c->urank, so, sb, ro, rb);
+  const char* sp = static_cast<const char*>(send);
+  char* rp = static_cast<char*>(recv);
+  const int me = c->urank;
+  if (sb[me] && cudaMemcpyAsync(rp + ro[me], sp + so[me], sb[me], cudaMemcpyDeviceToDevice, s) != cudaSuccess)
+    return QI_ERR_CUDA;
+  if (ncclGroupStart() != ncclSuccess) return QI_ERR_NCCL;
+  for (int q = 0; q < mp.P; ++q) {
+    if (q == me) continue;
+    if (sb[q] && ncclSend(sp + so[q], sb[q], ncclUint8, q, c->comm, s) != ncclSuccess) return QI_ERR_NCCL;
+    if (rb[q] && ncclRecv(rp + ro[q], rb[q], ncclUint8, q, c->comm, s) != ncclSuccess) return QI_ERR_NCCL;
+  }
+  return ncclGroupEnd() == ncclSuccess ? QI_OK : QI_ERR_NCCL;
+}
+
+// Shapes and workspace views of one forward; the stages below share it.
 struct Fwd {
   qi_ctx* c;
   const qi_model* m;
   cudaStream_t s;
   int nb, n_img, n_txt, S, BH;
-  long long Mi, Mt, Ma;
+  int P = 1, rank = 0, Hl = kHeads;  // head-parallel group
+  ShardMap map;
+  int img_lo = 0, n_img_l = 0, txt_lo = 0, n_txt_l = 0;  // this rank's tokens
+  long long Mi, Mt, Ma;  // this rank's image / text / all rows (nb entries)
   int n = 0;  // launches issued
 };
 
@@ -525,9 +627,17 @@ int fwd_init(Fwd& f, qi_ctx* c, const qi_model* m, int nb, int n_img, int n_txt,
   f.n_img = n_img;
   f.n_txt = n_txt;
   f.S = n_img + n_txt;
-  f.BH = nb * kHeads;
-  f.Mi = static_cast<long long>(nb) * n_img;
-  f.Mt = static_cast<long long>(nb) * n_txt;
+  f.P = c->usize;
+  f.rank = c->urank;
+  f.Hl = kHeads / f.P;
+  f.map = make_map(f.P, n_txt, n_img);
+  f.img_lo = f.map.img_lo[f.rank];
+  f.n_img_l = f.map.n_img_l(f.rank);
+  f.txt_lo = f.map.txt_lo[f.rank];
+  f.n_txt_l = f.map.n_txt_l(f.rank);
+  f.BH = nb * f.Hl;
+  f.Mi = static_cast<long long>(nb) * f.n_img_l;
+  f.Mt = static_cast<long long>(nb) * f.n_txt_l;
   f.Ma = f.Mi + f.Mt;
   const size_t hs = static_cast<size_t>(f.BH) * f.S * kHeadDim;
   QI_TRY(c->ensure(B_PATCH, f.Mi * kPatchDim * 2));
@@ -544,9 +654,7 @@ int fwd_init(Fwd& f, qi_ctx* c, const qi_model* m, int nb, int n_img, int n_txt,
   QI_TRY(c->ensure(B_ACT, f.Ma * kMlp));
   QI_TRY(c->ensure(B_ACT_S, f.Ma * 4));
   QI_TRY(c->ensure(B_QKV, f.Ma * 3 * kDim * 4));
-  QI_TRY(c->ensure(B_QH, hs * 2));
-  QI_TRY(c->ensure(B_KH, hs * 2));
-  QI_TRY(c->ensure(B_VH, hs * 2));
+  QI_TRY(c->ensure(B_QKVH, 3 * hs * 2));
   QI_TRY(c->ensure(B_QC, hs));
   QI_TRY(c->ensure(B_KC, hs));
   QI_TRY(c->ensure(B_QS, static_cast<size_t>(f.BH) * ((f.S + 127) / 128) * 32 * 4));
@@ -556,6 +664,13 @@ int fwd_init(Fwd& f, qi_ctx* c, const qi_model* m, int nb, int n_img, int n_txt,
   QI_TRY(c->ensure(B_H, f.Ma * kMlp * 4));
   QI_TRY(c->ensure(B_FIN, f.Mi * kDim * 2));
   QI_TRY(c->ensure(B_PROJ, f.Mi * kPatchDim * 4));
+  if (f.P > 1) {
+    QI_TRY(c->ensure(B_SEND1, f.Ma * 3 * kDim * 2));
+    QI_TRY(c->ensure(B_RECV1, 3 * hs * 2));
+    QI_TRY(c->ensure(B_SEND2, hs * 2));
+    QI_TRY(c->ensure(B_RECV2, f.Ma * kDim * 2));
+    QI_TRY(c->ensure(B_PROJF, static_cast<size_t>(nb) * n_img * kPatchDim * 4));
+  }
   return QI_OK;
 }
 
@@ -593,13 +708,26 @@ int fwd_inputs(Fwd& f, const void* x, const void* ctx_txt, int H, int W, float* 
   qi_ctx* c = f.c;
   const qi_model* m = f.m;
   cudaStream_t s = f.s;
-  QI_LAUNCH(QI_PROF_PRE, 1, patchify_launch(x, c->buf[B_PATCH], f.nb, H, W, s));
-  GemmBf16Desc d{c->buf[B_PATCH], m->img_in_w, m->img_in_b, x_img, static_cast<int>(f.Mi), kDim, kPatchDim, kDim};
-  QI_LAUNCH(QI_PROF_PRE, 1, gemm_bf16_launch(d, s, c->err, c->num_sms));
-  QI_LAUNCH(QI_PROF_PRE, 1,
-            rmsnorm_bf16_launch(ctx_txt, m->txt_norm, c->buf[B_TXTN], static_cast<int>(f.Mt), kTxtDim, 1e-6f, s));
-  GemmBf16Desc e{c->buf[B_TXTN], m->txt_in_w, m->txt_in_b, x_txt, static_cast<int>(f.Mt), kDim, kTxtDim, kDim};
-  QI_LAUNCH(QI_PROF_PRE, 1, gemm_bf16_launch(e, s, c->err, c->num_sms));
+  // this rank's image patches and text rows of every batch entry
+  QI_LAUNCH(QI_PROF_PRE, 1, patchify_launch(x, c->buf[B_PATCH], f.nb, H, W, f.img_lo, f.n_img_l, s));
+  if (f.Mi > 0) {
+    GemmBf16Desc d{c->buf[B_PATCH], m->img_in_w, m->img_in_b, x_img, static_cast<int>(f.Mi), kDim, kPatchDim, kDim};
+    QI_LAUNCH(QI_PROF_PRE, 1, gemm_bf16_launch(d, s, c->err, c->num_sms));
+  }
+  if (f.Mt > 0) {
+    const __nv_bfloat16* ctx_in = static_cast<const __nv_bfloat16*>(ctx_txt);
+    __nv_bfloat16* txtn = c->p<__nv_bfloat16>(B_TXTN);
+    if (f.P == 1) {
+      QI_LAUNCH(QI_PROF_PRE, 1, rmsnorm_bf16_launch(ctx_in, m->txt_norm, txtn, static_cast<int>(f.Mt), kTxtDim, 1e-6f, s));
+    } else {
+      for (int b = 0; b < f.nb; ++b)
+        QI_LAUNCH(QI_PROF_PRE, 1,
+                  rmsnorm_bf16_launch(ctx_in + (static_cast<size_t>(b) * f.n_txt + f.txt_lo) * kTxtDim, m->txt_norm,
+                                      txtn + static_cast<size_t>(b) * f.n_txt_l * kTxtDim, f.n_txt_l, kTxtDim, 1e-6f, s));
+    }
+    GemmBf16Desc e{c->buf[B_TXTN], m->txt_in_w, m->txt_in_b, x_txt, static_cast<int>(f.Mt), kDim, kTxtDim, kDim};
+    QI_LAUNCH(QI_PROF_PRE, 1, gemm_bf16_launch(e, s, c->err, c->num_sms));
+  }
   return QI_OK;
 }
 
@@ -611,6 +739,7 @@ int fwd_blocks(Fwd& f, float* x_img, float* x_txt, const float* pe, int b0, int 
   cudaStream_t s = f.s;
   const long long Mi = f.Mi, Mt = f.Mt, Ma = f.Ma;
   const int nb = f.nb, n_img = f.n_img, n_txt = f.n_txt, S = f.S, BH = f.BH;
+  if (Ma == 0) return QI_ERR_UNSUPPORTED;
   int8_t* act = c->p<int8_t>(B_ACT);
   float* act_s = c->p<float>(B_ACT_S);
   const float* mods = c->p<float>(B_MODS);
@@ -629,15 +758,28 @@ int fwd_blocks(Fwd& f, float* x_img, float* x_txt, const float* pe, int b0, int 
                       {act + Mi * kDim, act_s + Mi, B.qkv[1].w, B.qkv[1].s, B.qkv[1].b, qkv + Mi * 3 * kDim, nullptr,
                        static_cast<int>(Mt), 3 * kDim, kDim, 3 * kDim}};
     QI_LAUNCH(QI_PROF_GEMM_QKV, 1, gemm_i8_launch(gq, 2, kEpiStore, s, c->err, c->num_sms));
-    QkvPostArgs qa{qkv, qkv + Mi * 3 * kDim, B.norms, B.norms + kHeadDim, B.norms + 2 * kHeadDim,
-                   B.norms + 3 * kHeadDim, pe, c->buf[B_QH], c->buf[B_KH], c->buf[B_VH], nb, n_img, n_txt};
+    const bool par = f.P > 1;
+    __half* qkvh = c->p<__half>(B_QKVH);
+    const size_t hs = static_cast<size_t>(BH) * S * kHeadDim;
+    QkvPostArgs qa{qkv,       qkv + Mi * 3 * kDim, B.norms, B.norms + kHeadDim, B.norms + 2 * kHeadDim,
+                   B.norms + 3 * kHeadDim, pe, par ? c->buf[B_SEND1] : qkvh, nb, n_img, n_txt, f.img_lo, f.n_img_l,
+                   f.txt_lo, f.n_txt_l, f.Hl};
     QI_LAUNCH(QI_PROF_QKV_POST, 1, qkv_post_launch(qa, s));
+    if (par) {  // every token of this rank's heads
+      QI_LAUNCH(QI_PROF_EXCHANGE, 0, exchange(c, 0, nb, f.map, c->buf[B_SEND1], c->buf[B_RECV1], s));
+      QI_LAUNCH(QI_PROF_EXCHANGE, 1, ulysses_gather_qkv_launch(c->buf[B_RECV1], qkvh, nb, f.Hl, n_txt, f.map, s));
+    }
     QI_LAUNCH(QI_PROF_SAGE_QUANT, 3,
-              sage_quantize_launch(c->buf[B_QH], c->buf[B_KH], BH, S, c->p<float>(B_KMEAN), c->p<int8_t>(B_QC),
+              sage_quantize_launch(qkvh, qkvh + hs, BH, S, c->p<float>(B_KMEAN), c->p<int8_t>(B_QC),
                                    c->p<float>(B_QS), c->p<int8_t>(B_KC), c->p<float>(B_KS), s));
-    AttnArgs aa{c->p<int8_t>(B_QC), c->p<float>(B_QS), c->p<int8_t>(B_KC), c->p<float>(B_KS), c->buf[B_VH],
-                c->buf[B_O], BH, S, kHeads, 1.0f / sqrtf(128.0f), 1, nb, n_img, n_txt};
+    AttnArgs aa{c->p<int8_t>(B_QC), c->p<float>(B_QS), c->p<int8_t>(B_KC), c->p<float>(B_KS), qkvh + 2 * hs,
+                par ? c->buf[B_SEND2] : c->buf[B_O], BH, S, f.Hl, 1.0f / sqrtf(128.0f), par ? 2 : 1, nb, n_img, n_txt,
+                f.map};
     QI_LAUNCH(QI_PROF_ATTENTION, 1, attention_launch(aa, s, c->err));
+    if (par) {  // back to the token owners, token-major
+      QI_LAUNCH(QI_PROF_EXCHANGE, 0, exchange(c, 1, nb, f.map, c->buf[B_SEND2], c->buf[B_RECV2], s));
+      QI_LAUNCH(QI_PROF_EXCHANGE, 1, ulysses_gather_o_launch(c->buf[B_RECV2], c->buf[B_O], nb, f.Hl, f.rank, f.map, s));
+    }
     RowSeg os{c->buf[B_O], kDim, nullptr, nullptr, static_cast<int>(Ma)};
     QI_LAUNCH(QI_PROF_QUANT_O, 1, rowquant_launch(kSrcF16, kDim, 1024, &os, 1, act, act_s, 0.0f, s));
     GemmDesc go[2] = {{act, act_s, B.out[0].w, B.out[0].s, B.out[0].b, x_img, mi + 2 * kDim, static_cast<int>(Mi), kDim,
@@ -673,14 +815,51 @@ int fwd_output(Fwd& f, const float* x_img, int H, int W, void* out) {
   const float* ada = c->p<float>(B_ADA);
   QI_LAUNCH(QI_PROF_POST, 1,
             layernorm_mod_launch(x_img, ada + kDim, ada, static_cast<int>(f.Mi), kDim, 1e-6f, nullptr, c->buf[B_FIN], s));
-  GemmBf16Desc pd{c->buf[B_FIN], m->proj_out_w, m->proj_out_b, c->p<float>(B_PROJ), static_cast<int>(f.Mi), kPatchDim,
-                  kDim, kPatchDim};
-  QI_LAUNCH(QI_PROF_POST, 1, gemm_bf16_launch(pd, s, c->err, c->num_sms));
-  QI_LAUNCH(QI_PROF_POST, 1, unpatchify_launch(c->p<float>(B_PROJ), out, f.nb, H, W, s));
+  if (f.Mi > 0) {
+    GemmBf16Desc pd{c->buf[B_FIN], m->proj_out_w, m->proj_out_b, c->p<float>(B_PROJ), static_cast<int>(f.Mi),
+                    kPatchDim, kDim, kPatchDim};
+    QI_LAUNCH(QI_PROF_POST, 1, gemm_bf16_launch(pd, s, c->err, c->num_sms));
+  }
+  const float* proj = c->p<float>(B_PROJ);
+  if (f.P > 1) {  // every rank's image rows, for the full output on every rank
+    float* full = c->p<float>(B_PROJF);
+    const size_t rowb = kPatchDim * sizeof(float);
+    for (int b = 0; b < f.nb; ++b)
+      if (f.n_img_l &&
+          cudaMemcpyAsync(full + (static_cast<size_t>(b) * f.n_img + f.img_lo) * kPatchDim,
+                          proj + static_cast<size_t>(b) * f.n_img_l * kPatchDim, f.n_img_l * rowb,
+                          cudaMemcpyDeviceToDevice, s) != cudaSuccess)
+        return QI_ERR_CUDA;
+    if (ncclGroupStart() != ncclSuccess) return QI_ERR_NCCL;
+    for (int q = 0; q < f.P; ++q) {
+      if (q == f.rank) continue;
+      const int nq = f.map.n_img_l(q);
+      for (int b = 0; b < f.nb; ++b) {
+        if (f.n_img_l && ncclSend(proj + static_cast<size_t>(b) * f.n_img_l * kPatchDim,
+                                  static_cast<size_t>(f.n_img_l) * kPatchDim, ncclFloat32, q, c->comm, s) != ncclSuccess)
+          return QI_ERR_NCCL;
+        if (nq && ncclRecv(full + (static_cast<size_t>(b) * f.n_img + f.map.img_lo[q]) * kPatchDim,
+                           static_cast<size_t>(nq) * kPatchDim, ncclFloat32, q, c->comm, s) != ncclSuccess)
+          return QI_ERR_NCCL;
+      }
+    }
+    if (ncclGroupEnd() != ncclSuccess) return QI_ERR_NCCL;
+    proj = full;
+  }
+  QI_LAUNCH(QI_PROF_POST, 1, unpatchify_launch(proj, out, f.nb, H, W, s));
   return QI_OK;
 }
 #undef QI_LAUNCH
 }  // namespace
+
+extern "C" int qi_exchange_plan(int which, int nb, int n_txt, int n_img, int nranks, int rank, long long* send_off,
+                                long long* send_bytes, long long* recv_off, long long* recv_bytes) {
+  if ((which != 0 && which != 1) || nb < 1 || n_txt < 0 || n_img < 0 || nranks < 1 || nranks > kMaxRanks ||
+      kHeads % nranks || rank < 0 || rank >= nranks || !send_off || !send_bytes || !recv_off || !recv_bytes)
+    return QI_ERR_ARG;
+  exchange_plan(which, nb, make_map(nranks, n_txt, n_img), rank, send_off, send_bytes, recv_off, recv_bytes);
+  return QI_OK;
+}
 
 extern "C" int qi_forward(qi_ctx* c, const qi_model* m, int nb, const void* x, float timestep, const void* ctx_txt,
                           int n_txt, const float* pe, int H, int W, void* out, void* stream) {
@@ -704,6 +883,7 @@ extern "C" int qi_forward_blocks(qi_ctx* c, const qi_model* m, int nb, int n_img
   if (nb < 1 || nb > 8 || n_img < 1 || n_txt < 1 || block_begin < 0 || block_end > m->nblocks ||
       block_begin > block_end)
     return QI_ERR_ARG;
+  if (c->usize > 1) return QI_ERR_UNSUPPORTED;  // the caller-owned streams are whole sequences
   if ((reinterpret_cast<uintptr_t>(img) & 15) || (reinterpret_cast<uintptr_t>(txt) & 15)) return QI_ERR_ALIGN;
   Fwd f;
   QI_TRY(fwd_init(f, c, m, nb, n_img, n_txt, stream));

@@ -40,26 +40,31 @@ __global__ void qkv_post_kernel(QkvPostArgs a) {
   const int warps = blockDim.x >> 5;
   const long long gw = static_cast<long long>(blockIdx.x) * warps + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
-  const long long rows_img = static_cast<long long>(a.nb) * a.n_img;
-  const long long rows = rows_img + static_cast<long long>(a.nb) * a.n_txt;
+  const long long rows_img = static_cast<long long>(a.nb) * a.n_img_l;
+  const long long rows = rows_img + static_cast<long long>(a.nb) * a.n_txt_l;
   if (gw >= rows * kHeads) return;
   const long long r = gw / kHeads;
   const int h = static_cast<int>(gw % kHeads);
   const int S = a.n_img + a.n_txt;
+  const int L = a.n_img_l + a.n_txt_l;  // local sequence length
   const float* src;
-  int b, pos;
+  int b, pos, lpos;                     // batch entry, joint position, local position
   const __nv_bfloat16 *wq, *wk;
   if (r < rows_img) {
     src = a.qkv_img + r * (3 * kDim);
-    b = static_cast<int>(r / a.n_img);
-    pos = a.n_txt + static_cast<int>(r % a.n_img);
+    b = static_cast<int>(r / a.n_img_l);
+    const int i = static_cast<int>(r % a.n_img_l);
+    pos = a.n_txt + a.img_lo + i;
+    lpos = a.n_txt_l + i;
     wq = reinterpret_cast<const __nv_bfloat16*>(a.nq_img);
     wk = reinterpret_cast<const __nv_bfloat16*>(a.nk_img);
   } else {
     const long long rt = r - rows_img;
     src = a.qkv_txt + rt * (3 * kDim);
-    b = static_cast<int>(rt / a.n_txt);
-    pos = static_cast<int>(rt % a.n_txt);
+    b = static_cast<int>(rt / a.n_txt_l);
+    const int t = static_cast<int>(rt % a.n_txt_l);
+    pos = a.txt_lo + t;
+    lpos = t;
     wq = reinterpret_cast<const __nv_bfloat16*>(a.nq_txt);
     wk = reinterpret_cast<const __nv_bfloat16*>(a.nk_txt);
   }
@@ -70,7 +75,11 @@ __global__ void qkv_post_kernel(QkvPostArgs a) {
   const float* pe = a.pe + (static_cast<long long>(b) * S + pos) * 256 + lane * 8;
   const float4 pe0 = __ldg(reinterpret_cast<const float4*>(pe));
   const float4 pe1 = __ldg(reinterpret_cast<const float4*>(pe + 4));
-  const size_t dst = ((static_cast<size_t>(b) * kHeads + h) * S + pos) * kHeadDim + d0;
+  const int dest = h / a.Hl, hh = h % a.Hl;
+  // qkvh[dest][which][b][hh][lpos][128]; `which` adds one (nb * Hl * L * 128) slab
+  const size_t slab = static_cast<size_t>(a.nb) * a.Hl * L * kHeadDim;
+  const size_t dst = static_cast<size_t>(dest) * 3 * slab + ((static_cast<size_t>(b) * a.Hl + hh) * L + lpos) * kHeadDim + d0;
+  __half* base = reinterpret_cast<__half*>(a.qkvh);
 
   auto norm_rope = [&](float4 x, const __nv_bfloat16* w, __half* out) {
     float ss = x.x * x.x + x.y * x.y + x.z * x.z + x.w * x.w;
@@ -91,13 +100,71 @@ __global__ void qkv_post_kernel(QkvPostArgs a) {
     pk.y = *reinterpret_cast<uint32_t*>(&h23);
     *reinterpret_cast<uint2*>(out + dst) = pk;
   };
-  norm_rope(qv, wq, reinterpret_cast<__half*>(a.q));
-  norm_rope(kv, wk, reinterpret_cast<__half*>(a.k));
+  norm_rope(qv, wq, base);
+  norm_rope(kv, wk, base + slab);
   __half2 v01 = __floats2half2_rn(vv.x, vv.y), v23 = __floats2half2_rn(vv.z, vv.w);
   uint2 pv;
   pv.x = *reinterpret_cast<uint32_t*>(&v01);
   pv.y = *reinterpret_cast<uint32_t*>(&v23);
-  *reinterpret_cast<uint2*>(reinterpret_cast<__half*>(a.v) + dst) = pv;
+  *reinterpret_cast<uint2*>(base + 2 * slab + dst) = pv;
+}
+
+// Received Q/K/V of this rank's heads, [src][3][nb][Hl][len(src)][128], into
+// [3][nb*Hl][S][128] in the joint order: one 256-byte row per thread group of
+// 16 (16 bytes each).
+__global__ void ulysses_gather_qkv_kernel(const uint4* __restrict__ recv, uint4* __restrict__ out, int nb, int Hl,
+                                          int n_txt, ShardMap map) {
+  const int S = map.txt_lo[map.P] + map.img_lo[map.P];
+  const long long total = 3LL * nb * Hl * S * 16;  // 16-byte pieces of the output
+  for (long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; idx < total;
+       idx += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int piece = static_cast<int>(idx & 15);
+    const long long row = idx >> 4;  // [which][b][hh][pos]
+    const int pos = static_cast<int>(row % S);
+    const long long wbh = row / S;   // (which * nb + b) * Hl + hh
+    // owner of the joint position and its local index there
+    int src = 0, lpos;
+    if (pos < n_txt) {
+      while (src + 1 < map.P && map.txt_lo[src + 1] <= pos) ++src;
+      lpos = pos - map.txt_lo[src];
+    } else {
+      const int gi = pos - n_txt;
+      while (src + 1 < map.P && map.img_lo[src + 1] <= gi) ++src;
+      lpos = map.n_txt_l(src) + gi - map.img_lo[src];
+    }
+    long long off = 0;  // start of src's chunk, in 128-element rows
+    for (int q = 0; q < src; ++q) off += 3LL * nb * Hl * map.len(q);
+    const long long in_row = off + wbh * map.len(src) + lpos;
+    out[idx] = recv[in_row * 16 + piece];
+  }
+}
+
+// Received attention output, [src][nb][len(r)][Hl][128] (src's heads), into
+// this rank's token-major rows: image rows [nb][n_img_l] then text rows
+// [nb][n_txt_l], each [24 heads][128] with head = src * Hl + hh.
+__global__ void ulysses_gather_o_kernel(const uint4* __restrict__ recv, uint4* __restrict__ out, int nb, int Hl,
+                                        int rank, ShardMap map) {
+  const int nt = map.n_txt_l(rank), ni = map.n_img_l(rank), L = nt + ni;
+  const long long rows = static_cast<long long>(nb) * L;
+  const long long total = rows * kHeads * 16;
+  for (long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; idx < total;
+       idx += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int piece = static_cast<int>(idx & 15);
+    const int h = static_cast<int>((idx >> 4) % kHeads);
+    const long long orow = (idx >> 4) / kHeads;
+    int b, lpos;
+    if (orow < static_cast<long long>(nb) * ni) {
+      b = static_cast<int>(orow / ni);
+      lpos = nt + static_cast<int>(orow % ni);
+    } else {
+      const long long t = orow - static_cast<long long>(nb) * ni;
+      b = static_cast<int>(t / nt);
+      lpos = static_cast<int>(t % nt);
+    }
+    const int src = h / Hl, hh = h % Hl;
+    const long long in_row = ((static_cast<long long>(src) * nb + b) * L + lpos) * Hl + hh;
+    out[idx] = recv[in_row * 16 + piece];
+  }
 }
 
 // ------------------------------------------------------------------ GEMV
@@ -180,15 +247,15 @@ __global__ void silu_kernel(const float* x, float* out, int n) {
 
 // patchify_kernel (cuda_kernels.cu:1244-1272) for N latents, 2x2 patches.
 __global__ void patchify_kernel(const __nv_bfloat16* __restrict__ in, __nv_bfloat16* __restrict__ out, int nb, int H,
-                                int W) {
+                                int W, int p_lo, int n_loc) {
   const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
-  const int wp_n = W / 2, n_p = (H / 2) * wp_n;
-  const long long total = static_cast<long long>(nb) * n_p * kPatchDim;
+  const int wp_n = W / 2;
+  const long long total = static_cast<long long>(nb) * n_loc * kPatchDim;
   if (idx >= total) return;
   const int d = static_cast<int>(idx % kPatchDim);
   const long long rest = idx / kPatchDim;
-  const int p = static_cast<int>(rest % n_p);
-  const int n = static_cast<int>(rest / n_p);
+  const int p = p_lo + static_cast<int>(rest % n_loc);
+  const int n = static_cast<int>(rest / n_loc);
   const int hp = p / wp_n, wp = p % wp_n;
   const int c = d / 4, dh = (d % 4) / 2, dw = d % 2;
   out[idx] = in[(static_cast<long long>(n) * kOutCh + c) * H * W + static_cast<long long>(hp * 2 + dh) * W + wp * 2 + dw];
@@ -311,7 +378,8 @@ __global__ void rmsnorm_kernel(const T* x, const __nv_bfloat16* w, T* out, int d
 static int ok_or_err() { return cudaGetLastError() == cudaSuccess ? QI_OK : QI_ERR_CUDA; }
 
 int qkv_post_launch(const QkvPostArgs& a, cudaStream_t stream) {
-  const long long items = static_cast<long long>(a.nb) * (a.n_img + a.n_txt) * kHeads;
+  if (a.Hl <= 0 || kHeads % a.Hl) return QI_ERR_ARG;
+  const long long items = static_cast<long long>(a.nb) * (a.n_img_l + a.n_txt_l) * kHeads;
   if (items == 0) return QI_OK;
   const int threads = 256;
   const long long blocks = (items + 7) / 8;
@@ -352,10 +420,40 @@ int silu_launch(const float* x, float* out, int n, cudaStream_t stream) {
   return ok_or_err();
 }
 
-int patchify_launch(const void* x_bf16, void* patches_bf16, int nb, int H, int W, cudaStream_t stream) {
-  const long long total = static_cast<long long>(nb) * (H / 2) * (W / 2) * kPatchDim;
+int patchify_launch(const void* x_bf16, void* patches_bf16, int nb, int H, int W, int p_lo, int n_loc,
+                    cudaStream_t stream) {
+  if (p_lo < 0 || n_loc < 0 || p_lo + n_loc > (H / 2) * (W / 2)) return QI_ERR_ARG;
+  const long long total = static_cast<long long>(nb) * n_loc * kPatchDim;
+  if (total == 0) return QI_OK;
   patchify_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, stream>>>(
-      reinterpret_cast<const __nv_bfloat16*>(x_bf16), reinterpret_cast<__nv_bfloat16*>(patches_bf16), nb, H, W);
+      reinterpret_cast<const __nv_bfloat16*>(x_bf16), reinterpret_cast<__nv_bfloat16*>(patches_bf16), nb, H, W, p_lo,
+      n_loc);
+  return ok_or_err();
+}
+
+static unsigned grid_for(long long total) {
+  long long g = (total + 255) / 256;
+  if (g > 148LL * 16) g = 148LL * 16;
+  return static_cast<unsigned>(g < 1 ? 1 : g);
+}
+
+int ulysses_gather_qkv_launch(const void* recv, void* qkvh, int nb, int Hl, int n_txt, const ShardMap& map,
+                              cudaStream_t stream) {
+  if (map.P < 1 || map.P > kMaxRanks || Hl <= 0) return QI_ERR_ARG;
+  const long long S = map.txt_lo[map.P] + map.img_lo[map.P];
+  const long long total = 3LL * nb * Hl * S * 16;
+  ulysses_gather_qkv_kernel<<<grid_for(total), 256, 0, stream>>>(reinterpret_cast<const uint4*>(recv),
+                                                                 reinterpret_cast<uint4*>(qkvh), nb, Hl, n_txt, map);
+  return ok_or_err();
+}
+
+int ulysses_gather_o_launch(const void* recv, void* out, int nb, int Hl, int rank, const ShardMap& map,
+                            cudaStream_t stream) {
+  if (map.P < 1 || map.P > kMaxRanks || Hl <= 0 || rank < 0 || rank >= map.P) return QI_ERR_ARG;
+  const long long total = static_cast<long long>(nb) * map.len(rank) * kHeads * 16;
+  if (total == 0) return QI_OK;
+  ulysses_gather_o_kernel<<<grid_for(total), 256, 0, stream>>>(reinterpret_cast<const uint4*>(recv),
+                                                               reinterpret_cast<uint4*>(out), nb, Hl, rank, map);
   return ok_or_err();
 }
 

@@ -34,6 +34,20 @@ inline int smem_optin(const void* fn, int bytes, unsigned long long* done) {
   return QI_OK;
 }
 
+// Sequence split of the joint [txt; img] sequence over the P ranks of a
+// head-parallel (Ulysses) group: rank r owns text tokens [txt_lo[r],
+// txt_lo[r+1]) and image tokens [img_lo[r], img_lo[r+1]) of every batch entry.
+// Its local sequence is its text tokens followed by its image tokens.
+constexpr int kMaxRanks = 8;
+struct ShardMap {
+  int P;
+  int txt_lo[kMaxRanks + 1];
+  int img_lo[kMaxRanks + 1];
+  __host__ __device__ int n_txt_l(int r) const { return txt_lo[r + 1] - txt_lo[r]; }
+  __host__ __device__ int n_img_l(int r) const { return img_lo[r + 1] - img_lo[r]; }
+  __host__ __device__ int len(int r) const { return n_txt_l(r) + n_img_l(r); }
+};
+
 // ---------------------------------------------------------------- GEMMs
 // INT8: out = acc * sa[m] * sw[n] + bias[n] (+ epilogue).  a [M,K], w [N,K].
 struct GemmDesc {
@@ -101,24 +115,40 @@ int gemv_bf16_launch(const float* x, const void* w, const void* bias, float* out
 // ---------------------------------------------------------------- elementwise
 int timestep_embedding_launch(float t, float* out256, cudaStream_t stream);
 int silu_launch(const float* x, float* out, int n, cudaStream_t stream);
-int patchify_launch(const void* x_bf16, void* patches_bf16, int nb, int H, int W, cudaStream_t stream);
+// Patches [p_lo, p_lo + n_loc) of every batch entry -> [nb][n_loc][64].
+int patchify_launch(const void* x_bf16, void* patches_bf16, int nb, int H, int W, int p_lo, int n_loc,
+                    cudaStream_t stream);
+// Ulysses reorders.  gather_qkv: received [src][3][nb][Hl][len(src)][128]
+// FP16 -> [3][nb*Hl][S][128] in the joint order.  gather_o: received
+// [src][nb][len(r)][Hl][128] (src's heads for this rank's positions) ->
+// token-major rows [nb * n_img_l image rows; nb * n_txt_l text rows][24*128].
+int ulysses_gather_qkv_launch(const void* recv, void* qkvh, int nb, int Hl, int n_txt, const ShardMap& map,
+                              cudaStream_t stream);
+int ulysses_gather_o_launch(const void* recv, void* out, int nb, int Hl, int rank, const ShardMap& map,
+                            cudaStream_t stream);
 int unpatchify_launch(const float* proj, void* out_bf16, int nb, int H, int W, cudaStream_t stream);
 
 // q/k RMSNorm + RoPE + FP16 + head-major joint layout.  qkv rows hold
 // [q | k | v] (3 x 3072).  Rows [0, nb*n_img) are image tokens, rows
 // [nb*n_img, nb*(n_img+n_txt)) text tokens.  Outputs [nb, 24, S, 128] FP16.
+// q/k RMSNorm + RoPE + FP16 for this rank's rows.  Output layout, by
+// destination rank d (heads [d*Hl, (d+1)*Hl)):
+//   qkvh[d][which = q,k,v][b][head - d*Hl][local position][128]
+// with local position = text rows first, then image rows.  For a single rank
+// (P = 1, Hl = 24) this is [3][nb*24][S][128] in the joint order.
 struct QkvPostArgs {
-  const float* qkv_img;
-  const float* qkv_txt;
+  const float* qkv_img;  // [nb * n_img_l, 9216]
+  const float* qkv_txt;  // [nb * n_txt_l, 9216]
   const void* nq_img;  // BF16 [128] norm_q
   const void* nk_img;
   const void* nq_txt;  // norm_added_q
   const void* nk_txt;
-  const float* pe;     // nb x [S, 64, 2, 2]
-  void* q;
-  void* k;
-  void* v;
-  int nb, n_img, n_txt;
+  const float* pe;     // nb x [S, 64, 2, 2] (full sequence)
+  void* qkvh;
+  int nb, n_img, n_txt;        // full sizes
+  int img_lo, n_img_l;         // this rank's image range
+  int txt_lo, n_txt_l;         // this rank's text range
+  int Hl;                      // heads per destination rank
 };
 int qkv_post_launch(const QkvPostArgs& a, cudaStream_t stream);
 
@@ -136,10 +166,14 @@ struct AttnArgs {
   const float* ks;
   const void* v;  // FP16 [BH, S, 128]
   void* out;
-  int BH, S, heads;
+  int BH, S, heads;  // heads per batch entry in the BH layout
   float sm_scale;
+  // 0: FP32 [BH, S, 128]; 1: FP16 token-major rows (image rows of every batch
+  // entry, then text rows) x [heads * 128]; 2: FP16 by destination rank of
+  // the query position, [dest][nb][len(dest)][heads][128] (Ulysses return)
   int out_mode;
   int nb, n_img, n_txt;
+  ShardMap map;  // out_mode 2
 };
 int attention_launch(const AttnArgs& a, cudaStream_t stream, int* err_dev);
 

@@ -95,6 +95,9 @@ def lib():
             "qi_ctx_set_profiling": ([vp, i], i),
             "qi_selftest_wait_timeout": ([vp, i, vp], i),
             "qi_ctx_profile": ([vp, vp, vp, i], i),
+            "qi_comm_unique_id": ([vp], i),
+            "qi_ctx_set_comm": ([vp, vp, i, i], i),
+            "qi_exchange_plan": ([i, i, i, i, i, i, vp, vp, vp, vp], i),
             "qi_rope_table": ([i, i, i, vp], i),
             "qi_synth_fill": ([vp, ll, ull, f, f, i, vp], i),
             "qi_seed_for": ([ull, ctypes.c_char_p], ull),
@@ -277,6 +280,23 @@ def table_pointers(g, block_lists):
     return garr, barrs, bt
 
 
+COMM_ID_BYTES = 128
+
+
+def comm_unique_id():
+    buf = ctypes.create_string_buffer(COMM_ID_BYTES)
+    check(lib().qi_comm_unique_id(buf))
+    return buf.raw
+
+
+def exchange_plan(which, nb, n_txt, n_img, nranks, rank):
+    """Per-peer (send_off, send_bytes, recv_off, recv_bytes) of a head-parallel
+    block's exchange `which` (0: Q/K/V, 1: attention output); host only."""
+    arrs = [(ctypes.c_longlong * nranks)() for _ in range(4)]
+    check(lib().qi_exchange_plan(which, nb, n_txt, n_img, nranks, rank, *arrs))
+    return [list(a) for a in arrs]
+
+
 class Context:
     def __init__(self, device=0):
         self.h = ctypes.c_void_p()
@@ -287,6 +307,12 @@ class Context:
 
     def launches(self):
         return lib().qi_ctx_last_launch_count(self.h)
+
+    def set_comm(self, uid, rank, nranks):
+        """Joins the head-parallel group `uid` (bytes from comm_unique_id() on
+        rank 0) as `rank` of `nranks`; collective over the group."""
+        buf = ctypes.create_string_buffer(bytes(uid), COMM_ID_BYTES) if uid is not None else None
+        check(lib().qi_ctx_set_comm(self.h, buf, rank, nranks))
 
     def close(self):
         if self.h:
