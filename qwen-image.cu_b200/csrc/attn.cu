@@ -80,6 +80,8 @@ struct alignas(64) AttnArgsDev {
   float qk_scale;  // sm_scale * log2(e)
   int* err;
   ShardMap map;
+  void* peer_o[kMaxRanks];
+  int head_base;
 };
 
 // Not volatile: a pure function of its input, so the compiler may schedule
@@ -419,8 +421,25 @@ __global__ void __launch_bounds__(attn::THREADS, 1) sage_attn_kernel(const __gri
       const float rl = rcp_approx(l);
       const bool valid = qrow < S;
       const int b = bh / args.heads, h = bh % args.heads;
-      // out_mode 2: this row's slot in the send buffer of the rank that owns it
+      // out_mode 2: this row's slot in the send buffer of the rank that owns it;
+      // out_mode 3: its row in the owner's token-major output (peer memory)
       long long dst_off = 0;
+      __half* owner_o = nullptr;
+      if (args.out_mode == 3 && valid) {
+        const ShardMap& mp = args.map;
+        int dr = 0;
+        long long orow;
+        if (qrow < args.n_txt) {
+          while (dr + 1 < mp.P && mp.txt_lo[dr + 1] <= qrow) ++dr;
+          orow = static_cast<long long>(args.nb) * mp.n_img_l(dr) + static_cast<long long>(b) * mp.n_txt_l(dr) +
+                 (qrow - mp.txt_lo[dr]);
+        } else {
+          const int gi = qrow - args.n_txt;
+          while (dr + 1 < mp.P && mp.img_lo[dr + 1] <= gi) ++dr;
+          orow = static_cast<long long>(b) * mp.n_img_l(dr) + (gi - mp.img_lo[dr]);
+        }
+        owner_o = reinterpret_cast<__half*>(args.peer_o[dr]) + orow * kDim + (args.head_base + h) * D;
+      }
       if (args.out_mode == 2 && valid) {
         const ShardMap& mp = args.map;
         int dr = 0, lpos;
@@ -452,8 +471,8 @@ __global__ void __launch_bounds__(attn::THREADS, 1) sage_attn_kernel(const __gri
             o.w = __half2float(__float2half_rn(__uint_as_float(r[i + 3]) * rl));
             *reinterpret_cast<float4*>(dst + i) = o;
           }
-        } else if (args.out_mode == 2) {
-          __half* dst = reinterpret_cast<__half*>(args.out) + dst_off + c;
+        } else if (args.out_mode >= 2) {
+          __half* dst = (args.out_mode == 3 ? owner_o : reinterpret_cast<__half*>(args.out) + dst_off) + c;
 #pragma unroll
           for (int i = 0; i < 32; i += 8) {
             uint32_t pk[4];
@@ -709,7 +728,9 @@ int attention_launch(const AttnArgs& a, cudaStream_t stream, int* err_dev) {
   d.qk_scale = a.sm_scale * 1.44269504088896340736f;
   d.err = err_dev;
   d.map = a.map;
-  if (a.out_mode == 2 && (a.map.P < 1 || a.map.P > kMaxRanks)) return QI_ERR_ARG;
+  for (int i = 0; i < kMaxRanks; ++i) d.peer_o[i] = a.peer_o[i];
+  d.head_base = a.head_base;
+  if (a.out_mode >= 2 && (a.map.P < 1 || a.map.P > kMaxRanks)) return QI_ERR_ARG;
   dim3 grid((a.S + attn::NT * attn::BQ - 1) / (attn::NT * attn::BQ), a.BH);
   sage_attn_kernel<<<grid, attn::THREADS, attn::smem_bytes(d.ngk), stream>>>(d);
   return cudaGetLastError() == cudaSuccess ? QI_OK : QI_ERR_CUDA;

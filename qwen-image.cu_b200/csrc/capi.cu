@@ -28,6 +28,7 @@
 #include <cuda_bf16.h>
 #include <nccl.h>
 
+#include <cstdlib>
 #include <map>
 #include <mutex>
 #include <string>
@@ -88,6 +89,22 @@ struct qi_ctx {
   int* err = nullptr;  // device error word
   ncclComm_t comm = nullptr;  // head-parallel group (qi_ctx_set_comm)
   int urank = 0, usize = 1;
+  // direct exchanges over peer memory: the group's buffers mapped here (CUDA
+  // IPC), set up for one forward shape (peer_key) at a time
+  PeerSet peers = {};
+  bool peers_ready = false;
+  long long peer_key[3] = {-1, -1, -1};
+  std::vector<void*> peer_opened;
+  unsigned* flags = nullptr;  // this rank's flag words [2][kMaxRanks]
+  unsigned epoch = 0;
+  void* handles = nullptr;    // device staging for the IPC handle all-gather
+
+  void close_peers() {
+    for (void* p : peer_opened) cudaIpcCloseMemHandle(p);
+    peer_opened.clear();
+    peers_ready = false;
+    peer_key[0] = peer_key[1] = peer_key[2] = -1;
+  }
   void* buf[B_COUNT] = {};
   size_t cap[B_COUNT] = {};
   int launches = 0;
@@ -203,6 +220,9 @@ int qi_ctx_destroy(qi_ctx* c) {
   for (int i = 0; i < B_COUNT; ++i)
     if (c->buf[i]) cudaFree(c->buf[i]);
   if (c->err) cudaFree(c->err);
+  c->close_peers();
+  if (c->flags) cudaFree(c->flags);
+  if (c->handles) cudaFree(c->handles);
   if (c->comm) ncclCommDestroy(c->comm);
   delete c;
   return QI_OK;
@@ -219,12 +239,16 @@ int qi_comm_unique_id(void* id_out) {
 
 int qi_ctx_set_comm(qi_ctx* c, const void* id, int rank, int nranks) {
   if (!c || nranks < 1 || nranks > kMaxRanks || kHeads % nranks || rank < 0 || rank >= nranks) return QI_ERR_ARG;
+  c->close_peers();
   if (c->comm) {
     ncclCommDestroy(c->comm);
     c->comm = nullptr;
   }
   c->urank = 0;
   c->usize = 1;
+  // a new group starts its barrier epochs from zero on every rank
+  if (c->flags && cudaMemset(c->flags, 0, 2 * kMaxRanks * sizeof(unsigned)) != cudaSuccess) return QI_ERR_CUDA;
+  c->epoch = 0;
   if (nranks == 1) return QI_OK;
   if (!id) return QI_ERR_ARG;
   if (cudaSetDevice(c->device) != cudaSuccess) return QI_ERR_CUDA;
@@ -597,8 +621,88 @@ struct Fwd {
   ShardMap map;
   int img_lo = 0, n_img_l = 0, txt_lo = 0, n_txt_l = 0;  // this rank's tokens
   long long Mi, Mt, Ma;  // this rank's image / text / all rows (nb entries)
+  bool direct = false;   // exchanges by stores into peer memory (else NCCL)
   int n = 0;  // launches issued
 };
+
+// Maps the group's Q/K/V buffers, attention-output buffers and flag words
+// into this process (CUDA IPC; handles all-gathered over NCCL) for the
+// current forward shape.  Collective over the group: every rank runs the same
+// shapes in the same order, so all of them come here together.  If any rank
+// cannot map its peers, all fall back to the NCCL exchanges.
+int setup_peers(Fwd& f) {
+  qi_ctx* c = f.c;
+  const long long key[3] = {f.nb, f.n_img, f.n_txt};
+  if (c->peer_key[0] == key[0] && c->peer_key[1] == key[1] && c->peer_key[2] == key[2]) {
+    f.direct = c->peers_ready;
+    return QI_OK;
+  }
+  c->close_peers();
+  const int P = f.P, me = f.rank;
+  constexpr int kH = sizeof(cudaIpcMemHandle_t);
+  if (!c->flags) {
+    if (cudaMalloc(&c->flags, 2 * kMaxRanks * sizeof(unsigned)) != cudaSuccess) return QI_ERR_OOM;
+    if (cudaMemset(c->flags, 0, 2 * kMaxRanks * sizeof(unsigned)) != cudaSuccess) return QI_ERR_CUDA;
+    c->epoch = 0;
+  }
+  if (!c->handles && cudaMalloc(&c->handles, (kMaxRanks + 1) * 3 * kH + sizeof(int) * 2) != cudaSuccess)
+    return QI_ERR_OOM;
+  cudaIpcMemHandle_t mine[3];
+  // QI_PEER_EXCHANGE=0 selects the NCCL exchanges (the same on every rank)
+  const char* env = getenv("QI_PEER_EXCHANGE");
+  const bool want = !(env && env[0] == '0');
+  int ok = want && cudaIpcGetMemHandle(&mine[0], c->buf[B_QKVH]) == cudaSuccess &&
+           cudaIpcGetMemHandle(&mine[1], c->buf[B_O]) == cudaSuccess &&
+           cudaIpcGetMemHandle(&mine[2], c->flags) == cudaSuccess;
+  char* hd = static_cast<char*>(c->handles);  // [mine 3][all P x 3][ok, ok_min]
+  if (cudaMemcpyAsync(hd, mine, 3 * kH, cudaMemcpyHostToDevice, f.s) != cudaSuccess) return QI_ERR_CUDA;
+  if (ncclAllGather(hd, hd + 3 * kH, 3 * kH, ncclUint8, c->comm, f.s) != ncclSuccess) return QI_ERR_NCCL;
+  std::vector<cudaIpcMemHandle_t> all(static_cast<size_t>(P) * 3);
+  if (cudaMemcpyAsync(all.data(), hd + 3 * kH, static_cast<size_t>(P) * 3 * kH, cudaMemcpyDeviceToHost, f.s) !=
+          cudaSuccess ||
+      cudaStreamSynchronize(f.s) != cudaSuccess)
+    return QI_ERR_CUDA;
+  PeerSet ps = {};
+  ps.P = P;
+  ps.rank = me;
+  for (int q = 0; q < P && ok; ++q) {
+    if (q == me) {
+      ps.qkvh[q] = c->buf[B_QKVH];
+      ps.o[q] = c->buf[B_O];
+      ps.flags[q] = c->flags;
+      continue;
+    }
+    void* ptr[3] = {};
+    for (int k = 0; k < 3 && ok; ++k) {
+      if (cudaIpcOpenMemHandle(&ptr[k], all[static_cast<size_t>(q) * 3 + k], cudaIpcMemLazyEnablePeerAccess) !=
+          cudaSuccess) {
+        cudaGetLastError();
+        ok = 0;
+        break;
+      }
+      c->peer_opened.push_back(ptr[k]);
+    }
+    ps.qkvh[q] = ptr[0];
+    ps.o[q] = ptr[1];
+    ps.flags[q] = static_cast<unsigned*>(ptr[2]);
+  }
+  // every rank must take the same path
+  int* okd = reinterpret_cast<int*>(hd + (kMaxRanks + 1) * 3 * kH);
+  int ok_all = 0;
+  if (cudaMemcpyAsync(okd, &ok, sizeof(int), cudaMemcpyHostToDevice, f.s) != cudaSuccess) return QI_ERR_CUDA;
+  if (ncclAllReduce(okd, okd + 1, 1, ncclInt32, ncclMin, c->comm, f.s) != ncclSuccess) return QI_ERR_NCCL;
+  if (cudaMemcpyAsync(&ok_all, okd + 1, sizeof(int), cudaMemcpyDeviceToHost, f.s) != cudaSuccess ||
+      cudaStreamSynchronize(f.s) != cudaSuccess)
+    return QI_ERR_CUDA;
+  if (!ok_all) c->close_peers();
+  c->peers = ps;
+  c->peers_ready = ok_all != 0;
+  c->peer_key[0] = key[0];
+  c->peer_key[1] = key[1];
+  c->peer_key[2] = key[2];
+  f.direct = c->peers_ready;
+  return QI_OK;
+}
 
 // One launch (or a fixed group) per QI_LAUNCH; with profiling on, an event
 // pair brackets it on the stream and is resolved in qi_ctx_profile.
@@ -665,10 +769,13 @@ int fwd_init(Fwd& f, qi_ctx* c, const qi_model* m, int nb, int n_img, int n_txt,
   QI_TRY(c->ensure(B_FIN, f.Mi * kDim * 2));
   QI_TRY(c->ensure(B_PROJ, f.Mi * kPatchDim * 4));
   if (f.P > 1) {
-    QI_TRY(c->ensure(B_SEND1, f.Ma * 3 * kDim * 2));
-    QI_TRY(c->ensure(B_RECV1, 3 * hs * 2));
-    QI_TRY(c->ensure(B_SEND2, hs * 2));
-    QI_TRY(c->ensure(B_RECV2, f.Ma * kDim * 2));
+    QI_TRY(setup_peers(f));
+    if (!f.direct) {  // NCCL exchange buffers
+      QI_TRY(c->ensure(B_SEND1, f.Ma * 3 * kDim * 2));
+      QI_TRY(c->ensure(B_RECV1, 3 * hs * 2));
+      QI_TRY(c->ensure(B_SEND2, hs * 2));
+      QI_TRY(c->ensure(B_RECV2, f.Ma * kDim * 2));
+    }
     QI_TRY(c->ensure(B_PROJF, static_cast<size_t>(nb) * n_img * kPatchDim * 4));
   }
   return QI_OK;
@@ -758,14 +865,18 @@ int fwd_blocks(Fwd& f, float* x_img, float* x_txt, const float* pe, int b0, int 
                       {act + Mi * kDim, act_s + Mi, B.qkv[1].w, B.qkv[1].s, B.qkv[1].b, qkv + Mi * 3 * kDim, nullptr,
                        static_cast<int>(Mt), 3 * kDim, kDim, 3 * kDim}};
     QI_LAUNCH(QI_PROF_GEMM_QKV, 1, gemm_i8_launch(gq, 2, kEpiStore, s, c->err, c->num_sms));
-    const bool par = f.P > 1;
+    const bool par = f.P > 1, direct = par && f.direct;
     __half* qkvh = c->p<__half>(B_QKVH);
     const size_t hs = static_cast<size_t>(BH) * S * kHeadDim;
     QkvPostArgs qa{qkv,       qkv + Mi * 3 * kDim, B.norms, B.norms + kHeadDim, B.norms + 2 * kHeadDim,
                    B.norms + 3 * kHeadDim, pe, par ? c->buf[B_SEND1] : qkvh, nb, n_img, n_txt, f.img_lo, f.n_img_l,
-                   f.txt_lo, f.n_txt_l, f.Hl};
+                   f.txt_lo, f.n_txt_l, f.Hl, direct ? 1 : 0};
+    if (direct)
+      for (int q = 0; q < f.P; ++q) qa.peer_qkvh[q] = c->peers.qkvh[q];
     QI_LAUNCH(QI_PROF_QKV_POST, 1, qkv_post_launch(qa, s));
-    if (par) {  // every token of this rank's heads
+    if (direct) {  // every rank has stored its rows of this rank's heads
+      QI_LAUNCH(QI_PROF_EXCHANGE, 1, peer_barrier_launch(c->peers, 0, ++c->epoch, c->err, s));
+    } else if (par) {  // every token of this rank's heads
       QI_LAUNCH(QI_PROF_EXCHANGE, 0, exchange(c, 0, nb, f.map, c->buf[B_SEND1], c->buf[B_RECV1], s));
       QI_LAUNCH(QI_PROF_EXCHANGE, 1, ulysses_gather_qkv_launch(c->buf[B_RECV1], qkvh, nb, f.Hl, n_txt, f.map, s));
     }
@@ -773,10 +884,16 @@ int fwd_blocks(Fwd& f, float* x_img, float* x_txt, const float* pe, int b0, int 
               sage_quantize_launch(qkvh, qkvh + hs, BH, S, c->p<float>(B_KMEAN), c->p<int8_t>(B_QC),
                                    c->p<float>(B_QS), c->p<int8_t>(B_KC), c->p<float>(B_KS), s));
     AttnArgs aa{c->p<int8_t>(B_QC), c->p<float>(B_QS), c->p<int8_t>(B_KC), c->p<float>(B_KS), qkvh + 2 * hs,
-                par ? c->buf[B_SEND2] : c->buf[B_O], BH, S, f.Hl, 1.0f / sqrtf(128.0f), par ? 2 : 1, nb, n_img, n_txt,
-                f.map};
+                par && !direct ? c->buf[B_SEND2] : c->buf[B_O], BH, S, f.Hl, 1.0f / sqrtf(128.0f),
+                direct ? 3 : (par ? 2 : 1), nb, n_img, n_txt, f.map};
+    if (direct) {
+      for (int q = 0; q < f.P; ++q) aa.peer_o[q] = c->peers.o[q];
+      aa.head_base = f.rank * f.Hl;
+    }
     QI_LAUNCH(QI_PROF_ATTENTION, 1, attention_launch(aa, s, c->err));
-    if (par) {  // back to the token owners, token-major
+    if (direct) {  // every rank has stored its heads of this rank's rows
+      QI_LAUNCH(QI_PROF_EXCHANGE, 1, peer_barrier_launch(c->peers, 1, ++c->epoch, c->err, s));
+    } else if (par) {  // back to the token owners, token-major
       QI_LAUNCH(QI_PROF_EXCHANGE, 0, exchange(c, 1, nb, f.map, c->buf[B_SEND2], c->buf[B_RECV2], s));
       QI_LAUNCH(QI_PROF_EXCHANGE, 1, ulysses_gather_o_launch(c->buf[B_RECV2], c->buf[B_O], nb, f.Hl, f.rank, f.map, s));
     }

@@ -76,10 +76,19 @@ __global__ void qkv_post_kernel(QkvPostArgs a) {
   const float4 pe0 = __ldg(reinterpret_cast<const float4*>(pe));
   const float4 pe1 = __ldg(reinterpret_cast<const float4*>(pe + 4));
   const int dest = h / a.Hl, hh = h % a.Hl;
-  // qkvh[dest][which][b][hh][lpos][128]; `which` adds one (nb * Hl * L * 128) slab
-  const size_t slab = static_cast<size_t>(a.nb) * a.Hl * L * kHeadDim;
-  const size_t dst = static_cast<size_t>(dest) * 3 * slab + ((static_cast<size_t>(b) * a.Hl + hh) * L + lpos) * kHeadDim + d0;
-  __half* base = reinterpret_cast<__half*>(a.qkvh);
+  size_t slab, dst;
+  __half* base;
+  if (a.direct) {
+    // the head owner's buffer, [which][b][hh][joint position][128]
+    slab = static_cast<size_t>(a.nb) * a.Hl * S * kHeadDim;
+    dst = ((static_cast<size_t>(b) * a.Hl + hh) * S + pos) * kHeadDim + d0;
+    base = reinterpret_cast<__half*>(a.peer_qkvh[dest]);
+  } else {
+    // qkvh[dest][which][b][hh][lpos][128]; `which` adds one (nb * Hl * L * 128) slab
+    slab = static_cast<size_t>(a.nb) * a.Hl * L * kHeadDim;
+    dst = static_cast<size_t>(dest) * 3 * slab + ((static_cast<size_t>(b) * a.Hl + hh) * L + lpos) * kHeadDim + d0;
+    base = reinterpret_cast<__half*>(a.qkvh);
+  }
 
   auto norm_rope = [&](float4 x, const __nv_bfloat16* w, __half* out) {
     float ss = x.x * x.x + x.y * x.y + x.z * x.z + x.w * x.w;

@@ -118,6 +118,19 @@ int silu_launch(const float* x, float* out, int n, cudaStream_t stream);
 // Patches [p_lo, p_lo + n_loc) of every batch entry -> [nb][n_loc][64].
 int patchify_launch(const void* x_bf16, void* patches_bf16, int nb, int H, int W, int p_lo, int n_loc,
                     cudaStream_t stream);
+// Ranks of a head-parallel group that write into each other's buffers (CUDA
+// IPC mappings): each rank's Q/K/V buffer, token-major attention output and
+// flag words [2 slots][kMaxRanks].
+struct PeerSet {
+  int P, rank;
+  void* qkvh[kMaxRanks];
+  void* o[kMaxRanks];
+  unsigned* flags[kMaxRanks];
+};
+// Raises this rank's flag `slot` = epoch on every peer, then waits (bounded)
+// until every peer has raised its flag here: all earlier work on `stream`
+// of every rank is then visible to the later work of every rank.
+int peer_barrier_launch(const PeerSet& ps, int slot, unsigned epoch, int* err, cudaStream_t stream);
 // Ulysses reorders.  gather_qkv: received [src][3][nb][Hl][len(src)][128]
 // FP16 -> [3][nb*Hl][S][128] in the joint order.  gather_o: received
 // [src][nb][len(r)][Hl][128] (src's heads for this rank's positions) ->
@@ -149,6 +162,10 @@ struct QkvPostArgs {
   int img_lo, n_img_l;         // this rank's image range
   int txt_lo, n_txt_l;         // this rank's text range
   int Hl;                      // heads per destination rank
+  // direct != 0: store straight into each head owner's Q/K/V buffer (peer
+  // memory over NVLink), final layout [3][nb*Hl][S][128] in joint order
+  int direct;
+  void* peer_qkvh[kMaxRanks];
 };
 int qkv_post_launch(const QkvPostArgs& a, cudaStream_t stream);
 
@@ -173,7 +190,11 @@ struct AttnArgs {
   // the query position, [dest][nb][len(dest)][heads][128] (Ulysses return)
   int out_mode;
   int nb, n_img, n_txt;
-  ShardMap map;  // out_mode 2
+  ShardMap map;  // out_mode 2, 3
+  // out_mode 3: FP16 straight into the token owner's token-major rows (peer
+  // memory), columns (head_base + head) * 128
+  void* peer_o[kMaxRanks];
+  int head_base;
 };
 int attention_launch(const AttnArgs& a, cudaStream_t stream, int* err_dev);
 

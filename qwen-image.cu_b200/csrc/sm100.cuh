@@ -30,6 +30,7 @@ enum DeviceError : int {
   kErrTimeoutEpilogue = 3,
   kErrTimeoutSoftmax = 4,
   kErrTimeoutSelftest = 5,
+  kErrTimeoutPeer = 6,  // a peer rank never raised its flag
 };
 
 // A bounded wait gives up after this many nanoseconds of %globaltimer.  One

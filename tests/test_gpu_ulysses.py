@@ -3,21 +3,26 @@
 Every per-token computation (linears, norms, quantizers) and every per-head
 computation (K mean, Sage quantization, attention over the full joint
 sequence) is the same arithmetic in both, so the outputs must be equal bit
-for bit.  Uneven splits (odd token counts) and nb = 2 are covered.  Needs two
-GPUs; skipped otherwise."""
+for bit.  Uneven splits (odd token counts) and nb = 2 are covered, for both
+exchange paths: stores into peer memory with flag barriers, and NCCL
+all-to-alls.  Needs P GPUs; skipped otherwise."""
 import pytest
 import torch
 import torch.multiprocessing as mp
 
 pytestmark = pytest.mark.gpu
 
-needs2 = pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
-                            reason="needs 2 GPUs")
+
+def _gpus():
+    return torch.cuda.device_count() if torch.cuda.is_available() else 0
 
 
-def _worker(rank, P, H, W, n_txt, nb, blocks, uid_q, out_q):
+def _worker(rank, P, H, W, n_txt, nb, blocks, exchange, uid_q, out_q):
     try:
+        import os
+
         import numpy as np
+        os.environ["QI_PEER_EXCHANGE"] = "1" if exchange == "peer" else "0"
 
         import qib200 as Q
         import qi_oracle as O
@@ -56,13 +61,16 @@ def _worker(rank, P, H, W, n_txt, nb, blocks, uid_q, out_q):
         out_q.put((rank, repr(e)))
 
 
-@needs2
-@pytest.mark.parametrize("H,W,n_txt,nb", [(66, 66, 77, 1), (32, 48, 30, 2)])
-def test_head_parallel_forward_equals_single_gpu(H, W, n_txt, nb):
-    P, blocks = 2, 2
+@pytest.mark.parametrize("exchange", ["peer", "nccl"])
+@pytest.mark.parametrize("P,H,W,n_txt,nb", [(2, 66, 66, 77, 1), (2, 32, 48, 30, 2), (4, 66, 66, 77, 2)])
+def test_head_parallel_forward_equals_single_gpu(P, H, W, n_txt, nb, exchange):
+    if _gpus() < P:
+        pytest.skip(f"needs {P} GPUs")
+    blocks = 2
     ctx = mp.get_context("spawn")
     uid_q, out_q = ctx.Queue(), ctx.Queue()
-    procs = [ctx.Process(target=_worker, args=(r, P, H, W, n_txt, nb, blocks, uid_q, out_q)) for r in range(P)]
+    procs = [ctx.Process(target=_worker, args=(r, P, H, W, n_txt, nb, blocks, exchange, uid_q, out_q))
+             for r in range(P)]
     for p in procs:
         p.start()
     results = dict(out_q.get(timeout=600) for _ in range(P))
