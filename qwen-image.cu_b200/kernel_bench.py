@@ -49,6 +49,11 @@ def bench_gemm(iters, res):
         ms = time_it(lambda: Q.linear_i8(a, sa, w, sw, b, epi, out=out), iters)
         tf = 2.0 * M * N * K / (ms * 1e-3) / 1e12
         res[f"gemm_{name}"] = {"M": M, "N": N, "K": K, "ms": round(ms, 4), "tops": round(tf, 1)}
+        # cuBLASLt INT8 GEMM on the same operands (INT32 output, no epilogue),
+        # for reference: the library's rate on this B200 for this shape
+        wt = w.t()
+        ms_cb = time_it(lambda: torch._int_mm(a, wt), iters)
+        res[f"cublas_int8_{name}"] = {"ms": round(ms_cb, 4), "tops": round(2.0 * M * N * K / (ms_cb * 1e-3) / 1e12, 1)}
         del a, w, out
 
 

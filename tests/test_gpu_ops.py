@@ -82,8 +82,11 @@ def test_activation_quantizer_bitexact(M, K, B):
 
 
 # ------------------------------------------------------------------ GEMM
+# the last three shapes (M >= 512, K >= 8192) run on CTA pairs (256-row tiles),
+# with M not a multiple of 256 and N not a multiple of the 256-column tile
 @pytest.mark.parametrize("M,N,K", [(1, 256, 128), (100, 256, 3072), (128, 3072, 3072), (300, 96, 3072),
-                                   (1000, 9216, 3072), (257, 3072, 12288), (64, 512, 64), (513, 12288, 3072)])
+                                   (1000, 9216, 3072), (257, 3072, 12288), (64, 512, 64), (513, 12288, 3072),
+                                   (1000, 3072, 12288), (700, 544, 8192), (512, 256, 8192)])
 def test_gemm_int32_accumulators_exact(M, N, K):
     g = torch.Generator(device="cuda").manual_seed(M * 7 + N + K)
     a = torch.randint(-128, 128, (M, K), dtype=torch.int8, device="cuda", generator=g)
@@ -119,13 +122,13 @@ def test_linear_dequant_matches_reference(M, N, K, gelu):
         assert cos > 0.999999 and maxrel < 1e-5, (cos, maxrel)
 
 
-def test_linear_residual_epilogue():
-    M, N, K = 200, 3072, 3072
-    x = Q.synth((M, K), Q.seed_for(22, "x"), 1.0)
-    w = Q.synth((N, K), Q.seed_for(22, "w"), 0.02, dtype=torch.bfloat16)
-    b = Q.synth((N,), Q.seed_for(22, "b"), 0.02, dtype=torch.bfloat16)
-    gate = Q.synth((N,), Q.seed_for(22, "g"), 0.5)
-    resid = Q.synth((M, N), Q.seed_for(22, "r"), 3.0)
+@pytest.mark.parametrize("M,N,K", [(200, 3072, 3072), (900, 3072, 12288)])  # second: CTA pairs
+def test_linear_residual_epilogue(M, N, K):
+    x = Q.synth((M, K), Q.seed_for(22, f"x{K}"), 1.0)
+    w = Q.synth((N, K), Q.seed_for(22, f"w{K}"), 0.02, dtype=torch.bfloat16)
+    b = Q.synth((N,), Q.seed_for(22, f"b{K}"), 0.02, dtype=torch.bfloat16)
+    gate = Q.synth((N,), Q.seed_for(22, f"g{K}"), 0.5)
+    resid = Q.synth((M, N), Q.seed_for(22, f"r{K}"), 3.0)
     wc, ws = Q.quantize_weight(w)
     ac, asc = Q.fwht_quantize(x)
     y = R.linear_int8_preq(ac, asc, wc, ws, b, False)
