@@ -71,14 +71,30 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Non-suspending test of the phase (returns at once).
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 // Waits for the phase with the given parity to complete.  Returns false when
 // the wait gives up (time limit) or when another role has raised *abort; the
-// caller then leaves its loop and the kernel tears down normally.
+// caller then leaves its loop and the kernel tears down normally.  Spins on
+// test_wait rather than try_wait: measured on B200, a thread suspended in
+// try_wait can wake several hundred cycles after the phase completes, which
+// sits on the critical path of every pipeline hand-off.
 __device__ __forceinline__ bool mbar_wait_limit(uint64_t* bar, uint32_t parity, volatile int* abort, uint64_t limit_ns) {
-  if (mbar_try_wait(bar, parity)) return true;
-  uint64_t t0 = global_timer_ns();
+  if (mbar_test_wait(bar, parity)) return true;
+  const uint64_t t0 = global_timer_ns();
   while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
+#pragma unroll 1
+    for (int i = 0; i < 64; ++i)
+      if (mbar_test_wait(bar, parity)) return true;
     if (*abort) return false;
     if (global_timer_ns() - t0 > limit_ns) return false;
   }
