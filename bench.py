@@ -38,6 +38,9 @@ sys.path.insert(0, os.path.join(ROOT, "oracle"))
 import numpy as np  # noqa: E402
 import torch  # noqa: E402
 
+# default workload C4; --workload c5 switches to configs[4]
+# (2048x2048: 256x256 latent, 16384 image + 512 text tokens, 20 steps)
+WORKLOAD = "c4"
 H_LAT = W_LAT = 166
 N_TXT = 256
 BLOCKS = 60
@@ -304,8 +307,8 @@ def run_ours(args):
         "vs_baseline": None,
         "dtype": "int8",
         "data": "synthetic (seeded N(0,1) latents/text states; random-init N(0,0.02^2) weights quantized to INT8)",
-        "config": {"workload": "C4: 1328x1328, 6889 img + 256 txt tokens, CFG cond+uncond, 60 blocks, W8A8 + "
-                               "SageAttention (INT8 QK, FP16 PV)",
+        "config": {"workload": f"{WORKLOAD.upper()}: {H_LAT * 8}x{W_LAT * 8}, {N_IMG} img + {N_TXT} txt tokens, CFG "
+                               "cond+uncond, 60 blocks, W8A8 + SageAttention (INT8 QK, FP16 PV)",
                    "latent": [16, H_LAT, W_LAT], "n_img": N_IMG, "n_txt": N_TXT, "blocks": BLOCKS,
                    "cfg": "batched (nb=2) on 1 GPU" if world == 1 else "cond/uncond on two rank groups",
                    "parallelism": "single" if world == 1 else ("cfg2" if P == 1 else f"cfg2 x ulysses{P}"),
@@ -432,8 +435,9 @@ def run_reference(args):
         "vs_baseline": None,
         "dtype": "int8",
         "data": "synthetic (same seeds as the product arm)",
-        "config": {"workload": "C4: 1328x1328, 6889 img + 256 txt tokens, CFG cond+uncond, 60 blocks, W8A8 + "
-                               "SageAttention sm80 (reference build, transformer_forward x2 per step)",
+        "config": {"workload": f"{WORKLOAD.upper()}: {H_LAT * 8}x{W_LAT * 8}, {N_IMG} img + {N_TXT} txt tokens, CFG "
+                               "cond+uncond, 60 blocks, W8A8 + SageAttention sm80 (reference build, transformer_forward "
+                               "x2 per step)",
                    "latent": [16, H_LAT, W_LAT], "n_img": N_IMG, "n_txt": N_TXT, "blocks": BLOCKS},
         "cpu_baseline": {"value": round(ms / 1000.0, 5), "unit": "s/step", "cores": 0, "kind": "reference",
                          "sample": "the reference's own CUDA build (it has no CPU path) timed on one GPU"},
@@ -450,7 +454,15 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--workload", default="c4", choices=["c4", "c5"],
+                    help="c4: 1328x1328 (the headline metric); c5: 2048x2048, 20 steps (scaling study)")
     args = ap.parse_args()
+    if args.workload == "c5":
+        global WORKLOAD, H_LAT, W_LAT, N_TXT, SCHED_STEPS, N_IMG, S_JOINT, METRIC
+        WORKLOAD, H_LAT, W_LAT, N_TXT, SCHED_STEPS = "c5", 256, 256, 512, 20
+        N_IMG = (H_LAT // 2) * (W_LAT // 2)
+        S_JOINT = N_IMG + N_TXT
+        METRIC = "MMDiT sec/denoise-step at 2048^2 @1/2/4/8 B200 (scaling study)"
     if args.warmup < 3:
         print("warmup < 3 is not a valid measurement; using 3", file=sys.stderr)
         args.warmup = 3
