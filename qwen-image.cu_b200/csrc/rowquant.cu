@@ -22,6 +22,7 @@
 //   kSrcF16:   the attention output rows (FP16, as the reference's half
 //              output converted to float, sageattention_sm80.cu:888-894).
 #include "qi_internal.h"
+#include "sm100.cuh"
 
 #include <cuda_fp16.h>
 #include <cuda_bf16.h>
@@ -232,32 +233,65 @@ __global__ void __launch_bounds__(NW * 32) rowquant_warp_kernel(RowSegs segs, in
 // runs those stages in registers, and transposes back for bits 7-11; the
 // stage order (half = 1, 2, 4, ..., 2048) and every butterfly's operands are
 // those of the reference.
+// Persistent: each CTA takes rows blockIdx.x, blockIdx.x + gridDim.x, ...; as
+// soon as a warp has copied its 16 KB slice of a row from shared memory into
+// registers, it issues the bulk copy of its slice of the CTA's next row, so
+// the HBM latency of row r+1 overlaps the butterflies of row r.
 __global__ void __launch_bounds__(96) rowquant_b4096_kernel(RowSegs segs, int had_block, int8_t* __restrict__ codes,
-                                                            float* __restrict__ scales) {
+                                                            float* __restrict__ scales, int rows) {
   constexpr int K = 12288, NW = 3, J = 32;
-  extern __shared__ float4 tile4[];  // [NW][32 rows][32 float4], swizzled: (row, col) at row*32 + (col ^ row)
-  __shared__ float red[NW];
-  const int row = blockIdx.x;
-  const bool second = segs.nseg > 1 && row >= segs.s[0].rows;
-  const void* in = second ? segs.s[1].in : segs.s[0].in;
-  const long long ld = second ? segs.s[1].ld : segs.s[0].ld;
-  const int local = second ? row - segs.s[0].rows : row;
+  // [NW][32 rows][32 float4] transpose tiles, swizzled: (row, col) at row*32 + (col ^ row);
+  // then [NW][1024 float4] prefetch slices
+  extern __shared__ float4 tile4[];
+  __shared__ float red[2][NW];
+  __shared__ __align__(8) uint64_t pbar[NW];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int base = warp * 4096 + 4 * lane;
   float4* tw = tile4 + warp * 1024;
-
-  float v[J][4];
-  {
-    const float* src = reinterpret_cast<const float*>(in) + static_cast<long long>(local) * ld + base;
-#pragma unroll
-    for (int j = 0; j < J; ++j) {
-      const float4 f = *reinterpret_cast<const float4*>(src + 128 * j);
-      v[j][0] = f.x;
-      v[j][1] = f.y;
-      v[j][2] = f.z;
-      v[j][3] = f.w;
-    }
+  float4* pw = tile4 + NW * 1024 + warp * 1024;
+  auto slice_of = [&](int r) {
+    const bool second = segs.nseg > 1 && r >= segs.s[0].rows;
+    const void* in = second ? segs.s[1].in : segs.s[0].in;
+    const long long ld = second ? segs.s[1].ld : segs.s[0].ld;
+    const int local = second ? r - segs.s[0].rows : r;
+    return reinterpret_cast<const float*>(in) + static_cast<long long>(local) * ld + warp * 4096;
+  };
+  auto prefetch = [&](int r) {
+    mbar_expect_tx(&pbar[warp], 16384);
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(pw)),
+        "l"(slice_of(r)), "r"(16384), "r"(smem_u32(&pbar[warp]))
+        : "memory");
+  };
+  if (lane == 0) {
+    mbar_init(&pbar[warp], 1);
+    fence_mbar_init();
   }
+  __syncwarp();
+  if (lane == 0 && static_cast<int>(blockIdx.x) < rows) prefetch(blockIdx.x);
+  uint32_t phase = 0;
+  int it = 0;
+#pragma unroll 1
+  for (int row = blockIdx.x; row < rows; row += gridDim.x, ++it) {
+  // the bulk copy needs no other work to finish; the limit only bounds the spin
+  {
+    const uint64_t t0 = global_timer_ns();
+    while (!mbar_test_wait(&pbar[warp], phase) && global_timer_ns() - t0 < kWaitLimitNs) {
+    }
+    phase ^= 1u;
+  }
+  float v[J][4];
+#pragma unroll
+  for (int j = 0; j < J; ++j) {
+    const float4 f = pw[32 * j + lane];
+    v[j][0] = f.x;
+    v[j][1] = f.y;
+    v[j][2] = f.z;
+    v[j][3] = f.w;
+  }
+  fence_proxy_async_smem();  // every lane's reads of the slice come before the copy overwrites it
+  __syncwarp();
+  if (lane == 0 && row + static_cast<int>(gridDim.x) < rows) prefetch(row + gridDim.x);
   auto stage_components = [&]() {
 #pragma unroll
     for (int j = 0; j < J; ++j) {
@@ -325,9 +359,9 @@ __global__ void __launch_bounds__(96) rowquant_b4096_kernel(RowSegs segs, int ha
       mx = fmaxf(mx, fabsf(v[j][e]));
     }
   mx = warp_max(mx);
-  if (lane == 0) red[warp] = mx;
+  if (lane == 0) red[it & 1][warp] = mx;  // double buffered: the next row's writes go to the other slot
   __syncthreads();
-  mx = fmaxf(fmaxf(red[0], red[1]), red[2]);
+  mx = fmaxf(fmaxf(red[it & 1][0], red[it & 1][1]), red[it & 1][2]);
   if (threadIdx.x == 0) scales[row] = mx / 127.0f;
   const float inv = (mx > 0.0f) ? 127.0f / mx : 0.0f;
   int8_t* dst = codes + static_cast<long long>(row) * K + base;
@@ -339,6 +373,7 @@ __global__ void __launch_bounds__(96) rowquant_b4096_kernel(RowSegs segs, int ha
     q.z = static_cast<signed char>(max(-128, min(127, __float2int_rn(v[j][2] * inv))));
     q.w = static_cast<signed char>(max(-128, min(127, __float2int_rn(v[j][3] * inv))));
     *reinterpret_cast<char4*>(dst + 128 * j) = q;
+  }
   }
 }
 
@@ -430,11 +465,12 @@ int rowquant_launch(int src, int K, int had_block, const RowSeg* segs, int nseg,
   if (K == 3072 && src == kSrcLnMod)
     return launch_warp<3072, 3, kSrcLnMod>(s, rows, had_block, codes, scales, eps, stream);
   if (K == 12288 && src == kSrcF32 && had_block == 4096) {
-    const int smem = 3 * 1024 * 16;  // three 16 KB warp tiles
+    const int smem = 2 * 3 * 1024 * 16;  // three 16 KB transpose tiles + three 16 KB prefetch slices
     static unsigned long long attr_done = 0;
     if (smem_optin(reinterpret_cast<const void*>(rowquant_b4096_kernel), smem, &attr_done) != QI_OK)
       return QI_ERR_CUDA;
-    rowquant_b4096_kernel<<<rows, 96, smem, stream>>>(s, had_block, codes, scales);
+    const int grid = rows < 2 * device_num_sms() ? rows : 2 * device_num_sms();
+    rowquant_b4096_kernel<<<grid, 96, smem, stream>>>(s, had_block, codes, scales, rows);
     return cudaGetLastError() == cudaSuccess ? QI_OK : QI_ERR_CUDA;
   }
   if (K == 12288 && src == kSrcF32)

@@ -187,6 +187,27 @@ def test_forward_is_deterministic(env):
     assert torch.equal(a, b)
 
 
+def test_forward_replays_from_a_cuda_graph(env):
+    """The forward is asynchronous work on the caller's stream only (no host
+    synchronisation, and no allocation once the workspace has grown to the
+    shape), so a caller can capture it into a CUDA graph: replays equal the
+    eager forward bit for bit."""
+    x, (txt,), pe = inputs(16, 16, 16)
+    eager = Q.forward(env["ctx"], env["model"], x, 400.0, txt, pe[None])  # grows the workspace
+    torch.cuda.synchronize()
+    out = torch.empty_like(eager)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        Q.forward(env["ctx"], env["model"], x, 400.0, txt, pe[None], out=out)
+    for _ in range(2):
+        out.zero_()
+        graph.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(out, eager)
+    env["ctx"].check()
+    del graph
+
+
 def test_one_block_forward_matches_cpu_oracle():
     """A one-block model end to end (boundary layers + block 0) at a tiny size
     against the CPU oracle's quantization-emulating forward."""
