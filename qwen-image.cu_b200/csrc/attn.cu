@@ -524,28 +524,36 @@ __device__ __forceinline__ int8_t cvt_rni_sat_s8(float x) {
 
 // K mean per (batch-head, dim): the reference sums over tokens serially in
 // token order (sageattention_sm80.cu:759-773); the K codes depend on it, so the
-// order is kept.  One CTA per (batch-head, 32 dims): all 256 threads prefetch
-// the next 256-token x 32-dim tile into shared memory while warp 0 runs the
-// 32 serial chains (lane = dim) over the current one.
+// order is kept.  One CTA per (batch-head, DPC dims): all 256 threads prefetch
+// the next 256-token x DPC-dim tile into shared memory while DPC/32 warps run
+// the serial chains (lane = dim) over the current one.  DPC is chosen so the
+// grid is a single wave: the chains are the kernel's whole cost.
+template <int DPC>
 __global__ void __launch_bounds__(256) sage_kmean_kernel(const __half* __restrict__ k, float* __restrict__ kmean, int S) {
   constexpr int T = 256;
-  __shared__ __align__(16) __half tile[2][T][32];
-  const int bh = blockIdx.x, d0 = blockIdx.y * 32;
+  constexpr int PRE = DPC / 8;  // 16-byte pieces per thread per tile
+  extern __shared__ __align__(16) __half km_tile[];  // [2][T][DPC]
+  const int bh = blockIdx.x, d0 = blockIdx.y * DPC;
   const __half* base = k + static_cast<size_t>(bh) * S * 128 + d0;
-  const int tid = threadIdx.x;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int nchunks = (S + T - 1) / T;
-  uint4 pre[4];
+  uint4 pre[PRE];
   auto load = [&](int c) {
 #pragma unroll
-    for (int r = 0; r < 4; ++r) {
-      const int t = c * T + (tid >> 2) + 64 * r;
-      pre[r] = (t < S) ? *reinterpret_cast<const uint4*>(base + static_cast<size_t>(t) * 128 + (tid & 3) * 8)
+    for (int r = 0; r < PRE; ++r) {
+      const int i = tid + 256 * r;  // piece index in the tile
+      const int t = c * T + i / (DPC / 8), piece = i % (DPC / 8);
+      pre[r] = (t < S) ? *reinterpret_cast<const uint4*>(base + static_cast<size_t>(t) * 128 + piece * 8)
                        : make_uint4(0, 0, 0, 0);
     }
   };
   auto stash = [&](int b) {
 #pragma unroll
-    for (int r = 0; r < 4; ++r) *reinterpret_cast<uint4*>(&tile[b][(tid >> 2) + 64 * r][(tid & 3) * 8]) = pre[r];
+    for (int r = 0; r < PRE; ++r) {
+      const int i = tid + 256 * r;
+      *reinterpret_cast<uint4*>(km_tile + (static_cast<size_t>(b) * T + i / (DPC / 8)) * DPC + (i % (DPC / 8)) * 8) =
+          pre[r];
+    }
   };
   float sum = 0.0f;
   load(0);
@@ -553,17 +561,27 @@ __global__ void __launch_bounds__(256) sage_kmean_kernel(const __half* __restric
   __syncthreads();
   for (int c = 0; c < nchunks; ++c) {
     if (c + 1 < nchunks) load(c + 1);
-    if (tid < 32) {
+    if (warp < DPC / 32) {
       const int n = min(T, S - c * T);
-      const __half* col = &tile[c & 1][0][tid];
+      const __half* col = km_tile + static_cast<size_t>(c & 1) * T * DPC + warp * 32 + lane;
 #pragma unroll 8
-      for (int t = 0; t < n; ++t) sum += __half2float(col[t * 32]);
+      for (int t = 0; t < n; ++t) sum += __half2float(col[t * DPC]);
     }
     __syncthreads();
     if (c + 1 < nchunks) stash((c + 1) & 1);
     __syncthreads();
   }
-  if (tid < 32) kmean[bh * 128 + d0 + tid] = sum / fmaxf(static_cast<float>(S), 1.0f);
+  if (warp < DPC / 32) kmean[bh * 128 + d0 + warp * 32 + lane] = sum / fmaxf(static_cast<float>(S), 1.0f);
+}
+
+template <int DPC>
+static int kmean_launch(const __half* k, float* kmean, int BH, int S, cudaStream_t stream) {
+  constexpr int smem = 2 * 256 * DPC * 2;
+  static unsigned long long attr_done = 0;
+  if (smem_optin(reinterpret_cast<const void*>(sage_kmean_kernel<DPC>), smem, &attr_done) != QI_OK)
+    return QI_ERR_CUDA;
+  sage_kmean_kernel<DPC><<<dim3(BH, 128 / DPC), 256, smem, stream>>>(k, kmean, S);
+  return QI_OK;
 }
 
 __device__ __forceinline__ float warp_max_f(float v) {
@@ -669,7 +687,13 @@ __global__ void __launch_bounds__(128) sage_quant_k_kernel(const __half* __restr
 int sage_quantize_launch(const void* q, const void* k, int BH, int S, float* kmean, int8_t* qc, float* qs, int8_t* kc,
                          float* ks, cudaStream_t stream) {
   if (BH <= 0 || S <= 0) return QI_ERR_ARG;
-  sage_kmean_kernel<<<dim3(BH, 4), 256, 0, stream>>>(reinterpret_cast<const __half*>(k), kmean, S);
+  // one wave of CTAs: 32, 64 or 128 dims per CTA
+  const int sms = device_num_sms();
+  const __half* kh = reinterpret_cast<const __half*>(k);
+  const int st = (BH * 4 <= sms) ? kmean_launch<32>(kh, kmean, BH, S, stream)
+                 : (BH * 2 <= sms) ? kmean_launch<64>(kh, kmean, BH, S, stream)
+                                   : kmean_launch<128>(kh, kmean, BH, S, stream);
+  if (st != QI_OK) return st;
   sage_quant_q_kernel<<<dim3((S + 127) / 128, BH), 256, 0, stream>>>(reinterpret_cast<const __half*>(q), qc, qs, S);
   sage_quant_k_kernel<<<dim3((S + 63) / 64, BH), 128, 0, stream>>>(reinterpret_cast<const __half*>(k), kmean, kc, ks,
                                                                     S);

@@ -140,7 +140,7 @@ def test_linear_residual_epilogue(M, N, K):
 
 
 # ------------------------------------------------------------------ Sage
-@pytest.mark.parametrize("BH,S", [(2, 200), (1, 77), (2, 384), (48, 1088), (3, 4352), (1, 1)])
+@pytest.mark.parametrize("BH,S", [(2, 200), (1, 77), (2, 384), (48, 1088), (3, 4352), (1, 1), (64, 257), (200, 131)])
 def test_sage_quantizers_bitexact(BH, S):
     q = Q.synth((BH, S, 128), Q.seed_for(13, f"q_{BH}_{S}"), 1.0).half()
     k = Q.synth((BH, S, 128), Q.seed_for(13, f"k_{BH}_{S}"), 1.0).half()
