@@ -16,13 +16,14 @@
 //     accumulation in TMEM; the row sum is accumulated in FP32; the running
 //     max used for P moves only when the row max grows by more than 2^8 (then
 //     O is rescaled in TMEM), which leaves O / l unchanged in exact arithmetic;
-//   * exponentials on MUFU (ex2.approx); a degree-3 polynomial on the FMA
-//     pipe can take a share of them (compile-time option, off by default);
+//   * exponentials on MUFU (ex2.approx, 16 per clock per SM: the bound of
+//     the softmax);
 //   * the result is O * rcp(l) rounded to FP16 (normalize_d, :719-760).
 //
 // Tiling: one CTA per (256 queries, batch-head) = two 128-query tiles that
 // share one K/V stream (keys in blocks of 128, two of the reference's 64-key
-// scale blocks; a three-stage TMA ring).  Warp 0 issues TMA, warp 1 the MMAs,
+// scale blocks; a three-stage TMA ring).  Warp 0 issues TMA, warp 1 the MMAs
+// (the whole warp, converged, with one elected lane issuing each instruction),
 // warps 4-7 run the softmax of tile 0 and warps 8-11 that of tile 1 (one query
 // row per thread, TMEM lane = row); the softmax warpgroups take the registers
 // warpgroup 0 does not need (setmaxnreg).  TMEM holds, per tile, S (128 columns)
@@ -55,20 +56,13 @@ constexpr int MAX_S = 131072;          // K scales of up to 8192 64-key blocks f
 constexpr int smem_bytes(int ngk) { return OFF_KS + ngk * 4 + 1024; }
 constexpr int THREADS = 384;  // warpgroup 0: TMA warp, MMA warp, 2 idle; warpgroups 1, 2: softmax of tiles 0, 1
 // Register split (setmaxnreg): launched at 168 per thread (384 x 168 = 64512);
-// warpgroup 0 gives up to 56, the two softmax warpgroups take 224:
-// 128 x 56 + 256 x 224 = 64512.
-constexpr int LAUNCH_REGS = 168, PRODUCER_REGS = 56, SOFTMAX_REGS = 224;
+// warpgroup 0 keeps 88 (the MMA warp holds its descriptors in every lane),
+// the two softmax warpgroups take 208: 128 x 88 + 256 x 208 = 64512.
+constexpr int LAUNCH_REGS = 168, PRODUCER_REGS = 88, SOFTMAX_REGS = 208;
 static_assert(128 * PRODUCER_REGS + 256 * SOFTMAX_REGS <= THREADS * LAUNCH_REGS, "register split exceeds the launch");
 constexpr int TMEM_COLS = 512;
 constexpr int TM_S = 0;    // S / P of tile t at column 128 t
 constexpr int TM_O = 256;  // O of tile t at column 256 + 128 t
-// Optional: every POLY_EVERY-th odd key's exponential on the FMA pipe
-// (exp2_poly) instead of MUFU.  Off by default: measured on B200, the softmax
-// is not MUFU-bound at this tiling and the extra instructions cost time.
-#ifndef QI_ATTN_POLY_EVERY
-#define QI_ATTN_POLY_EVERY 0
-#endif
-constexpr int POLY_EVERY = QI_ATTN_POLY_EVERY;
 }  // namespace attn
 
 struct alignas(64) AttnArgsDev {
@@ -91,22 +85,6 @@ __device__ __forceinline__ float ex2_approx(float x) {
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
-// 2^x for x <= 0 on the FMA/ALU pipes (the POLY_EVERY option): x = n + f with
-// n = round(x), |f| <= 1/2; 2^f by a degree-3 polynomial fitted on [-1/2, 1/2]
-// (max relative error 7.5e-5, under FP16's 4.9e-4 half ulp); 2^n is added to
-// the exponent field.  x is clamped at -125 so the exponent cannot underflow
-// (2^-125 rounds to zero in FP16 anyway).
-__device__ __forceinline__ float exp2_poly(float x) {
-  x = fmaxf(x, -125.0f);
-  const float t = __fadd_rn(x, 12582912.0f);  // 1.5 * 2^23: rounds x to an integer in the low mantissa bits
-  const float n = __fadd_rn(t, -12582912.0f);
-  const float f = __fadd_rn(x, -n);
-  float p = fmaf(0x1.c3f73ep-5f, f, 0x1.f0de18p-3f);
-  p = fmaf(p, f, 0x1.62f31ap-1f);
-  p = fmaf(p, f, 0x1.fff692p-1f);
-  return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
-}
-
 __device__ __forceinline__ float rcp_approx(float x) {
   float y;
   asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -217,36 +195,45 @@ __global__ void __launch_bounds__(attn::THREADS, 1) sage_attn_kernel(const __gri
         }
       }
     } else if (warp == 1) {
-      if (lane == 0) {
-        bool ok = mbar_wait(q_full, 0, abort_flag);
+      {  // the whole warp runs this role; one elected lane issues each MMA / commit
+        // every lane waits; the vote keeps the warp converged for elect.sync
+        auto wait_all = [&](uint64_t* bar, uint32_t parity) {
+          return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag));
+        };
+        bool ok = wait_all(q_full, 0);
         const uint32_t id_qk = idesc_i8(BQ, BKV);
         const uint32_t id_pv = idesc_f16(BQ, D, false, true);
         const uint32_t q_addr = smem_u32(sQ);
+        // Shared-memory descriptors are built once; an operand at a byte offset is
+        // the base descriptor plus offset / 16 in its address field (no carry: shared
+        // addresses stay below 2^18).
+        const uint64_t qd0 = umma_desc_sw128(q_addr, 16, 1024);
+        const uint64_t kd0 = umma_desc_sw128(smem_u32(sK), 16, 1024);
+        const uint64_t vd0 = umma_desc_sw128(smem_u32(sV), V_BYTES / 2, 1024);
         // S_t = Q_t . K^T for the block in stage st
         auto qk = [&](int t, int st) {
-          const uint32_t k_addr = smem_u32(sK + st * K_BYTES);
-          const uint32_t qa = q_addr + t * Q_BYTES;
+          const uint64_t qa = qd0 + static_cast<uint64_t>(t * (Q_BYTES >> 4));
+          const uint64_t kb = kd0 + static_cast<uint64_t>((st * K_BYTES) >> 4);
+          const uint32_t d = tmem + TM_S + 128 * t;
   #pragma unroll
-          for (int k = 0; k < D / 32; ++k)
-            mma_i8_ss(tmem + TM_S + 128 * t, umma_desc_sw128(qa + k * 32, 16, 1024),
-                      umma_desc_sw128(k_addr + k * 32, 16, 1024), id_qk, k > 0 ? 1u : 0u);
-          mma_commit(&s_full[t]);
+          for (int k = 0; k < D / 32; ++k) mma_i8_ss_elect(d, qa + 2 * k, kb + 2 * k, id_qk, k > 0 ? 1u : 0u);
+          mma_commit_elect(&s_full[t]);
         };
         // O_t += P_t . V over keys 64h .. 64h+63 of the block in stage st; P_t is read from TMEM
         auto pv_half = [&](int t, int st, int j, int h) {
-          const uint32_t v_addr = smem_u32(sV + st * V_BYTES);
+          const uint64_t vb = vd0 + static_cast<uint64_t>((st * V_BYTES) >> 4);
+          const uint32_t d = tmem + TM_O + 128 * t, a = tmem + TM_S + 128 * t;
   #pragma unroll
           for (int k4 = 0; k4 < BKV / 32; ++k4) {
             const int kk = h * (BKV / 32) + k4;
-            mma_f16_ts(tmem + TM_O + 128 * t, tmem + TM_S + 128 * t + kk * 8,
-                       umma_desc_sw128(v_addr + kk * 16 * 128, V_BYTES / 2, 1024), id_pv, (j > 0 || kk > 0) ? 1u : 0u);
+            mma_f16_ts_elect(d, a + kk * 8, vb + 128 * kk, id_pv, (j > 0 || kk > 0) ? 1u : 0u);
           }
         };
-        if (ok) ok = mbar_wait(&k_full[0], 0, abort_flag);
+        if (ok) ok = wait_all(&k_full[0], 0);
         if (ok) {
           tc_fence_after();
           for (int t = 0; t < NT; ++t) qk(t, 0);
-          mma_commit(&k_empty[0]);
+          mma_commit_elect(&k_empty[0]);
         }
         for (int j = 0; j < nkb && ok; ++j) {
           const int st = j % STAGES, nst = (j + 1) % STAGES;
@@ -254,32 +241,33 @@ __global__ void __launch_bounds__(attn::THREADS, 1) sage_attn_kernel(const __gri
           const bool more = j + 1 < nkb;
           for (int t = 0; t < NT && ok; ++t) {
             // each half of P_t . V starts as soon as that half of P_t is in TMEM
-            if (!mbar_wait(&p_half[2 * t], j & 1, abort_flag)) { ok = false; break; }
-            if (t == 0 && !mbar_wait(&v_full[st], ph, abort_flag)) { ok = false; break; }
+            if (!wait_all(&p_half[2 * t], j & 1)) { ok = false; break; }
+            if (t == 0 && !wait_all(&v_full[st], ph)) { ok = false; break; }
             tc_fence_after();
             pv_half(t, st, j, 0);
-            if (!mbar_wait(&p_half[2 * t + 1], j & 1, abort_flag)) { ok = false; break; }
+            if (!wait_all(&p_half[2 * t + 1], j & 1)) { ok = false; break; }
             tc_fence_after();
             pv_half(t, st, j, 1);
-            if (j == nkb - 1) mma_commit(&o_final[t]);
-            if (t == NT - 1) mma_commit(&v_empty[st]);
+            if (j == nkb - 1) mma_commit_elect(&o_final[t]);
+            if (t == NT - 1) mma_commit_elect(&v_empty[st]);
             if (more) {
-              if (t == 0 && !mbar_wait(&k_full[nst], nph, abort_flag)) { ok = false; break; }
+              if (t == 0 && !wait_all(&k_full[nst], nph)) { ok = false; break; }
               // QK(j+1) overwrites the S_t / P_t columns that P_t . V of block j
               // reads; the tensor pipe runs one CTA's MMAs in issue order, so it
               // is issued right behind it.
               tc_fence_after();
               qk(t, nst);
-              if (t == NT - 1) mma_commit(&k_empty[nst]);
+              if (t == NT - 1) mma_commit_elect(&k_empty[nst]);
             }
           }
         }
-        if (!ok) {
+        if (!ok && lane == 0) {
           *abort_flag = 1;
           atomicCAS(args.err, 0, kErrTimeoutMma);
         }
+        __syncwarp();
         // every MMA this thread issued has completed before TMEM is released
-        mma_commit(drain);
+        mma_commit_elect(drain);
         drain_wait(drain, 0);
       }
     }
@@ -319,6 +307,8 @@ __global__ void __launch_bounds__(attn::THREADS, 1) sage_attn_kernel(const __gri
         for (int g = 0; g < 4; ++g) kf[h * 4 + g] = (kb64 * 64 < S) ? sKS[kb64 * 4 + g] * qsm : 1.0f;
       }
       tmem_ld_wait();
+#pragma unroll
+      for (int q = 0; q < BKV / 32; ++q) tmem_reg_fence32(*reinterpret_cast<uint32_t(*)[32]>(r + 32 * q));
       const bool tail = (j + 1) * BKV > S;  // last block reaches past the sequence end
       if (tail) {
 #pragma unroll
@@ -352,6 +342,7 @@ __global__ void __launch_bounds__(attn::THREADS, 1) sage_attn_kernel(const __gri
           uint32_t o[32];
           tmem_ld32(o_tm + c, o);
           tmem_ld_wait();
+          tmem_reg_fence32(o);
 #pragma unroll
           for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
           tmem_st32(o_tm + c, o);
@@ -362,9 +353,8 @@ __global__ void __launch_bounds__(attn::THREADS, 1) sage_attn_kernel(const __gri
       float kb[8];
 #pragma unroll
       for (int g = 0; g < 8; ++g) kb[g] = fmaf(-12582912.0f, kf[g], -m_use);
-      // P = exp2(.) -> packed FP16 pairs over columns 0-63 of S_t (one odd key in
-      // POLY_EVERY on the FMA pipe, the rest on MUFU); the row sum accumulates
-      // the FP32 values in 8 partial sums.
+      // P = exp2(.) -> packed FP16 pairs over columns 0-63 of S_t; the row sum
+      // accumulates the FP32 values in 8 partial sums.
       float lp[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
       const int valid = S - j * BKV;  // keys of this block inside the sequence
       // TAIL: the last block, whose keys past the sequence end get P = 0
@@ -379,8 +369,7 @@ __global__ void __launch_bounds__(attn::THREADS, 1) sage_attn_kernel(const __gri
           const float x0 = fmaf(__int_as_float(static_cast<int>(r[i0]) + 0x4B400000), kf[g0], kb[g0]);
           const float x1 = fmaf(__int_as_float(static_cast<int>(r[i1]) + 0x4B400000), kf[g1], kb[g1]);
           float p0 = ex2_approx(x0);
-          float p1 = (POLY_EVERY > 0 && c % (POLY_EVERY > 0 ? POLY_EVERY : 1) == POLY_EVERY - 1) ? exp2_poly(x1)
-                                                                                           : ex2_approx(x1);
+          float p1 = ex2_approx(x1);
           if (TAIL) {
             if (i0 >= valid) p0 = 0.0f;
             if (i1 >= valid) p1 = 0.0f;
@@ -459,6 +448,7 @@ __global__ void __launch_bounds__(attn::THREADS, 1) sage_attn_kernel(const __gri
         uint32_t r[32];
         tmem_ld32(o_tm + c, r);
         tmem_ld_wait();
+        tmem_reg_fence32(r);
         if (!valid) continue;
         if (args.out_mode == 0) {
           float* dst = reinterpret_cast<float*>(args.out) + (static_cast<size_t>(bh) * S + qrow) * D + c;
