@@ -297,12 +297,20 @@ __global__ void __launch_bounds__(gemm::THREADS, 1) gemm_kernel(const __grid_con
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    {
+      // the whole warp runs this role: every lane waits (the vote keeps the warp
+      // converged) and one elected lane issues each MMA / commit
+      auto wait_all = [&](uint64_t* bar, uint32_t parity) {
+        return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag));
+      };
       int stage = 0;
       uint32_t phase = 0;
       int local = 0;
       bool ok = true;
       const uint32_t idesc = BF16 ? idesc_bf16(BM, BN) : idesc_i8(BM, BN);
+      // descriptors built once; an operand at a byte offset is the base plus
+      // offset / 16 in the address field (shared addresses stay below 2^18)
+      const uint64_t ad0 = umma_desc_sw128(smem_u32(sA), 16, 1024), bd0 = umma_desc_sw128(smem_u32(sB), 16, 1024);
       for (int t = blockIdx.x; t < args.total_tiles && ok; t += gridDim.x, ++local) {
         int pi, m0, n0;
         locate(t, pi, m0, n0);
@@ -310,44 +318,43 @@ __global__ void __launch_bounds__(gemm::THREADS, 1) gemm_kernel(const __grid_con
         const int kblocks = (P.K * (BF16 ? 2 : 1) + BK - 1) / BK;
         const int buf = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
-        if (!mbar_wait(&tempty[buf], acc_phase ^ 1u, abort_flag)) {
+        if (!wait_all(&tempty[buf], acc_phase ^ 1u)) {
           ok = false;
           break;
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + buf * BN;
         for (int kb = 0; kb < kblocks; ++kb) {
-          if (!mbar_wait(&full[stage], phase, abort_flag)) {
+          if (!wait_all(&full[stage], phase)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t a_addr = smem_u32(sA + stage * A_BYTES);
-          const uint32_t b_addr = smem_u32(sB + stage * B_BYTES);
+          const uint64_t ad = ad0 + static_cast<uint64_t>((stage * A_BYTES) >> 4);
+          const uint64_t bd = bd0 + static_cast<uint64_t>((stage * B_BYTES) >> 4);
 #pragma unroll
           for (int k = 0; k < BK / 32; ++k) {
-            uint64_t ad = umma_desc_sw128(a_addr + k * 32, 16, 1024);
-            uint64_t bd = umma_desc_sw128(b_addr + k * 32, 16, 1024);
             if (BF16)
-              mma_f16_ss(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+              mma_f16_ss_elect(d_tmem, ad + 2 * k, bd + 2 * k, idesc, (kb | k) != 0 ? 1u : 0u);
             else
-              mma_i8_ss(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+              mma_i8_ss_elect(d_tmem, ad + 2 * k, bd + 2 * k, idesc, (kb | k) != 0 ? 1u : 0u);
           }
-          mma_commit(&empty[stage]);
+          mma_commit_elect(&empty[stage]);
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1u;
           }
         }
         if (!ok) break;
-        mma_commit(&tfull[buf]);
+        mma_commit_elect(&tfull[buf]);
       }
-      if (!ok) {
+      if (!ok && lane == 0) {
         *abort_flag = 1;
         atomicCAS(args.err, 0, kErrTimeoutMma);
       }
+      __syncwarp();
       // every MMA issued above has completed before TMEM is released
-      mma_commit(drain);
+      mma_commit_elect(drain);
       const uint64_t t0 = global_timer_ns();
       while (!mbar_try_wait(drain, 0) && global_timer_ns() - t0 < kWaitLimitNs / 4) {
       }
@@ -517,12 +524,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(gemm::THREADS, 1)
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer (even CTA)
-    if (lane == 0 && leader) {
+    if (leader) {
+      // the whole warp runs this role: every lane waits (the vote keeps the warp
+      // converged) and one elected lane issues each MMA / commit
+      auto wait_all = [&](uint64_t* bar, uint32_t parity) {
+        return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag));
+      };
       int stage = 0;
       uint32_t phase = 0;
       int local = 0;
       bool ok = true;
       const uint32_t idesc = idesc_i8(BM, BN);
+      const uint64_t ad0 = umma_desc_sw128(smem_u32(sA), 16, 1024), bd0 = umma_desc_sw128(smem_u32(sB), 16, 1024);
       for (int t = cluster; t < args.total_tiles && ok; t += nclusters, ++local) {
         int pi, m0, n0;
         locate(t, pi, m0, n0);
@@ -530,39 +543,39 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(gemm::THREADS, 1)
         const int kblocks = (P.K + BK - 1) / BK;
         const int buf = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
-        if (!mbar_wait(&tempty[buf], acc_phase ^ 1u, abort_flag)) {
+        if (!wait_all(&tempty[buf], acc_phase ^ 1u)) {
           ok = false;
           break;
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + buf * BN;
         for (int kb = 0; kb < kblocks; ++kb) {
-          if (!mbar_wait(&full[stage], phase, abort_flag)) {
+          if (!wait_all(&full[stage], phase)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t a_addr = smem_u32(sA + stage * A_BYTES);
-          const uint32_t b_addr = smem_u32(sB + stage * B_BYTES);
+          const uint64_t ad = ad0 + static_cast<uint64_t>((stage * A_BYTES) >> 4);
+          const uint64_t bd = bd0 + static_cast<uint64_t>((stage * B_BYTES) >> 4);
 #pragma unroll
           for (int k = 0; k < BK / 32; ++k)
-            mma_i8_ss_pair(d_tmem, umma_desc_sw128(a_addr + k * 32, 16, 1024),
-                           umma_desc_sw128(b_addr + k * 32, 16, 1024), idesc, (kb | k) != 0 ? 1u : 0u);
-          mma_commit_pair(&empty[stage], 0x3);  // the stage is free in both CTAs
+            mma_i8_ss_pair_elect(d_tmem, ad + 2 * k, bd + 2 * k, idesc, (kb | k) != 0 ? 1u : 0u);
+          mma_commit_pair_elect(&empty[stage], 0x3);  // the stage is free in both CTAs
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1u;
           }
         }
         if (!ok) break;
-        mma_commit_pair(&tfull[buf], 0x3);  // both CTAs' accumulator rows are ready
+        mma_commit_pair_elect(&tfull[buf], 0x3);  // both CTAs' accumulator rows are ready
       }
-      if (!ok) {
+      if (!ok && lane == 0) {
         *abort_flag = 1;
         atomicCAS(args.err, 0, kErrTimeoutMma);
       }
+      __syncwarp();
       // every MMA issued above (it writes both CTAs' TMEM) completes before teardown
-      mma_commit_pair(drain, 0x1);
+      mma_commit_pair_elect(drain, 0x1);
       const uint64_t t0 = global_timer_ns();
       while (!mbar_try_wait(drain, 0) && global_timer_ns() - t0 < kWaitLimitNs / 4) {
       }
