@@ -100,14 +100,12 @@ __device__ __forceinline__ bool epilogue_tile(const GemmArgsDev& args, const Gem
   const int grow = r0 + lane;
   const float sa = (grow < P.M && !BF16) ? __ldg(P.sa + grow) : 0.0f;
   const uint32_t taddr_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + buf * BN;
-#pragma unroll 1
-  for (int c = 0; c < nch; ++c) {
+  if (r0 >= P.M) return true;  // the whole 32-row slab is past M (all lanes agree)
+  // One chunk: dequant (+GELU / gated residual) of `acc` -> staging -> TMA store.
+  auto chunk = [&](const uint32_t (&acc)[32], int c) -> bool {
     const int b = c & 1;
     uint8_t* sbuf = ebuf + b * EPI_BUF;
-    uint32_t acc[32];
-    tmem_ld32(taddr_row + c * 32, acc);
-    tmem_ld_wait();
-    if (r0 >= P.M) continue;  // the whole 32-row slab is past M (all lanes agree)
+    bool w;
     const int gcol = n0 + c * 32;
     if (resid) {
       // prefetch the next chunk's residual into the other buffer
@@ -175,6 +173,29 @@ __device__ __forceinline__ bool epilogue_tile(const GemmArgsDev& args, const Gem
     if (lane == 0) {
       tma_store_2d(&P.tmO, sbuf, gcol, r0);
       bulk_commit();
+    }
+    return true;
+  };
+  // TMEM loads run one chunk ahead of the dequant: chunk c + 1 is in flight
+  // while chunk c is computed (two register buffers, unrolled by two).
+  uint32_t acc0[32], acc1[32];
+  tmem_ld32(taddr_row, acc0);
+#pragma unroll 1
+  for (int c = 0; c < nch; c += 2) {
+    tmem_ld_wait();
+    tmem_reg_fence32(acc0);
+    if (c + 1 < nch) tmem_ld32(taddr_row + (c + 1) * 32, acc1);
+    if (!chunk(acc0, c)) {
+      tmem_ld_wait();
+      return false;
+    }
+    if (c + 1 >= nch) break;
+    tmem_ld_wait();
+    tmem_reg_fence32(acc1);
+    if (c + 2 < nch) tmem_ld32(taddr_row + (c + 2) * 32, acc0);
+    if (!chunk(acc1, c + 1)) {
+      tmem_ld_wait();
+      return false;
     }
   }
   return true;
