@@ -514,59 +514,60 @@ __device__ __forceinline__ int8_t cvt_rni_sat_s8(float x) {
 
 // K mean per (batch-head, dim): the reference sums over tokens serially in
 // token order (sageattention_sm80.cu:759-773); the K codes depend on it, so the
-// order is kept.  One CTA per (batch-head, DPC dims): all 256 threads prefetch
-// the next 256-token x DPC-dim tile into shared memory while DPC/32 warps run
-// the serial chains (lane = dim) over the current one.  DPC is chosen so the
-// grid is a single wave: the chains are the kernel's whole cost.
+// order is kept.  One CTA per (batch-head, DPC dims): DPC/32 warps run the
+// serial chains (lane = dim) over 32 KB tiles of T tokens x DPC dims in shared
+// memory, which all 256 threads fill with cp.async three tiles ahead (a
+// four-buffer ring, one __syncthreads per tile).  DPC is chosen so the grid is a
+// single wave: the chains are the kernel's whole cost.
 template <int DPC>
 __global__ void __launch_bounds__(256) sage_kmean_kernel(const __half* __restrict__ k, float* __restrict__ kmean, int S) {
-  constexpr int T = 256;
-  constexpr int PRE = DPC / 8;  // 16-byte pieces per thread per tile
-  extern __shared__ __align__(16) __half km_tile[];  // [2][T][DPC]
+  constexpr int T = 16384 / DPC;  // tokens per 32 KB tile
+  constexpr int NB = 4;           // ring buffers
+  constexpr int PIECES = T * DPC / 8 / 256;  // 16-byte pieces per thread per tile
+  extern __shared__ __align__(16) __half km_tile[];  // [NB][T][DPC]
   const int bh = blockIdx.x, d0 = blockIdx.y * DPC;
   const __half* base = k + static_cast<size_t>(bh) * S * 128 + d0;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int nchunks = (S + T - 1) / T;
-  uint4 pre[PRE];
-  auto load = [&](int c) {
+  const int ntiles = (S + T - 1) / T;
+  // copies of tile c into buffer c % NB (rows past S are not copied and not read)
+  auto issue = [&](int c) {
+    if (c < ntiles) {
+      __half* buf = km_tile + static_cast<size_t>(c % NB) * T * DPC;
 #pragma unroll
-    for (int r = 0; r < PRE; ++r) {
-      const int i = tid + 256 * r;  // piece index in the tile
-      const int t = c * T + i / (DPC / 8), piece = i % (DPC / 8);
-      pre[r] = (t < S) ? *reinterpret_cast<const uint4*>(base + static_cast<size_t>(t) * 128 + piece * 8)
-                       : make_uint4(0, 0, 0, 0);
+      for (int r = 0; r < PIECES; ++r) {
+        const int i = tid + 256 * r;
+        const int t = c * T + i / (DPC / 8), piece = i % (DPC / 8);
+        if (t < S) {
+          const uint32_t dst = smem_u32(buf + (i / (DPC / 8)) * DPC + piece * 8);
+          const __half* src = base + static_cast<size_t>(t) * 128 + piece * 8;
+          asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+        }
+      }
     }
+    asm volatile("cp.async.commit_group;" ::: "memory");  // one group per tile, empty past the end
   };
-  auto stash = [&](int b) {
-#pragma unroll
-    for (int r = 0; r < PRE; ++r) {
-      const int i = tid + 256 * r;
-      *reinterpret_cast<uint4*>(km_tile + (static_cast<size_t>(b) * T + i / (DPC / 8)) * DPC + (i % (DPC / 8)) * 8) =
-          pre[r];
-    }
-  };
+  issue(0);
+  issue(1);
+  issue(2);
   float sum = 0.0f;
-  load(0);
-  stash(0);
-  __syncthreads();
-  for (int c = 0; c < nchunks; ++c) {
-    if (c + 1 < nchunks) load(c + 1);
+  for (int c = 0; c < ntiles; ++c) {
+    asm volatile("cp.async.wait_group 2;" ::: "memory");  // this thread's copies of tile c have landed
+    __syncthreads();  // everyone's have; and every chain has left the buffer refilled next
+    issue(c + 3);
     if (warp < DPC / 32) {
       const int n = min(T, S - c * T);
-      const __half* col = km_tile + static_cast<size_t>(c & 1) * T * DPC + warp * 32 + lane;
+      const __half* col = km_tile + static_cast<size_t>(c % NB) * T * DPC + warp * 32 + lane;
 #pragma unroll 8
       for (int t = 0; t < n; ++t) sum += __half2float(col[t * DPC]);
     }
-    __syncthreads();
-    if (c + 1 < nchunks) stash((c + 1) & 1);
-    __syncthreads();
   }
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
   if (warp < DPC / 32) kmean[bh * 128 + d0 + warp * 32 + lane] = sum / fmaxf(static_cast<float>(S), 1.0f);
 }
 
 template <int DPC>
 static int kmean_launch(const __half* k, float* kmean, int BH, int S, cudaStream_t stream) {
-  constexpr int smem = 2 * 256 * DPC * 2;
+  constexpr int smem = 4 * 32768;
   static unsigned long long attr_done = 0;
   if (smem_optin(reinterpret_cast<const void*>(sage_kmean_kernel<DPC>), smem, &attr_done) != QI_OK)
     return QI_ERR_CUDA;
@@ -630,34 +631,41 @@ __global__ void __launch_bounds__(256) sage_quant_q_kernel(const __half* __restr
 }
 
 // K per-thread INT8 after mean smoothing (sageattention_sm80.cu:826-886): one
-// CTA per (64-key block, batch-head), warp w = scale group w covering tokens
-// 2w + 8i + {0, 1}, i = 0..7.
-__global__ void __launch_bounds__(128) sage_quant_k_kernel(const __half* __restrict__ k, const float* __restrict__ kmean,
+// CTA per (128 keys, batch-head); warp w handles scale group w % 4 of 64-key
+// block w / 4, tokens 2 (w % 4) + 8i + {0, 1}, i = 0..7, lane = 4 dims.  Two
+// passes over the group's 4 KB: the absolute max, then (from L1) the codes --
+// few registers, so many warps per SM keep enough loads in flight.
+__global__ void __launch_bounds__(256) sage_quant_k_kernel(const __half* __restrict__ k, const float* __restrict__ kmean,
                                                            int8_t* __restrict__ kc, float* __restrict__ ks, int S) {
-  const int blk = blockIdx.x, bh = blockIdx.y;
-  const int g = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int bh = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int blk = blockIdx.x * 2 + (warp >> 2), g = warp & 3;
+  if (blk * 64 >= S) return;  // the second block of the last CTA may not exist
   const __half* hp = k + static_cast<size_t>(bh) * S * 128 + lane * 4;
   int8_t* out = kc + static_cast<size_t>(bh) * S * 128 + lane * 4;
   const float4 mean = *reinterpret_cast<const float4*>(kmean + bh * 128 + lane * 4);
   const int token_base = blk * 64 + g * 2;
-  float vals[16][4];
-  float amax = 1e-7f;
-#pragma unroll
-  for (int i = 0; i < 16; ++i) {
+  auto load = [&](int i, float (&v)[4]) {
     const int t = token_base + (i >> 1) * 8 + (i & 1);
-    uint2 raw = make_uint2(0, 0);
     const bool in = t < S;
+    uint2 raw = make_uint2(0, 0);
     if (in) raw = *reinterpret_cast<const uint2*>(hp + static_cast<size_t>(t) * 128);
     const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
     const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
-    vals[i][0] = in ? a.x - mean.x : 0.0f;
-    vals[i][1] = in ? a.y - mean.y : 0.0f;
-    vals[i][2] = in ? b.x - mean.z : 0.0f;
-    vals[i][3] = in ? b.y - mean.w : 0.0f;
+    v[0] = in ? a.x - mean.x : 0.0f;
+    v[1] = in ? a.y - mean.y : 0.0f;
+    v[2] = in ? b.x - mean.z : 0.0f;
+    v[3] = in ? b.y - mean.w : 0.0f;
+  };
+  float am[4] = {1e-7f, 1e-7f, 1e-7f, 1e-7f};
 #pragma unroll
-    for (int e = 0; e < 4; ++e) amax = fmaxf(amax, fabsf(vals[i][e]));
+  for (int i = 0; i < 16; ++i) {
+    float v[4];
+    load(i, v);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) am[i & 3] = fmaxf(am[i & 3], fabsf(v[e]));
   }
-  const float block_amax = warp_max_f(amax);
+  const float block_amax = warp_max_f(fmaxf(fmaxf(am[0], am[1]), fmaxf(am[2], am[3])));
   const float block_scale = block_amax / 127.0f + 1e-7f;
   if (lane == 0) ks[static_cast<size_t>(bh) * (((S + 63) / 64) * 4) + blk * 4 + g] = block_scale;
   const float inv_scale = 1.0f / block_scale;
@@ -665,11 +673,13 @@ __global__ void __launch_bounds__(128) sage_quant_k_kernel(const __half* __restr
   for (int i = 0; i < 16; ++i) {
     const int t = token_base + (i >> 1) * 8 + (i & 1);
     if (t >= S) continue;
+    float v[4];
+    load(i, v);
     char4 c;
-    c.x = cvt_rni_sat_s8(vals[i][0] * inv_scale);
-    c.y = cvt_rni_sat_s8(vals[i][1] * inv_scale);
-    c.z = cvt_rni_sat_s8(vals[i][2] * inv_scale);
-    c.w = cvt_rni_sat_s8(vals[i][3] * inv_scale);
+    c.x = cvt_rni_sat_s8(v[0] * inv_scale);
+    c.y = cvt_rni_sat_s8(v[1] * inv_scale);
+    c.z = cvt_rni_sat_s8(v[2] * inv_scale);
+    c.w = cvt_rni_sat_s8(v[3] * inv_scale);
     *reinterpret_cast<char4*>(out + static_cast<size_t>(t) * 128) = c;
   }
 }
@@ -685,8 +695,8 @@ int sage_quantize_launch(const void* q, const void* k, int BH, int S, float* kme
                                    : kmean_launch<128>(kh, kmean, BH, S, stream);
   if (st != QI_OK) return st;
   sage_quant_q_kernel<<<dim3((S + 127) / 128, BH), 256, 0, stream>>>(reinterpret_cast<const __half*>(q), qc, qs, S);
-  sage_quant_k_kernel<<<dim3((S + 63) / 64, BH), 128, 0, stream>>>(reinterpret_cast<const __half*>(k), kmean, kc, ks,
-                                                                    S);
+  sage_quant_k_kernel<<<dim3((S + 127) / 128, BH), 256, 0, stream>>>(reinterpret_cast<const __half*>(k), kmean, kc, ks,
+                                                                     S);
   return cudaGetLastError() == cudaSuccess ? QI_OK : QI_ERR_CUDA;
 }
 
