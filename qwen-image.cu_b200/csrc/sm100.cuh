@@ -232,34 +232,8 @@ __host__ __device__ constexpr uint32_t idesc_bf16(int M, int N) {
          (static_cast<uint32_t>(M >> 4) << 24);
 }
 
-__device__ __forceinline__ void mma_i8_ss(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                          uint32_t accumulate) {
-  asm volatile(
-      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-      " tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-__device__ __forceinline__ void mma_f16_ss(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                           uint32_t accumulate) {
-  asm volatile(
-      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-// kind::f16 with the A operand (M rows = TMEM lanes, K packed two FP16 per
-// 32-bit column) read from tensor memory instead of shared memory.
-__device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
-                                           uint32_t accumulate) {
-  asm volatile(
-      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-      " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(d_tmem),
-      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-// Warp-collective forms: every lane of a converged warp executes them and one
-// elected lane issues.  Descriptors computed by the whole warp are warp-uniform,
+// MMA issue, warp-collective: every lane of a converged warp executes these and
+// one elected lane issues.  Descriptors computed by the whole warp are warp-uniform,
 // and the issuing warp does not run divergent single-lane code, which keeps its
 // instruction stream short when it shares a scheduler with busy warps.
 __device__ __forceinline__ void mma_i8_ss_elect(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
@@ -270,6 +244,8 @@ __device__ __forceinline__ void mma_i8_ss_elect(uint32_t d_tmem, uint64_t adesc,
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
+// kind::f16 with the A operand (M rows = TMEM lanes, K packed two FP16 per
+// 32-bit column) read from tensor memory instead of shared memory.
 __device__ __forceinline__ void mma_f16_ts_elect(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
                                                  uint32_t accumulate) {
   asm volatile(
@@ -286,21 +262,14 @@ __device__ __forceinline__ void mma_f16_ss_elect(uint32_t d_tmem, uint64_t adesc
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
+// Arrives once on the mbarrier when all MMAs previously issued by this warp
+// have completed.
 __device__ __forceinline__ void mma_commit_elect(uint64_t* bar) {
   asm volatile(
       "{\n .reg .pred e;\n elect.sync _|e, 0xffffffff;\n"
       " @e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n}\n" ::"r"(smem_u32(bar))
       : "memory");
 }
-
-// Arrives once on the mbarrier when all previously issued MMAs of this thread
-// have completed.
-__device__ __forceinline__ void mma_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-               : "memory");
-}
-
-__device__ __forceinline__ uint32_t elect_lane0() { return (threadIdx.x & 31) == 0; }
 
 // ---------------------------------------------------------------- CTA pairs
 // Two CTAs of a cluster computing one M = 256 tile (tcgen05 cta_group::2):
@@ -334,23 +303,6 @@ __device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* t
       "l"(reinterpret_cast<uint64_t>(tm)), "r"(bar_cluster_addr), "r"(c0), "r"(c1)
       : "memory");
 }
-__device__ __forceinline__ void mma_i8_ss_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                               uint32_t accumulate) {
-  asm volatile(
-      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-      " tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-// Arrives once on the mbarrier at `bar`'s offset in every CTA of `cta_mask`
-// when all previously issued pair MMAs have completed.
-__device__ __forceinline__ void mma_commit_pair(uint64_t* bar, uint16_t cta_mask) {
-  asm volatile(
-      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
-          smem_u32(bar)),
-      "h"(cta_mask)
-      : "memory");
-}
 // Warp-collective pair forms (one elected lane issues), as above.
 __device__ __forceinline__ void mma_i8_ss_pair_elect(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
                                                      uint32_t accumulate) {
@@ -360,6 +312,8 @@ __device__ __forceinline__ void mma_i8_ss_pair_elect(uint32_t d_tmem, uint64_t a
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
+// Arrives once on the mbarrier at `bar`'s offset in every CTA of `cta_mask`
+// when all previously issued pair MMAs have completed.
 __device__ __forceinline__ void mma_commit_pair_elect(uint64_t* bar, uint16_t cta_mask) {
   asm volatile(
       "{\n .reg .pred e;\n elect.sync _|e, 0xffffffff;\n"
