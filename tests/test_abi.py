@@ -45,6 +45,14 @@ def test_argument_validation_without_device():
     assert L.qi_forward(null, null, 1, null, 0.0, null, 8, null, 8, 8, null, null) == 1
     assert L.qi_model_create(null, 1, null, null, None) == 1
     assert L.qi_rope_table(8, 8, 8, null) == 1
+    # the allocation-free linear checks its arguments and its scratch limits
+    # (4096 rows, 4 Mi codes) before it looks for a device; pointers that are
+    # never dereferenced stand in for buffers
+    p = ctypes.c_void_p(256)
+    assert L.qi_linear_i8_f32in_noalloc(null, 4, 256, null, null, 64, null, 0, null, null) == 1
+    assert L.qi_linear_i8_f32in_noalloc(p, 4097, 256, p, p, 64, null, 0, p, null) == 5
+    assert L.qi_linear_i8_f32in_noalloc(p, 4096, 2048, p, p, 64, null, 0, p, null) == 5
+    assert L.qi_linear_i8_f32in_noalloc(p, 0, 256, p, p, 64, null, 0, p, null) == 0
 
 
 @pytest.mark.parametrize("h,w,n_txt", [(8, 8, 8), (128, 128, 256), (166, 166, 256), (7, 9, 5)])
