@@ -55,6 +55,32 @@ def test_argument_validation_without_device():
     assert L.qi_linear_i8_f32in_noalloc(p, 0, 256, p, p, 64, null, 0, p, null) == 0
 
 
+def test_null_handles_and_buffers_are_rejected_without_device():
+    """Every entry point checks its handles and buffers before any CUDA call:
+    null ones give QI_ERR_ARG (1); destroying a null handle is a no-op; the
+    read-only queries answer 0 for a null handle."""
+    L = Q.lib()
+    null = None
+    assert L.qi_version() > 0
+    assert L.qi_ctx_create(0, null) == 1
+    assert L.qi_ctx_destroy(null) == 0
+    assert L.qi_ctx_check(null) == 1
+    assert L.qi_ctx_last_launch_count(null) == 0
+    assert L.qi_ctx_set_profiling(null, 1) == 1
+    assert L.qi_ctx_profile(null, null, null, 0) == 1
+    assert L.qi_selftest_wait_timeout(null, 1000, null) == 1
+    assert L.qi_comm_unique_id(null) == 1
+    assert L.qi_ctx_set_comm(null, null, 0, 1) == 1
+    assert L.qi_model_load_safetensors(null, null, null) == 1
+    assert L.qi_model_num_blocks(null) == 0
+    assert L.qi_model_destroy(null) == 0
+    assert L.qi_forward_blocks(null, null, 2, 16, 8, null, null, 500.0, null, 0, 1, null) == 1
+    assert L.qi_layer_norm_modulate(null, null, null, null, 4, 64, 1e-6, null) == 1
+    assert L.qi_rms_norm(null, null, null, 4, 64, 1e-6, null) == 1
+    assert L.qi_sage_quantize(null, null, 1, 64, null, null, null, null, null, null) == 1
+    assert L.qi_cfg_euler_step(null, null, null, 4.0, 0.5, 0.4, 8, 8, null, null) == 1
+
+
 @pytest.mark.parametrize("h,w,n_txt", [(8, 8, 8), (128, 128, 256), (166, 166, 256), (7, 9, 5)])
 def test_rope_table_matches_oracle(h, w, n_txt):
     a = Q.rope_table(h, w, n_txt)
