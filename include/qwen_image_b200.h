@@ -78,19 +78,39 @@ int qi_linear_i8_f32in(const float* x, int M, int K, const int8_t* w, const floa
  * that cannot take cudaMalloc's implicit device synchronisation).  The
  * quantised activations live in a fixed scratch array compiled into the
  * library (about 4 MiB per device), so:
- *   - M <= QI_NOALLOC_MAX_ROWS and M * K <= QI_NOALLOC_MAX_CODES, else the
- *     call returns QI_ERR_UNSUPPORTED and launches nothing;
+ *   - M <= QI_NOALLOC_MAX_ROWS, M * K <= QI_NOALLOC_MAX_CODES and
+ *     K <= 12288, else the call returns QI_ERR_UNSUPPORTED; K % 16 != 0, or
+ *     N % 32 != 0 when M > 1 or apply_gelu, is QI_ERR_ARG; w, w_scales (and
+ *     out when M > 1 or apply_gelu) not 16-byte aligned is QI_ERR_ALIGN; none
+ *     of these launches anything or touches the scratch;
  *   - the first call on a device does one-time setup (looks up the scratch
  *     address with that device current): make it before any stream capture;
  *   - the scratch is shared by all calls on a device: calls that can overlap
  *     (different streams or host threads without ordering between them)
  *     race and corrupt each other's results; serialise them.
- * Only the scratch's error word must be zero when the kernels start; the call
- * clears it on `stream` itself.  Codes and scales are fully overwritten.     */
+ * A GEMM whose bounded wait gives up leaves `out` undefined and records the
+ * fact in the scratch's error word, which stays set until
+ * qi_linear_i8_f32in_noalloc_check reads it.                                */
 #define QI_NOALLOC_MAX_ROWS 4096
 #define QI_NOALLOC_MAX_CODES (4 * 1024 * 1024)
 int qi_linear_i8_f32in_noalloc(const float* x, int M, int K, const int8_t* w, const float* w_scales, int N,
                                const void* bias_bf16, int apply_gelu, float* out, void* stream);
+/* Error report of qi_linear_i8_f32in_noalloc on the current device: waits
+ * for the device, then returns QI_ERR_DEVICE (and clears the word) if any
+ * call since the last check gave up a bounded wait, else QI_OK.  Allocates
+ * nothing.  No counterpart in the reference.                                */
+int qi_linear_i8_f32in_noalloc_check(void);
+/* Failure-path self test of that report: a kernel waits on an mbarrier
+ * nothing arrives on and gives up after limit_us (<= 2 s), recording the
+ * timeout in the scratch's error word the way the GEMM does; the next
+ * qi_linear_i8_f32in_noalloc_check returns QI_ERR_DEVICE.  No counterpart in
+ * the reference.                                                            */
+int qi_linear_i8_f32in_noalloc_selftest(int limit_us, void* stream);
+
+/* Number of CUDA allocations (device memory, and pinned host memory for the
+ * checkpoint upload) this library has made since it was loaded, over all
+ * devices.  Lets a caller verify that a call allocated nothing.             */
+long long qi_alloc_count(void);
 
 /* SageAttention on FP16 Q, K, V laid out [BH, S, 128] (head-major):
  * K mean smoothing, per-thread INT8 Q/K quantisation, INT8 QK^T, FP16 P.V,
@@ -116,6 +136,25 @@ int qi_layer_norm_modulate(const float* x, const float* shift, const float* scal
 /* Per-row RMSNorm, FP32 in/out, BF16 weight.  Replaces rms_norm_fp32
  * (cuda_kernels.cuh:510).                                                    */
 int qi_rms_norm(const float* x, const void* w_bf16, float* out, int rows, int dim, float eps, void* stream);
+
+/* LayerNorm + modulate fused with the activation quantizer, the kernel the
+ * forward runs before the QKV and fc1 linears: FP32 [rows, 3072] -> INT8
+ * codes [rows, 3072] + FP32 scales [rows] (block-FWHT 1024).  Replaces the
+ * pair layer_norm_modulate_fp32 (cuda_kernels.cuh:524) +
+ * quantize_activation_int8_hadamard_fp32 (cuda_kernels.cuh:277) of
+ * transformer.cu:526-563.  dim must be 3072.                                 */
+int qi_layer_norm_modulate_quantize(const float* x, const float* shift, const float* scale, int rows, int dim,
+                                    float eps, int8_t* codes, float* scales, void* stream);
+
+/* q/k RMSNorm + joint [txt; img] head-major layout + RoPE -> FP16, the
+ * forward's qkv_post stage on caller buffers.  qkv_img [nb*n_img, 9216] and
+ * qkv_txt [nb*n_txt, 9216] FP32 rows [q | k | v]; norms_bf16 [4][128] =
+ * norm_q, norm_k, norm_added_q, norm_added_k; pe as for qi_forward; output
+ * FP16 [3][nb*24][n_txt + n_img][128] (q, k, v).  Replaces rms_norm_fp32 x 4
+ * + concat_transpose_fused_fp32 x 3 + rope_apply_fp32_to_fp16 x 2
+ * (transformer.cu:618-671; cuda_kernels.cuh:510, 536).                       */
+int qi_qk_norm_rope(const float* qkv_img, const float* qkv_txt, const void* norms_bf16, const float* pe, int nb,
+                    int n_img, int n_txt, void* qkv_f16, void* stream);
 
 /* ------------------------------------------------------------ model level */
 typedef struct qi_ctx qi_ctx;

@@ -8,7 +8,7 @@
 #                               product's drop-in shim instead of transformer.cu
 # Test infrastructure.  main.cu is not built (it needs libpng).
 set -e
-REF=${QI_REFERENCE_DIR:-/root/reference}
+REF=${QI_REFERENCE_DIR:?set QI_REFERENCE_DIR to the reference source tree}
 HERE=$(cd "$(dirname "$0")" && pwd)
 PKG="$HERE/../qwen-image.cu_b200"
 OUT="$HERE/_ref"

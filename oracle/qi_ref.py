@@ -37,6 +37,8 @@ def lib():
             "ref_layer_norm_modulate": [vp, vp, vp, vp, i, i, f],
             "ref_rms_norm_fp32": [vp, vp, vp, i, i, f],
             "ref_rope_table": [i, i, i, vp],
+            "ref_rope_fp16": [vp, vp, vp, i, i],
+            "ref_gate_add": [vp, vp, vp, vp, i, i],
             "ref_transformer_forward": [vp, vp, vp, f, vp, i, vp, i, i, i, vp],
         }
         for name, args in sig.items():
@@ -123,6 +125,20 @@ def layer_norm_modulate(x, shift, scale, eps=1e-6):
 def rms_norm(x, w, eps=1e-6):
     out = torch.empty_like(x)
     _ok(lib().ref_rms_norm_fp32(_p(x), _p(w), _p(out), x.shape[0], x.shape[1], eps))
+    return out
+
+
+def rope_fp16(x, pe):
+    """x: head-major [H, L, 128] FP32, pe [L, 64, 2, 2] -> FP16 [H, L, 128]."""
+    H, L, _ = x.shape
+    out = torch.empty(H, L, 128, dtype=torch.float16, device="cuda")
+    _ok(lib().ref_rope_fp16(_p(x), _p(pe), _p(out), H, L))
+    return out
+
+
+def gate_add(inp, gate, x):
+    out = torch.empty_like(inp)
+    _ok(lib().ref_gate_add(_p(inp), _p(gate), _p(x), _p(out), inp.shape[0], inp.shape[1]))
     return out
 
 

@@ -172,6 +172,18 @@ int ref_rms_norm_fp32(const float* x, const void* w, float* out, int rows, int d
   return sync_status();
 }
 
+// rope_apply_fp32_to_fp16 (cuda_kernels.cu:1939-1971) on head-major [H, L, 128].
+int ref_rope_fp16(const float* x, const float* pe, void* out, int H, int L) {
+  rope_apply_fp32_to_fp16(x, pe, reinterpret_cast<__half*>(out), H, L, 128);
+  return sync_status();
+}
+
+// gate_add_fp32f (cuda_kernels.cu:2181-2197): out = input + gate[col] * x.
+int ref_gate_add(const float* input, const float* gate, const float* x, float* out, int rows, int dim) {
+  gate_add_fp32f(input, gate, x, out, rows, dim);
+  return sync_status();
+}
+
 // RoPE table from the reference's own host code (rope.h:175).
 int ref_rope_table(int h, int w, int n_txt, float* pe_host) {
   std::vector<float> pe = RoPE::gen_qwen_image_pe(h, w, 2, 1, n_txt, 10000, {16, 56, 56});

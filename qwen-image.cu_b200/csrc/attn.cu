@@ -52,7 +52,7 @@ constexpr int OFF_K = OFF_Q + NT * Q_BYTES;
 constexpr int OFF_V = OFF_K + STAGES * K_BYTES;
 constexpr int OFF_BAR = OFF_V + STAGES * V_BYTES;
 constexpr int OFF_KS = OFF_BAR + 256;  // this batch-head's K scales (FP32), loaded once
-constexpr int MAX_S = 131072;          // K scales of up to 8192 64-key blocks fit in shared memory
+constexpr int MAX_S = kAttnMaxS;
 constexpr int smem_bytes(int ngk) { return OFF_KS + ngk * 4 + 1024; }
 constexpr int THREADS = 384;  // warpgroup 0: TMA warp, MMA warp, 2 idle; warpgroups 1, 2: softmax of tiles 0, 1
 // Register split (setmaxnreg): launched at 168 per thread (384 x 168 = 64512);

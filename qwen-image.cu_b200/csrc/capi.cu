@@ -28,6 +28,7 @@
 #include <cuda_bf16.h>
 #include <nccl.h>
 
+#include <atomic>
 #include <cstdlib>
 #include <map>
 #include <mutex>
@@ -56,6 +57,20 @@ CUresult qi_encode_tiled(CUtensorMap* tm, CUtensorMapDataType dt, cuuint32_t ran
     fn = reinterpret_cast<Fn>(p);
   }
   return fn(tm, dt, rank, base, dims, strides, box, estr, il, sw, l2, oob);
+}
+
+namespace {
+std::atomic<long long> g_alloc_count{0};
+}
+
+cudaError_t dev_malloc(void** p, size_t bytes) {
+  g_alloc_count.fetch_add(1, std::memory_order_relaxed);
+  return cudaMalloc(p, bytes);
+}
+
+cudaError_t host_malloc_pinned(void** p, size_t bytes) {
+  g_alloc_count.fetch_add(1, std::memory_order_relaxed);
+  return cudaMallocHost(p, bytes);
 }
 
 int device_num_sms() {
@@ -133,7 +148,7 @@ struct qi_ctx {
     if (buf[id]) cudaFree(buf[id]);
     buf[id] = nullptr;
     cap[id] = 0;
-    if (cudaMalloc(&buf[id], bytes) != cudaSuccess) return QI_ERR_OOM;
+    if (dev_malloc(&buf[id], bytes) != cudaSuccess) return QI_ERR_OOM;
     cap[id] = bytes;
     return QI_OK;
   }
@@ -167,7 +182,7 @@ struct qi_model {
   template <typename T>
   T* alloc(size_t n) {
     void* p = nullptr;
-    if (cudaMalloc(&p, n * sizeof(T)) != cudaSuccess) return nullptr;
+    if (dev_malloc(&p, n * sizeof(T)) != cudaSuccess) return nullptr;
     allocs.push_back(p);
     return reinterpret_cast<T*>(p);
   }
@@ -195,13 +210,15 @@ const char* qi_status_string(int st) {
 
 int qi_version(void) { return 1; }
 
+long long qi_alloc_count(void) { return g_alloc_count.load(std::memory_order_relaxed); }
+
 int qi_ctx_create(int device, qi_ctx** out) {
   if (!out) return QI_ERR_ARG;
   if (cudaSetDevice(device) != cudaSuccess) return QI_ERR_CUDA;
   qi_ctx* c = new qi_ctx();
   c->device = device;
   c->num_sms = device_num_sms();
-  if (cudaMalloc(&c->err, sizeof(int)) != cudaSuccess) {
+  if (dev_malloc(reinterpret_cast<void**>(&c->err), sizeof(int)) != cudaSuccess) {
     delete c;
     return QI_ERR_OOM;
   }
@@ -385,6 +402,7 @@ int qi_sage_attention(const void* q_f16, const void* k_f16, const void* v_f16, f
                       int D, void* stream) {
   if (D != 128) return QI_ERR_UNSUPPORTED;
   if (!q_f16 || !k_f16 || !v_f16 || !out || BH <= 0 || S <= 0) return QI_ERR_ARG;
+  if (S > kAttnMaxS) return QI_ERR_UNSUPPORTED;  // before any workspace grows or kernel runs
   qi_ctx* c = default_ctx();
   if (!c) return QI_ERR_CUDA;
   const size_t n = static_cast<size_t>(BH) * S * 128;
@@ -409,6 +427,26 @@ int qi_layer_norm_modulate(const float* x, const float* shift, const float* scal
 int qi_rms_norm(const float* x, const void* w_bf16, float* out, int rows, int dim, float eps, void* stream) {
   if (!x || !w_bf16 || !out || rows < 0 || dim <= 0) return QI_ERR_ARG;
   return rmsnorm_f32_launch(x, w_bf16, out, rows, dim, eps, S_(stream));
+}
+
+int qi_layer_norm_modulate_quantize(const float* x, const float* shift, const float* scale, int rows, int dim,
+                                    float eps, int8_t* codes, float* scales, void* stream) {
+  if (!x || !shift || !scale || !codes || !scales || rows < 0 || dim <= 0) return QI_ERR_ARG;
+  if (dim != kDim) return QI_ERR_UNSUPPORTED;
+  RowSeg seg{x, dim, shift, scale, rows};
+  return rowquant_launch(kSrcLnMod, dim, dim & (-dim), &seg, 1, codes, scales, eps, S_(stream));
+}
+
+int qi_qk_norm_rope(const float* qkv_img, const float* qkv_txt, const void* norms_bf16, const float* pe, int nb,
+                    int n_img, int n_txt, void* qkv_f16, void* stream) {
+  if (!qkv_img || !qkv_txt || !norms_bf16 || !pe || !qkv_f16 || nb < 1 || n_img < 0 || n_txt < 0) return QI_ERR_ARG;
+  if ((reinterpret_cast<uintptr_t>(qkv_img) | reinterpret_cast<uintptr_t>(qkv_txt) |
+       reinterpret_cast<uintptr_t>(pe) | reinterpret_cast<uintptr_t>(qkv_f16)) & 15)
+    return QI_ERR_ALIGN;
+  const __nv_bfloat16* n = static_cast<const __nv_bfloat16*>(norms_bf16);
+  QkvPostArgs a{qkv_img, qkv_txt, n, n + kHeadDim, n + 2 * kHeadDim, n + 3 * kHeadDim, pe, qkv_f16, nb, n_img, n_txt,
+                0, n_img, 0, n_txt, kHeads, 0};
+  return qkv_post_launch(a, S_(stream));
 }
 
 int qi_rope_table(int h, int w, int n_txt, float* pe_host) {
@@ -641,11 +679,11 @@ int setup_peers(Fwd& f) {
   const int P = f.P, me = f.rank;
   constexpr int kH = sizeof(cudaIpcMemHandle_t);
   if (!c->flags) {
-    if (cudaMalloc(&c->flags, 2 * kMaxRanks * sizeof(unsigned)) != cudaSuccess) return QI_ERR_OOM;
+    if (dev_malloc(reinterpret_cast<void**>(&c->flags), 2 * kMaxRanks * sizeof(unsigned)) != cudaSuccess) return QI_ERR_OOM;
     if (cudaMemset(c->flags, 0, 2 * kMaxRanks * sizeof(unsigned)) != cudaSuccess) return QI_ERR_CUDA;
     c->epoch = 0;
   }
-  if (!c->handles && cudaMalloc(&c->handles, (kMaxRanks + 1) * 3 * kH + sizeof(int) * 2) != cudaSuccess)
+  if (!c->handles && dev_malloc(&c->handles, (kMaxRanks + 1) * 3 * kH + sizeof(int) * 2) != cudaSuccess)
     return QI_ERR_OOM;
   cudaIpcMemHandle_t mine[3];
   // QI_PEER_EXCHANGE=0 selects the NCCL exchanges (the same on every rank)

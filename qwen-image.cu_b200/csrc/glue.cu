@@ -91,9 +91,23 @@ __global__ void qkv_post_kernel(QkvPostArgs a) {
   }
 
   auto norm_rope = [&](float4 x, const __nv_bfloat16* w, __half* out) {
-    float ss = x.x * x.x + x.y * x.y + x.z * x.z + x.w * x.w;
-    ss = warp_sum(ss);
-    const float rms = rsqrtf(ss / kHeadDim + 1e-6f);
+    // sum of squares in the order of rms_norm_fp32_kernel's reduction (128
+    // threads, thread t = element t, shfl_down 16..1 per warp, then warp 0
+    // over the 4 warp sums): reference warp w = lane / 8 and lane bits 2..0,
+    // then the float4 components (offsets 2, 1), hold its lane offsets
+    // 16, 8, 4 and 2, 1; the warp sums combine as (w0 + w2) + (w1 + w3).
+    float s0 = x.x * x.x, s1 = x.y * x.y, s2 = x.z * x.z, s3 = x.w * x.w;
+#pragma unroll
+    for (int o = 4; o > 0; o >>= 1) {
+      s0 += __shfl_xor_sync(0xffffffffu, s0, o);
+      s1 += __shfl_xor_sync(0xffffffffu, s1, o);
+      s2 += __shfl_xor_sync(0xffffffffu, s2, o);
+      s3 += __shfl_xor_sync(0xffffffffu, s3, o);
+    }
+    float ss = (s0 + s2) + (s1 + s3);
+    ss += __shfl_xor_sync(0xffffffffu, ss, 16);
+    ss += __shfl_xor_sync(0xffffffffu, ss, 8);
+    const float rms = rsqrtf(ss / a.norm_dim + a.eps);
     const __nv_bfloat162* w2 = reinterpret_cast<const __nv_bfloat162*>(w + d0);
     const float2 w01 = __bfloat1622float2(w2[0]);
     const float2 w23 = __bfloat1622float2(w2[1]);
@@ -392,7 +406,10 @@ int qkv_post_launch(const QkvPostArgs& a, cudaStream_t stream) {
   if (items == 0) return QI_OK;
   const int threads = 256;
   const long long blocks = (items + 7) / 8;
-  qkv_post_kernel<<<static_cast<unsigned>(blocks), threads, 0, stream>>>(a);
+  QkvPostArgs b = a;
+  b.norm_dim = kHeadDim;  // run-time operands, as in rms_norm_fp32 (same division and add)
+  b.eps = 1e-6f;
+  qkv_post_kernel<<<static_cast<unsigned>(blocks), threads, 0, stream>>>(b);
   return ok_or_err();
 }
 

@@ -23,8 +23,10 @@ constexpr size_t kCodesOff = kScalesOff + 4 * static_cast<size_t>(QI_NOALLOC_MAX
 constexpr size_t kScratchBytes = kCodesOff + static_cast<size_t>(QI_NOALLOC_MAX_CODES);
 static_assert(kCodesOff % 256 == 0, "codes must stay 256-byte aligned");
 
-// Zero at module load; only the error word has to be zero when a launch
-// starts, and the entry clears it itself before every call.
+// Zero at module load.  The error word is sticky: a GEMM wait that gives up
+// records its code there (only if the word is still zero; the kernels never
+// read it back) and it stays until qi_linear_i8_f32in_noalloc_check reads and
+// clears it.  Codes and scales are fully overwritten by every call.
 __device__ __align__(256) unsigned char g_noalloc_scratch[kScratchBytes];
 
 constexpr int kMaxDevices = 64;
@@ -50,12 +52,51 @@ int setup(int dev, unsigned char** scratch, int* num_sms) {
   return QI_OK;
 }
 
+// The scratch address on the current device if a call has set it up there,
+// else null.
+unsigned char* scratch_if_set_up(int* dev_out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
+  *dev_out = dev;
+  std::lock_guard<std::mutex> lock(g_setup_mu);
+  return g_scratch_addr[dev];
+}
+
+inline bool misaligned(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) != 0; }
+
 }  // namespace
+
+extern "C" int qi_linear_i8_f32in_noalloc_check(void) {
+  int dev = 0;
+  unsigned char* scratch = scratch_if_set_up(&dev);
+  if (!scratch) return QI_OK;  // no call has run on this device
+  if (cudaDeviceSynchronize() != cudaSuccess) return QI_ERR_CUDA;
+  int h = 0;
+  if (cudaMemcpy(&h, scratch, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return QI_ERR_CUDA;
+  if (h && cudaMemset(scratch, 0, sizeof(int)) != cudaSuccess) return QI_ERR_CUDA;
+  return h ? QI_ERR_DEVICE : QI_OK;
+}
+
+extern "C" int qi_linear_i8_f32in_noalloc_selftest(int limit_us, void* stream) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return QI_ERR_CUDA;
+  unsigned char* scratch = nullptr;
+  int num_sms = 0;
+  const int st = setup(dev, &scratch, &num_sms);
+  if (st != QI_OK) return st;
+  return qi::selftest_wait_timeout(reinterpret_cast<int*>(scratch), limit_us, reinterpret_cast<cudaStream_t>(stream));
+}
 
 extern "C" int qi_linear_i8_f32in_noalloc(const float* x, int M, int K, const int8_t* w, const float* w_scales, int N,
                                           const void* bias_bf16, int apply_gelu, float* out, void* stream) {
   if (!x || !w || !w_scales || !out || M < 0 || K <= 0 || N <= 0) return QI_ERR_ARG;
-  if (M > QI_NOALLOC_MAX_ROWS || static_cast<long long>(M) * K > QI_NOALLOC_MAX_CODES) return QI_ERR_UNSUPPORTED;
+  if (M > QI_NOALLOC_MAX_ROWS || static_cast<long long>(M) * K > QI_NOALLOC_MAX_CODES || K > 12288)
+    return QI_ERR_UNSUPPORTED;
+  // everything the quantizer and the GEMM / GEMV launchers would reject, before
+  // anything is enqueued or the shared scratch is touched
+  const bool gemv = M == 1 && !apply_gelu;
+  if (K % 16 != 0 || (!gemv && N % 32 != 0)) return QI_ERR_ARG;
+  if (misaligned(w) || misaligned(w_scales) || (!gemv && misaligned(out))) return QI_ERR_ALIGN;
   if (M == 0) return QI_OK;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return QI_ERR_CUDA;
@@ -67,10 +108,9 @@ extern "C" int qi_linear_i8_f32in_noalloc(const float* x, int M, int K, const in
   int* err = reinterpret_cast<int*>(scratch);
   float* act_scales = reinterpret_cast<float*>(scratch + kScalesOff);
   int8_t* act = reinterpret_cast<int8_t*>(scratch + kCodesOff);
-  if (cudaMemsetAsync(err, 0, sizeof(int), s) != cudaSuccess) return QI_ERR_CUDA;
   const int qst = qi_fwht_quantize(x, M, K, K & (-K), act, act_scales, stream);
   if (qst != QI_OK) return qst;
-  if (M == 1 && !apply_gelu) {
+  if (gemv) {
     qi::GemvJob j{w, w_scales, bias_bf16, out, N};
     return qi::gemv_i8_launch(act, act_scales, K, &j, 1, s);
   }

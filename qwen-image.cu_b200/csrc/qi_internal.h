@@ -166,10 +166,15 @@ struct QkvPostArgs {
   // memory over NVLink), final layout [3][nb*Hl][S][128] in joint order
   int direct;
   void* peer_qkvh[kMaxRanks];
+  int norm_dim;  // set by qkv_post_launch
+  float eps;
 };
 int qkv_post_launch(const QkvPostArgs& a, cudaStream_t stream);
 
 // ---------------------------------------------------------------- attention
+// Longest joint sequence the attention kernel takes (its K scales of up to
+// 8192 64-key blocks fit in shared memory).
+constexpr int kAttnMaxS = 131072;
 int sage_quantize_launch(const void* q, const void* k, int BH, int S, float* kmean, int8_t* qc, float* qs,
                          int8_t* kc, float* ks, cudaStream_t stream);
 // out_mode 0: FP32 [BH, S, 128] head-major.
@@ -202,6 +207,11 @@ int cfg_euler_launch(float* x, const void* cond, const void* uncond, float cfg, 
                      int W, void* x_bf16, cudaStream_t stream);
 
 int selftest_wait_timeout(int* err, int limit_us, cudaStream_t stream);
+
+// Every CUDA allocation the library makes goes through these two, which count
+// it (qi_alloc_count).
+cudaError_t dev_malloc(void** p, size_t bytes);
+cudaError_t host_malloc_pinned(void** p, size_t bytes);
 
 int device_num_sms();
 

@@ -36,15 +36,48 @@ struct RowSegs {
   int nseg;
 };
 
-__device__ __forceinline__ float warp_sum(float v) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-  return v;
-}
 __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
   return v;
+}
+
+// Sum over the 1024 threads of a reference reduction block in the order of
+// its two-level shfl_down tree.  The lane stands for reference warp `lane`
+// (threads 32 * lane + L, L = 0..31); part(q, p) gives the partials of threads
+// L = 4q .. 4q + 3.  The warp's own tree (offsets 16, 8, 4 pair L with L + 16,
+// L + 8, L + 4, i.e. q with q + 4, q + 2, q + 1 at the same L % 4; then
+// offsets 2, 1 pair the components) runs in registers as
+//   c[e] = ((p0 + p4) + (p2 + p6)) + ((p1 + p5) + (p3 + p7)),
+//   warp sum = (c[0] + c[2]) + (c[1] + c[3]);
+// the 32 warp sums then go through offsets 16 .. 1 across lanes.  The xor
+// butterfly gives every lane the value the reference's lane 0 gets (each add
+// is commutative).  The __syncwarp between the halves keeps the compiler from
+// holding all eight float4 partials' operands in registers at once.
+template <typename Part>
+__device__ __forceinline__ float ref_block_tree(Part part) {
+  auto quad = [&](int q0, float (&c)[4]) {  // (p[q0] + p[q0 + 4]) + (p[q0 + 2] + p[q0 + 6])
+    float a[4], b[4];
+    part(q0, a);
+    part(q0 + 4, b);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) a[e] = a[e] + b[e];
+    float d[4];
+    part(q0 + 2, d);
+    part(q0 + 6, b);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) c[e] = a[e] + (d[e] + b[e]);
+  };
+  float c0[4], c1[4];
+  quad(0, c0);
+  __syncwarp();
+  quad(1, c1);
+#pragma unroll
+  for (int e = 0; e < 4; ++e) c0[e] = c0[e] + c1[e];
+  float w = (c0[0] + c0[2]) + (c0[1] + c0[3]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) w += __shfl_xor_sync(0xffffffffu, w, o);
+  return w;
 }
 
 // One row per CTA, NW warps per row; warp w owns the contiguous chunk
@@ -58,7 +91,7 @@ __device__ __forceinline__ float warp_max(float v) {
 // in the reference's stage order.  Only the row statistics cross warps.
 template <int K, int NW, int SRC>
 __global__ void __launch_bounds__(NW * 32) rowquant_warp_kernel(RowSegs segs, int had_block, int8_t* __restrict__ codes,
-                                                                float* __restrict__ scales, float eps) {
+                                                                float* __restrict__ scales, float eps, int dim) {
   constexpr int CH = K / NW;
   constexpr int J = CH / 128;
   static_assert(CH % 128 == 0, "chunk must be a multiple of 128");
@@ -99,36 +132,78 @@ __global__ void __launch_bounds__(NW * 32) rowquant_warp_kernel(RowSegs segs, in
     }
   }
 
-  if (SRC == kSrcLnMod) {
-    float s = 0.0f;
-#pragma unroll
-    for (int j = 0; j < J; ++j) s += (v[j][0] + v[j][1]) + (v[j][2] + v[j][3]);
-    s = warp_sum(s);
-    if (lane == 0) red[0][warp] = s;
-    __syncthreads();
-    float tot = 0.0f;
-#pragma unroll
-    for (int w = 0; w < NW; ++w) tot += red[0][w];
-    const float mean = tot / K;
-    float q = 0.0f;
-#pragma unroll
-    for (int j = 0; j < J; ++j)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float d = v[j][e] - mean;
-        q += d * d;
-      }
-    q = warp_sum(q);
-    if (lane == 0) red[1][warp] = q;
-    __syncthreads();
-    float var = 0.0f;
-#pragma unroll
-    for (int w = 0; w < NW; ++w) var += red[1][w];
-    const float inv_std = rsqrtf(var / K + eps);
+  if constexpr (SRC == kSrcLnMod) {
+    // Row statistics in the reference's own summation order, so that mean and
+    // inv_std carry the same bits (layer_norm_modulate_fp32_kernel,
+    // cuda_kernels.cu:1799-1853, launched with 1024 threads for dim 3072):
+    // thread t sums x[t], x[t + 1024], x[t + 2048] in that order; each warp of
+    // 32 threads reduces with shfl_down offsets 16, 8, 4, 2, 1; warp 0 reduces
+    // the 32 warp sums the same way; mean = sum / dim.  The variance repeats
+    // it on (x - mean)^2.  Here warp k holds chunk k (t = 128j + 4 lane + e),
+    // so the three chunks go through shared memory and lane W of warp 0
+    // replays reference warp W (threads 32W .. 32W + 31) in registers.
+    static_assert(K == 3072 && NW == 3, "the reference-order statistics assume 3 chunks of 1024");
+    __shared__ __align__(16) float xs[3][1152];  // t at t + 4 * (t / 32): conflict-free both ways
 #pragma unroll
     for (int j = 0; j < J; ++j) {
+      const int t = 128 * j + 4 * lane;
+      *reinterpret_cast<float4*>(&xs[warp][t + 4 * (t >> 5)]) = make_float4(v[j][0], v[j][1], v[j][2], v[j][3]);
+    }
+    __syncthreads();
+    if (warp == 0) {
+      const int a0 = 36 * lane;  // padded offset of thread 32 * lane
+      // thread partials of threads 32 * lane + 4q .. + 3, in the reference's
+      // per-thread order: sum += x[t]; sum += x[t + 1024]; sum += x[t + 2048]
+      auto sum_part = [&](int q, float (&o)[4]) {
+        const float4 f0 = *reinterpret_cast<const float4*>(&xs[0][a0 + 4 * q]);
+        const float4 f1 = *reinterpret_cast<const float4*>(&xs[1][a0 + 4 * q]);
+        const float4 f2 = *reinterpret_cast<const float4*>(&xs[2][a0 + 4 * q]);
+        o[0] = (f0.x + f1.x) + f2.x;
+        o[1] = (f0.y + f1.y) + f2.y;
+        o[2] = (f0.z + f1.z) + f2.z;
+        o[3] = (f0.w + f1.w) + f2.w;
+      };
+      const float mean = ref_block_tree(sum_part) / dim;
+      // var_sum += v * v over the same elements, v = x - mean
+      auto var_part = [&](int q, float (&o)[4]) {
+        const float4 f0 = *reinterpret_cast<const float4*>(&xs[0][a0 + 4 * q]);
+        const float4 f1 = *reinterpret_cast<const float4*>(&xs[1][a0 + 4 * q]);
+        const float4 f2 = *reinterpret_cast<const float4*>(&xs[2][a0 + 4 * q]);
+        const float x0[4] = {f0.x, f0.y, f0.z, f0.w}, x1[4] = {f1.x, f1.y, f1.z, f1.w},
+                    x2[4] = {f2.x, f2.y, f2.z, f2.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          float var_sum = 0.0f;
+          float d = x0[e] - mean;
+          var_sum += d * d;
+          d = x1[e] - mean;
+          var_sum += d * d;
+          d = x2[e] - mean;
+          var_sum += d * d;
+          o[e] = var_sum;
+        }
+      };
+      const float inv_std = rsqrtf(ref_block_tree(var_part) / dim + eps);
+      if (lane == 0) {
+        red[0][0] = mean;
+        red[1][0] = inv_std;
+      }
+    }
+    __syncthreads();
+    const float mean = red[0][0];
+    const float inv_std = red[1][0];
+    // this warp's chunk back from shared memory (not held in registers
+    // across the statistics)
+#pragma unroll
+    for (int j = 0; j < J; ++j) {
+      const int t = 128 * j + 4 * lane;
+      const float4 f = *reinterpret_cast<const float4*>(&xs[warp][t + 4 * (t >> 5)]);
       const float4 sc = __ldg(reinterpret_cast<const float4*>(scale + base + 128 * j));
       const float4 sh = __ldg(reinterpret_cast<const float4*>(shift + base + 128 * j));
+      v[j][0] = f.x;
+      v[j][1] = f.y;
+      v[j][2] = f.z;
+      v[j][3] = f.w;
       v[j][0] = (v[j][0] - mean) * inv_std * (1.0f + sc.x) + sh.x;
       v[j][1] = (v[j][1] - mean) * inv_std * (1.0f + sc.y) + sh.y;
       v[j][2] = (v[j][2] - mean) * inv_std * (1.0f + sc.z) + sh.z;
@@ -436,7 +511,7 @@ template <int K, int NW, int SRC>
 int launch_warp(const RowSegs& segs, int rows, int had_block, int8_t* codes, float* scales, float eps,
                 cudaStream_t stream) {
   if (had_block > K / NW) return QI_ERR_UNSUPPORTED;
-  rowquant_warp_kernel<K, NW, SRC><<<rows, NW * 32, 0, stream>>>(segs, had_block, codes, scales, eps);
+  rowquant_warp_kernel<K, NW, SRC><<<rows, NW * 32, 0, stream>>>(segs, had_block, codes, scales, eps, K);
   return cudaGetLastError() == cudaSuccess ? QI_OK : QI_ERR_CUDA;
 }
 

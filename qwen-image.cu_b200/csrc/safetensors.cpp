@@ -23,6 +23,7 @@
 #include <vector>
 
 #include "../../include/qwen_image_b200.h"
+#include "qi_internal.h"
 
 namespace {
 
@@ -245,14 +246,14 @@ struct Loader {
       return nullptr;
     }
     void* d = nullptr;
-    if (cudaMalloc(&d, bytes < 16 ? 16 : bytes) != cudaSuccess) {
+    if (qi::dev_malloc(&d, bytes < 16 ? 16 : bytes) != cudaSuccess) {
       *st = QI_ERR_OOM;
       return nullptr;
     }
     dev.push_back(d);
     const size_t chunk = 64ull << 20;
     if (!pinned) {
-      if (cudaMallocHost(&pinned, chunk) != cudaSuccess) {
+      if (qi::host_malloc_pinned(&pinned, chunk) != cudaSuccess) {
         *st = QI_ERR_OOM;
         return nullptr;
       }
@@ -295,9 +296,9 @@ struct Loader {
     void* wb = load(w, "BF16", static_cast<long long>(N) * K, &st);
     if (st) return st;
     void *c = nullptr, *s = nullptr;
-    if (cudaMalloc(&c, static_cast<size_t>(N) * K) != cudaSuccess) return QI_ERR_OOM;
+    if (qi::dev_malloc(reinterpret_cast<void**>(&c), static_cast<size_t>(N) * K) != cudaSuccess) return QI_ERR_OOM;
     dev.push_back(c);
-    if (cudaMalloc(&s, static_cast<size_t>(N) * 4) != cudaSuccess) return QI_ERR_OOM;
+    if (qi::dev_malloc(reinterpret_cast<void**>(&s), static_cast<size_t>(N) * 4) != cudaSuccess) return QI_ERR_OOM;
     dev.push_back(s);
     st = qi_quantize_weight(wb, N, K, static_cast<int8_t*>(c), static_cast<float*>(s), nullptr);
     if (st) return st;

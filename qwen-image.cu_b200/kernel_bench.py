@@ -2,13 +2,20 @@
 CUDA events on the launching stream).  Also the target of the ncu captures
 summarised in profiles/.
 
-    python qwen-image.cu_b200/kernel_bench.py [--which gemm,attn,quant] [--iters N] [--config c4|c2]
+    python qwen-image.cu_b200/kernel_bench.py [--which gemm,attn,quant,peaks] [--iters N] [--config c4|c2]
 
 GEMM shapes are those of one CFG-batched C4 forward (M = 2 x 6889 image +
 2 x 256 text tokens): fused QKV (N 9216), out-projection (N 3072), fc1
-(N 12288), fc2 (K 12288).  Attention: BASELINE config 2 (B 2, 24 heads,
-4352 tokens) or the C4 joint sequence (7145 tokens).
+(N 12288), fc2 (K 12288).  Attention: the Sage microbenchmark configuration
+(B 2, 24 heads, 4352 tokens) or the C4 joint sequence (7145 tokens).
+Quantizers: LayerNorm-modulate + FWHT-1024 (K 3072), the attention output
+(FP16, K 3072) and the MLP hidden (FWHT-4096, K 12288) at the C4 rows.
+`peaks`: the dense tensor-core rates of this GPU through the libraries
+(torch._int_mm INT8 -> INT32, torch.matmul FP16 and BF16 at 8192^3), as a
+burst (best of 10) and sustained (back to back for 4 s); the roofline
+denominators for the INT8 and FP16 kernels.
 """
+import time
 import argparse
 import json
 import os
@@ -79,6 +86,41 @@ def bench_quant(iters, res):
         ms = time_it(lambda: Q.fwht_quantize(x, B), iters)
         gbs = (M * K * 4 + M * K + M * 4) / (ms * 1e-3) / 1e9
         res[f"fwht_quant_{K}"] = {"M": M, "K": K, "ms": round(ms, 4), "gbs": round(gbs, 1)}
+    x = Q.synth((M, 3072), 8, 1.0)
+    shift = Q.synth((3072,), 9, 0.1)
+    scale = Q.synth((3072,), 10, 0.1)
+    ms = time_it(lambda: Q.layer_norm_modulate_quantize(x, shift, scale), iters)
+    gbs = (M * 3072 * 4 + M * 3072 + M * 4) / (ms * 1e-3) / 1e9
+    res["ln_mod_quant_3072"] = {"M": M, "K": 3072, "ms": round(ms, 4), "gbs": round(gbs, 1)}
+
+
+def bench_peaks(res, seconds=4.0):
+    n = 8192
+    flops = 2.0 * n ** 3
+    a8 = torch.randint(-127, 128, (n, n), dtype=torch.int8, device="cuda")
+    b8 = torch.randint(-127, 128, (n, n), dtype=torch.int8, device="cuda").t()
+    ah = torch.randn(n, n, device="cuda").half()
+    bh = torch.randn(n, n, device="cuda").half()
+    ab, bb = ah.bfloat16(), bh.bfloat16()
+    for name, fn in (("int8", lambda: torch._int_mm(a8, b8)), ("fp16", lambda: torch.matmul(ah, bh)),
+                     ("bf16", lambda: torch.matmul(ab, bb))):
+        best = min(time_it(fn, 1, warmup=3 if k == 0 else 0) for k in range(10))
+        fn()
+        torch.cuda.synchronize()
+        count, t0 = 0, time.time()
+        s = torch.cuda.current_stream()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        while time.time() - t0 < seconds:
+            for _ in range(20):
+                fn()
+            count += 20
+            torch.cuda.synchronize()
+        e1.record(s)
+        torch.cuda.synchronize()
+        sus = e0.elapsed_time(e1) / count
+        res[f"peak_{name}"] = {"n": n, "burst_tflops": round(flops / (best * 1e-3) / 1e12, 1),
+                               "sustained_tflops": round(flops / (sus * 1e-3) / 1e12, 1), "iters_sustained": count}
 
 
 def main():
@@ -96,6 +138,8 @@ def main():
         bench_attn(a.iters, res, a.config)
     if "quant" in w:
         bench_quant(a.iters, res)
+    if "peaks" in w:
+        bench_peaks(res)
     print(json.dumps(res))
 
 

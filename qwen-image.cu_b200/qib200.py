@@ -77,10 +77,15 @@ def lib():
             "qi_linear_i8": ([vp, vp, i, i, vp, vp, i, vp, i, vp, vp, i, vp], i),
             "qi_linear_i8_f32in": ([vp, i, i, vp, vp, i, vp, i, vp, vp], i),
             "qi_linear_i8_f32in_noalloc": ([vp, i, i, vp, vp, i, vp, i, vp, vp], i),
+            "qi_linear_i8_f32in_noalloc_check": ([], i),
+            "qi_linear_i8_f32in_noalloc_selftest": ([i, vp], i),
+            "qi_alloc_count": ([], ll),
             "qi_sage_attention": ([vp, vp, vp, vp, f, i, i, i, vp], i),
             "qi_sage_quantize": ([vp, vp, i, i, vp, vp, vp, vp, vp, vp], i),
             "qi_layer_norm_modulate": ([vp, vp, vp, vp, i, i, f, vp], i),
             "qi_rms_norm": ([vp, vp, vp, i, i, f, vp], i),
+            "qi_layer_norm_modulate_quantize": ([vp, vp, vp, i, i, f, vp, vp, vp], i),
+            "qi_qk_norm_rope": ([vp, vp, vp, vp, i, i, i, vp, vp], i),
             "qi_ctx_create": ([i, ctypes.POINTER(vp)], i),
             "qi_ctx_destroy": ([vp], i),
             "qi_ctx_check": ([vp], i),
@@ -192,6 +197,25 @@ def rms_norm(x, w, eps=1e-6):
     rows, dim = x.shape
     out = torch.empty_like(x)
     check(lib().qi_rms_norm(_p(x), _p(w), _p(out), rows, dim, eps, _stream()))
+    return out
+
+
+def layer_norm_modulate_quantize(x, shift, scale, eps=1e-6):
+    rows, dim = x.shape
+    codes = torch.empty(rows, dim, dtype=torch.int8, device=x.device)
+    scales = torch.empty(rows, dtype=torch.float32, device=x.device)
+    check(lib().qi_layer_norm_modulate_quantize(_p(x), _p(shift), _p(scale), rows, dim, eps, _p(codes), _p(scales),
+                                                _stream()))
+    return codes, scales
+
+
+def qk_norm_rope(qkv_img, qkv_txt, norms, pe, nb=1):
+    """qkv_img [nb*n_img, 9216], qkv_txt [nb*n_txt, 9216] FP32; norms [4,128]
+    BF16; pe nb x [S,64,2,2].  Returns FP16 [3, nb*24, S, 128] (q, k, v)."""
+    n_img = qkv_img.shape[0] // nb
+    n_txt = qkv_txt.shape[0] // nb
+    out = torch.empty(3, nb * HEADS, n_img + n_txt, HEAD_DIM, dtype=torch.float16, device=qkv_img.device)
+    check(lib().qi_qk_norm_rope(_p(qkv_img), _p(qkv_txt), _p(norms), _p(pe), nb, n_img, n_txt, _p(out), _stream()))
     return out
 
 

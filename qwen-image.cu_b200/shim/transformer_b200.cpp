@@ -13,7 +13,8 @@
 // TransformerWeights::load (transformer.h:144) keeps loading the INT8
 // checkpoint into the caller's QuantizedWeight tensors; the first forward on a
 // weights object copies them once into the kernels' layout (fused QKV,
-// stacked modulation) and caches the model for that object.
+// stacked modulation) and caches the model, keyed by the weight tensors'
+// device pointers.
 //
 // Behaviour kept from the reference: the returned Tensor is a new owning BF16
 // [1,16,H,W] allocation; odd H or W are zero-padded to the patch size and the
@@ -36,7 +37,11 @@ namespace {
 
 qi_ctx* g_ctx = nullptr;
 qi_model* g_model = nullptr;
-const TransformerWeights* g_key = nullptr;
+// The device tensors the cached model was built from (every pointer of the
+// weight table, in table order).  A forward on weights whose tensors differ
+// rebuilds the model; the address of the TransformerWeights object alone is
+// not a key (a caller may build a new object at the same address).
+std::vector<const void*> g_key;
 
 void die(const char* what, int st) {
   fprintf(stderr, "qwen-image-b200: %s failed: %s\n", what, qi_status_string(st));
@@ -61,7 +66,8 @@ const void* bf16_of(const QuantizedWeight& q) {
   return q.data.data;
 }
 
-void build_model(const TransformerWeights& w) {
+// Builds (or keeps) the kernel-layout model for `w`.
+void ensure_model(const TransformerWeights& w) {
   std::vector<const void*> g(QI_G_COUNT, nullptr);
   auto put_g = [&](int base, const QuantizedWeight& q, const Tensor& b) {
     if (q.mode != QuantMode::INT8_HADAMARD) {
@@ -109,11 +115,15 @@ void build_model(const TransformerWeights& w) {
     t[QI_B_NORM_ADDED_K] = B.norm_added_k_weight.data;
     bt[i] = t.data();
   }
+  std::vector<const void*> key(g);
+  for (const auto& t : bl) key.insert(key.end(), t.begin(), t.end());
+  if (g_model && key == g_key) return;
   if (g_model) qi_model_destroy(g_model);
   g_model = nullptr;
+  g_key.clear();
   int st = qi_model_create(g_ctx, nb, g.data(), bt.data(), &g_model);
   if (st != QI_OK) die("qi_model_create", st);
-  g_key = &w;
+  g_key.swap(key);
 }
 
 }  // namespace
@@ -121,7 +131,18 @@ void build_model(const TransformerWeights& w) {
 Tensor transformer_forward(const TransformerWeights& w, const Tensor& x_in, float timestep, const Tensor& context,
                            const Tensor& pe, int H, int W, CalibrationWriter* cal, bool use_sage_attention,
                            float* spectrum_hidden_out) {
-  (void)use_sage_attention;
+  if (!use_sage_attention) {
+    // the caller asked for the reference's materialised-softmax attention
+    // (transformer.cu:679, cuda_kernels.cu:2019-2112); this library has only
+    // the SageAttention kernels, so say once that those run instead
+    static bool told = false;
+    if (!told) {
+      fprintf(stderr,
+              "qwen-image-b200: use_sage_attention = false requested; running SageAttention (INT8 QK^T, "
+              "FP16 P.V) instead of the materialised-softmax path\n");
+      told = true;
+    }
+  }
   if (cal || spectrum_hidden_out) {
     fprintf(stderr, "qwen-image-b200: calibration / Spectrum capture is not supported\n");
     exit(1);
@@ -132,7 +153,7 @@ Tensor transformer_forward(const TransformerWeights& w, const Tensor& x_in, floa
     int st = qi_ctx_create(dev, &g_ctx);
     if (st != QI_OK) die("qi_ctx_create", st);
   }
-  if (g_key != &w || !g_model) build_model(w);
+  ensure_model(w);
   const int H_pad = H + (H & 1), W_pad = W + (W & 1);
   const int C = static_cast<int>(x_in.shape[1]);
   const void* x = x_in.data;

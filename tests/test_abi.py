@@ -42,6 +42,8 @@ def test_argument_validation_without_device():
     assert L.qi_linear_i8(null, null, 4, 64, null, null, 32, null, 0, null, null, 32, null) == 1
     assert L.qi_linear_i8(null, null, 4, 64, null, null, 32, null, 7, null, null, 32, null) == 1
     assert L.qi_sage_attention(null, null, null, null, 0.1, 1, 8, 64, null) == 5  # head_dim 64 unsupported
+    p16 = ctypes.c_void_p(256)
+    assert L.qi_sage_attention(p16, p16, p16, p16, 0.1, 1, 131073, 128, null) == 5  # longer than the kernel takes
     assert L.qi_forward(null, null, 1, null, 0.0, null, 8, null, 8, 8, null, null) == 1
     assert L.qi_model_create(null, 1, null, null, None) == 1
     assert L.qi_rope_table(8, 8, 8, null) == 1
@@ -53,6 +55,15 @@ def test_argument_validation_without_device():
     assert L.qi_linear_i8_f32in_noalloc(p, 4097, 256, p, p, 64, null, 0, p, null) == 5
     assert L.qi_linear_i8_f32in_noalloc(p, 4096, 2048, p, p, 64, null, 0, p, null) == 5
     assert L.qi_linear_i8_f32in_noalloc(p, 0, 256, p, p, 64, null, 0, p, null) == 0
+    # shapes and alignments the quantizer or GEMM would reject are refused
+    # before anything is launched or the shared scratch is touched
+    odd = ctypes.c_void_p(264)  # 8-byte aligned only
+    assert L.qi_linear_i8_f32in_noalloc(p, 4, 100, p, p, 64, null, 0, p, null) == 1  # K % 16
+    assert L.qi_linear_i8_f32in_noalloc(p, 4, 256, p, p, 48, null, 0, p, null) == 1  # N % 32 (GEMM path)
+    assert L.qi_linear_i8_f32in_noalloc(p, 4, 256, odd, p, 64, null, 0, p, null) == 2  # w alignment
+    assert L.qi_linear_i8_f32in_noalloc(p, 4, 256, p, odd, 64, null, 0, p, null) == 2  # w_scales alignment
+    assert L.qi_linear_i8_f32in_noalloc(p, 4, 256, p, p, 64, null, 0, odd, null) == 2  # out alignment
+    assert L.qi_linear_i8_f32in_noalloc(p, 1, 16384, p, p, 64, null, 0, p, null) == 5  # K beyond the quantizer
 
 
 def test_null_handles_and_buffers_are_rejected_without_device():
@@ -79,6 +90,9 @@ def test_null_handles_and_buffers_are_rejected_without_device():
     assert L.qi_rms_norm(null, null, null, 4, 64, 1e-6, null) == 1
     assert L.qi_sage_quantize(null, null, 1, 64, null, null, null, null, null, null) == 1
     assert L.qi_cfg_euler_step(null, null, null, 4.0, 0.5, 0.4, 8, 8, null, null) == 1
+    assert L.qi_layer_norm_modulate_quantize(null, null, null, 4, 3072, 1e-6, null, null, null) == 1
+    assert L.qi_qk_norm_rope(null, null, null, null, 1, 16, 8, null, null) == 1
+    assert L.qi_alloc_count() >= 0
 
 
 @pytest.mark.parametrize("h,w,n_txt", [(8, 8, 8), (128, 128, 256), (166, 166, 256), (7, 9, 5)])

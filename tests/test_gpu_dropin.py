@@ -54,3 +54,38 @@ def test_shim_forward_through_reference_types():
     assert float(a @ b / (a.norm() * b.norm())) >= 0.999
     model.close()
     ctx.close()
+
+
+def test_shim_reports_sage_substitution(capfd):
+    """use_sage_attention = false asks for the reference's materialised-softmax
+    attention; the shim runs its SageAttention kernels instead and says so on
+    stderr (once per process)."""
+    if not (R.available() and os.path.exists(SHIM)):
+        pytest.skip("reference / shim test build missing")
+    torch.cuda.set_device(0)
+    shim = ctypes.CDLL(SHIM)
+    vp, i, f = ctypes.c_void_p, ctypes.c_int, ctypes.c_float
+    shim.ref_transformer_forward.argtypes = [vp, vp, vp, f, vp, i, vp, i, i, i, vp]
+    shim.ref_transformer_forward.restype = i
+    g, blocks = R.make_table(60, distinct=1)
+    garr, _, bt = R.table_pointers(g, blocks)
+    H, W, n_txt, t = 16, 16, 12, 650.0
+    x = R.synth((1, 16, H, W), R.seed_for(6, "latent"), 1.0, dtype=torch.bfloat16)
+    txt = R.synth((1, n_txt, 3584), R.seed_for(6, "context"), 1.0, dtype=torch.bfloat16)
+    pe = torch.from_numpy(R.rope_table(H, W, n_txt)).cuda()
+    p = lambda t_: ctypes.c_void_p(t_.data_ptr())
+    a, b = torch.empty_like(x), torch.empty_like(x)
+    assert shim.ref_transformer_forward(garr, bt, p(x), t, p(txt), n_txt, p(pe), H, W, 1, p(a)) == 0
+    capfd.readouterr()
+    assert shim.ref_transformer_forward(garr, bt, p(x), t, p(txt), n_txt, p(pe), H, W, 0, p(b)) == 0
+    assert shim.ref_transformer_forward(garr, bt, p(x), t, p(txt), n_txt, p(pe), H, W, 0, p(b)) == 0
+    err = capfd.readouterr().err
+    assert err.count("use_sage_attention = false requested") == 1, err
+    assert torch.equal(a, b)
+    # a new weights object (other tensors) in the same process: the shim
+    # rebuilds its model instead of reusing the one of the test above
+    ctx = Q.Context(0)
+    model = Q.Model(ctx, g, blocks)
+    assert torch.equal(a, Q.forward(ctx, model, x, t, txt, pe[None]))
+    model.close()
+    ctx.close()

@@ -75,15 +75,18 @@ def ref_dumps(env, x, t, txt, pe, H, W, block):
     return out
 
 
-# Per-block bar.  Cosine >= 0.999 is the north-star bar.  Element-wise, two
-# W8A8 implementations of one block cannot agree to 2e-2 everywhere: the
-# reference's own block 0 deviates 3.5e-2 from an exact evaluation of its own
-# arithmetic (the CPU oracle), because rounding differences in the INT8
-# quantizer inputs move codes across rounding boundaries.  The element-wise
-# bound here is 3e-2 (2e-2 holds on the text stream and on all blocks but
-# block 0's image stream), and test_block0_no_less_accurate_than_reference
-# checks that the product's error against exact arithmetic is the reference's.
-PER_BLOCK_MAXREL = 3e-2
+# Per-block bar.  Cosine >= 0.999 is the north-star bar; element-wise, the
+# text stream meets 2e-2.  The image stream's element-wise deviation is what
+# the reference's own arithmetic makes of the attention output, the one stage
+# that cannot be bit-exact (tensor-core accumulation order; the product's
+# attention differs from the reference's by at most one FP16 ulp):
+# test_gpu_attribution.py shows every other stage bit-exact with the
+# reference and the product's block equal, bit for bit, to the reference's
+# own block fed the product's attention output (measured 1.6e-2 .. 2.3e-2 on
+# blocks 0, 1, 30, 59).  test_block0_no_less_accurate_than_reference checks
+# that the product's error against exact arithmetic is the reference's.
+PER_BLOCK_MAXREL = 2.5e-2
+FORWARD_MAXREL = 6e-2
 
 
 @pytest.mark.parametrize("H,W,n_txt,t,check_blocks", [(64, 64, 64, 500.0, (0, 1, 30, 59)),
@@ -153,10 +156,11 @@ def test_block0_no_less_accurate_than_reference(env):
 @pytest.mark.parametrize("H,W,n_txt,t", [(64, 64, 64, 500.0), (32, 48, 30, 871.3), (128, 128, 256, 250.0),
                                          (166, 166, 256, 980.0)])
 def test_forward_matches_reference(env, H, W, n_txt, t):
-    """The whole 60-block forward (velocity output).  Rounding differences of
-    each block (accumulation order, FMA contraction) compound over 60 blocks,
-    so the per-element bound here is looser than the per-block bar above;
-    the cosine bar is the north-star one."""
+    """The whole 60-block forward (velocity output).  Each block's attention
+    difference (the only stage that is not bit-exact) propagates through the
+    later blocks, so the per-element bound is looser than the per-block bar
+    above: measured 4.2e-2 .. 4.9e-2 on these four shapes, bound 6e-2.  The
+    cosine bar is the north-star one."""
     x, (txt,), pe = inputs(H, W, n_txt)
     garr, _, bt = env["ptrs"]
     ref = R.transformer_forward(garr, bt, x, t, txt, pe, H, W, sage=True)
@@ -164,7 +168,7 @@ def test_forward_matches_reference(env, H, W, n_txt, t):
     env["ctx"].check()
     cos, maxrel = metrics(ours.float(), ref.float())
     print(f"forward {H}x{W} n_txt={n_txt}: cos={cos:.6f} maxrel={maxrel:.4g}")
-    assert cos >= COS_MIN and maxrel <= 0.1, (cos, maxrel)
+    assert cos >= COS_MIN and maxrel <= FORWARD_MAXREL, (cos, maxrel)
 
 
 def test_cfg_batch_equals_two_single_forwards(env):

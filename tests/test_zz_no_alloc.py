@@ -13,6 +13,7 @@ pytestmark = pytest.mark.gpu
 
 QI_ERR_ARG = 1
 QI_ERR_UNSUPPORTED = 5
+QI_ERR_DEVICE = 7
 MAX_ROWS = 4096
 MAX_CODES = 4 * 1024 * 1024
 
@@ -46,26 +47,33 @@ def test_noalloc_matches_existing_entry_two_calls_in_a_row():
     cases = [case(M, K, N, f"{M}_{K}_{N}") for M, K, N, _ in shapes]
     expected = [Q.linear_i8_f32in(x, wc, ws, b, g) for (x, wc, ws, b), (_, _, _, g) in zip(cases, shapes)]
     outs = [torch.full_like(e, float("nan")) for e in expected]
+    n_first = Q.lib().qi_alloc_count()  # the first calls, with their set-up, allocate nothing either
     # two calls in a row on one stream, no synchronisation between them
     for pair in ((0, 1), (2, 3)):
         for i in pair:
             x, wc, ws, b = cases[i]
             Q.check(noalloc(x, wc, ws, b, shapes[i][3], outs[i]))
         torch.cuda.synchronize()
+    assert Q.lib().qi_alloc_count() == n_first
     for o, e in zip(outs, expected):
         cos, maxrel = metrics(o, e)
         assert cos > 0.999999 and maxrel < 1e-5, (cos, maxrel)
-    # setup is done: repeated calls leave the device's free memory unchanged
+    # the library counts every CUDA allocation it makes: none in these calls
+    # (the first one above included); the device's free memory is a second,
+    # coarser signal
     again = [torch.full_like(e, float("nan")) for e in expected[:2]]
     torch.cuda.synchronize()
     free0 = torch.cuda.mem_get_info()[0]
+    n0 = Q.lib().qi_alloc_count()
     for i in (0, 1):
         x, wc, ws, b = cases[i]
         Q.check(noalloc(x, wc, ws, b, shapes[i][3], again[i]))
     torch.cuda.synchronize()
+    assert Q.lib().qi_alloc_count() == n0
     assert torch.cuda.mem_get_info()[0] == free0
     for a, o in zip(again, outs[:2]):
         assert torch.equal(a, o)
+    assert Q.lib().qi_linear_i8_f32in_noalloc_check() == 0
 
 
 def test_noalloc_rejects_requests_beyond_its_scratch():
@@ -78,3 +86,23 @@ def test_noalloc_rejects_requests_beyond_its_scratch():
         assert bool((out == 7.0).all())
     null = ctypes.c_void_p(0)
     assert Q.lib().qi_linear_i8_f32in_noalloc(null, 4, 256, null, null, 64, null, 0, null, null) == QI_ERR_ARG
+
+
+def test_noalloc_reports_a_timed_out_wait():
+    """A GEMM wait that gives up leaves its mark in the scratch's error word;
+    qi_linear_i8_f32in_noalloc_check reports it once and clears it, and the
+    entry keeps working afterwards."""
+    torch.cuda.set_device(0)
+    L = Q.lib()
+    assert L.qi_linear_i8_f32in_noalloc_check() == 0
+    n0 = L.qi_alloc_count()
+    Q.check(L.qi_linear_i8_f32in_noalloc_selftest(2000, Q._stream()))
+    assert L.qi_linear_i8_f32in_noalloc_check() == QI_ERR_DEVICE
+    assert L.qi_linear_i8_f32in_noalloc_check() == 0
+    x, wc, ws, b = case(64, 3072, 3072, "after_timeout")
+    out = torch.empty(64, 3072, device="cuda")
+    Q.check(noalloc(x, wc, ws, b, False, out))
+    assert L.qi_linear_i8_f32in_noalloc_check() == 0
+    assert L.qi_alloc_count() == n0
+    cos, maxrel = metrics(out, Q.linear_i8_f32in(x, wc, ws, b, False))
+    assert cos > 0.999999 and maxrel < 1e-5, (cos, maxrel)
