@@ -85,6 +85,51 @@ __device__ __forceinline__ float ex2_approx(float x) {
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
+// 2^x for x <= 0 on the FMA and integer pipes, for the share of the softmax
+// exponentials (QI_ATTN_POLY of every 16) taken off MUFU.  Cody-Waite split
+// x = n + f with n = rint(x) (1.5 * 2^23 added: the sum's low mantissa bits
+// hold n) and |f| <= 1/2; 2^f by the degree-QI_ATTN_POLY_DEG polynomial that
+// minimises the maximum relative error on [-1/2, 1/2] (fitted here by
+// Lawson's iteratively reweighted least squares; max relative error 7.5e-5
+// for degree 3, 2.7e-6 for 4, 2.3e-7 for 5 in FP32 Horner evaluation); n is
+// added to the exponent field.  x is clamped at -125 so the exponent cannot
+// underflow (2^-125 is zero in FP16 and negligible in the row sum).
+#ifndef QI_ATTN_POLY
+#define QI_ATTN_POLY 0
+#endif
+#ifndef QI_ATTN_POLY_DEG
+#define QI_ATTN_POLY_DEG 5
+#endif
+__device__ __forceinline__ float exp2_poly(float x) {
+  x = fmaxf(x, -125.0f);
+  const float t = __fadd_rn(x, 12582912.0f);
+  const float n = __fadd_rn(t, -12582912.0f);
+  const float f = __fadd_rn(x, -n);
+  float p;
+  if (QI_ATTN_POLY_DEG == 3) {
+    p = fmaf(0x1.c3f760p-5f, f, 0x1.f0de1cp-3f);
+    p = fmaf(p, f, 0x1.62f31ap-1f);
+    p = fmaf(p, f, 0x1.fff692p-1f);
+  } else if (QI_ATTN_POLY_DEG == 4) {
+    p = fmaf(0x1.3997d4p-7f, f, 0x1.ca1442p-5f);
+    p = fmaf(p, f, 0x1.ec06dap-3f);
+    p = fmaf(p, f, 0x1.62e0dcp-1f);
+    p = fmaf(p, f, 0x1.ffffe8p-1f);
+  } else {
+    p = fmaf(0x1.5c08e4p-10f, f, 0x1.3d0c54p-7f);
+    p = fmaf(p, f, 0x1.c6b6e4p-5f);
+    p = fmaf(p, f, 0x1.ebf918p-3f);
+    p = fmaf(p, f, 0x1.62e428p-1f);
+    p = fmaf(p, f, 0x1.000002p+0f);
+  }
+  return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
+}
+// Element i of a 16-key group takes the polynomial: QI_ATTN_POLY of every 16,
+// spread evenly.
+__host__ __device__ constexpr bool poly_slot(int i) {
+  return (i % 16) * QI_ATTN_POLY / 16 != ((i % 16) + 1) * QI_ATTN_POLY / 16;
+}
+
 __device__ __forceinline__ float rcp_approx(float x) {
   float y;
   asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -368,8 +413,8 @@ __global__ void __launch_bounds__(attn::THREADS, 1) sage_attn_kernel(const __gri
           const int g0 = (i0 >> 6) * 4 + ((i0 & 7) >> 1), g1 = (i1 >> 6) * 4 + ((i1 & 7) >> 1);
           const float x0 = fmaf(__int_as_float(static_cast<int>(r[i0]) + 0x4B400000), kf[g0], kb[g0]);
           const float x1 = fmaf(__int_as_float(static_cast<int>(r[i1]) + 0x4B400000), kf[g1], kb[g1]);
-          float p0 = ex2_approx(x0);
-          float p1 = ex2_approx(x1);
+          float p0 = poly_slot(i0) ? exp2_poly(x0) : ex2_approx(x0);
+          float p1 = poly_slot(i1) ? exp2_poly(x1) : ex2_approx(x1);
           if (TAIL) {
             if (i0 >= valid) p0 = 0.0f;
             if (i1 >= valid) p1 = 0.0f;
