@@ -42,6 +42,41 @@ __device__ __forceinline__ float warp_max(float v) {
   return v;
 }
 
+// max that returns NaN if either input is NaN (fmaxf drops NaNs), flushing
+// subnormal inputs like fmaxf under the build's fast-math flags.  For inputs
+// without NaN it equals fmaxf, so the row maximum it gives is the reference's
+// (fmaxf-based) unless the row holds a NaN, which it then reports.
+__device__ __forceinline__ float fmax_nan(float a, float b) {
+  float d;
+  asm("max.NaN.ftz.f32 %0, %1, %2;" : "=f"(d) : "f"(a), "f"(b));
+  return d;
+}
+__device__ __forceinline__ float warp_max_nan(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmax_nan(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// The quantizer's code for x = v * inv: the reference's
+// clamp(__float2int_rn(x), -128, 127) (fwht_quantize_kernel,
+// cuda_kernels.cu:2571-2575), as four bytes packed little-endian.
+__device__ __forceinline__ uint32_t codes4_ref(float x0, float x1, float x2, float x3) {
+  const int t0 = max(-128, min(127, __float2int_rn(x0))), t1 = max(-128, min(127, __float2int_rn(x1)));
+  const int t2 = max(-128, min(127, __float2int_rn(x2))), t3 = max(-128, min(127, __float2int_rn(x3)));
+  return __byte_perm(__byte_perm(t0, t1, 0x0040), __byte_perm(t2, t3, 0x0040), 0x5410);
+}
+// The same codes without the float-to-integer conversion unit, for rows whose
+// scaled values are finite with |x| < 127.5 (no NaN in the row and a finite
+// 127 / max): adding 1.5 * 2^23 rounds x to the nearest integer, ties to even
+// (the rounding of __float2int_rn), and leaves it in the low mantissa bits in
+// two's complement; no value reaches the clamp.  x must be the rounded
+// product (no fused multiply-add into the addition).
+__device__ __forceinline__ uint32_t codes4_fast(float x0, float x1, float x2, float x3) {
+  const int t0 = __float_as_int(__fadd_rn(x0, 12582912.0f)), t1 = __float_as_int(__fadd_rn(x1, 12582912.0f));
+  const int t2 = __float_as_int(__fadd_rn(x2, 12582912.0f)), t3 = __float_as_int(__fadd_rn(x3, 12582912.0f));
+  return __byte_perm(__byte_perm(t0, t1, 0x0040), __byte_perm(t2, t3, 0x0040), 0x5410);
+}
+
 // Sum over the 1024 threads of a reference reduction block in the order of
 // its two-level shfl_down tree.  The lane stands for reference warp `lane`
 // (threads 32 * lane + L, L = 0..31); part(q, p) gives the partials of threads
@@ -240,13 +275,14 @@ __global__ void __launch_bounds__(NW * 32) rowquant_warp_kernel(RowSegs segs, in
 #pragma unroll
   for (int m = 1; m < 32; m <<= 1) {
     if (4 * m >= had_block) break;
-    const bool upper = (lane & m) != 0;
+    const float sgn = (lane & m) ? -1.0f : 1.0f;
 #pragma unroll
     for (int j = 0; j < J; ++j)
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
+        // lower lane: a + b = v + p; upper lane: a - b = p - v; one rounding each
         const float p = __shfl_xor_sync(0xffffffffu, v[j][e], m);
-        v[j][e] = upper ? (p - v[j][e]) : (v[j][e] + p);
+        v[j][e] = fmaf(v[j][e], sgn, p);
       }
   }
   // half = 128 ..: across registers
@@ -276,26 +312,39 @@ __global__ void __launch_bounds__(NW * 32) rowquant_warp_kernel(RowSegs segs, in
 #pragma unroll
   for (int j = 0; j < J; ++j)
 #pragma unroll
-    for (int e = 0; e < 4; ++e) mx = fmaxf(mx, fabsf(v[j][e]));
-  mx = warp_max(mx);
+    for (int e = 0; e < 4; ++e) mx = fmax_nan(mx, fabsf(v[j][e]));
+  mx = warp_max_nan(mx);
   if (lane == 0) red[2][warp] = mx;
   __syncthreads();
   mx = red[2][0];
 #pragma unroll
-  for (int w = 1; w < NW; ++w) mx = fmaxf(mx, red[2][w]);
+  for (int w = 1; w < NW; ++w) mx = fmax_nan(mx, red[2][w]);
+  const bool nan_row = mx != mx;  // the same on every thread of the row
+  if (nan_row) {  // the reference's maximum ignores NaNs
+    mx = 0.0f;
+#pragma unroll
+    for (int j = 0; j < J; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) mx = fmaxf(mx, fabsf(v[j][e]));
+    mx = warp_max(mx);
+    if (lane == 0) red[0][warp] = mx;
+    __syncthreads();
+    mx = red[0][0];
+#pragma unroll
+    for (int w = 1; w < NW; ++w) mx = fmaxf(mx, red[0][w]);
+  }
   if (threadIdx.x == 0) scales[row] = mx / 127.0f;
   const float inv = (mx > 0.0f) ? 127.0f / mx : 0.0f;
-  int8_t* dst = codes + static_cast<long long>(row) * K + base;
+  uint32_t* dst = reinterpret_cast<uint32_t*>(codes + static_cast<long long>(row) * K + base);
+  if (!nan_row && mx <= 3.40282347e38f && inv <= 3.40282347e38f) {
 #pragma unroll
-  for (int j = 0; j < J; ++j) {
-    char4 q;
-    int t0 = __float2int_rn(v[j][0] * inv), t1 = __float2int_rn(v[j][1] * inv);
-    int t2 = __float2int_rn(v[j][2] * inv), t3 = __float2int_rn(v[j][3] * inv);
-    q.x = static_cast<signed char>(max(-128, min(127, t0)));
-    q.y = static_cast<signed char>(max(-128, min(127, t1)));
-    q.z = static_cast<signed char>(max(-128, min(127, t2)));
-    q.w = static_cast<signed char>(max(-128, min(127, t3)));
-    *reinterpret_cast<char4*>(dst + 128 * j) = q;
+    for (int j = 0; j < J; ++j)
+      dst[32 * j] = codes4_fast(__fmul_rn(v[j][0], inv), __fmul_rn(v[j][1], inv), __fmul_rn(v[j][2], inv),
+                                __fmul_rn(v[j][3], inv));
+  } else {
+#pragma unroll
+    for (int j = 0; j < J; ++j)
+      dst[32 * j] = codes4_ref(v[j][0] * inv, v[j][1] * inv, v[j][2] * inv, v[j][3] * inv);
   }
 }
 
@@ -319,6 +368,7 @@ __global__ void __launch_bounds__(96) rowquant_b4096_kernel(RowSegs segs, int ha
   // then [NW][1024 float4] prefetch slices
   extern __shared__ float4 tile4[];
   __shared__ float red[2][NW];
+  __shared__ float red_nan[NW];
   __shared__ __align__(8) uint64_t pbar[NW];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int base = warp * 4096 + 4 * lane;
@@ -431,23 +481,36 @@ __global__ void __launch_bounds__(96) rowquant_b4096_kernel(RowSegs segs, int ha
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
       v[j][e] *= norm;
-      mx = fmaxf(mx, fabsf(v[j][e]));
+      mx = fmax_nan(mx, fabsf(v[j][e]));
     }
-  mx = warp_max(mx);
+  mx = warp_max_nan(mx);
   if (lane == 0) red[it & 1][warp] = mx;  // double buffered: the next row's writes go to the other slot
   __syncthreads();
-  mx = fmaxf(fmaxf(red[it & 1][0], red[it & 1][1]), red[it & 1][2]);
+  mx = fmax_nan(fmax_nan(red[it & 1][0], red[it & 1][1]), red[it & 1][2]);
+  const bool nan_row = mx != mx;  // the same on every thread of the row
+  if (nan_row) {  // the reference's maximum ignores NaNs
+    mx = 0.0f;
+#pragma unroll
+    for (int j = 0; j < J; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) mx = fmaxf(mx, fabsf(v[j][e]));
+    mx = warp_max(mx);
+    if (lane == 0) red_nan[warp] = mx;
+    __syncthreads();
+    mx = fmaxf(fmaxf(red_nan[0], red_nan[1]), red_nan[2]);
+  }
   if (threadIdx.x == 0) scales[row] = mx / 127.0f;
   const float inv = (mx > 0.0f) ? 127.0f / mx : 0.0f;
-  int8_t* dst = codes + static_cast<long long>(row) * K + base;
+  uint32_t* dst = reinterpret_cast<uint32_t*>(codes + static_cast<long long>(row) * K + base);
+  if (!nan_row && mx <= 3.40282347e38f && inv <= 3.40282347e38f) {
 #pragma unroll
-  for (int j = 0; j < J; ++j) {
-    char4 q;
-    q.x = static_cast<signed char>(max(-128, min(127, __float2int_rn(v[j][0] * inv))));
-    q.y = static_cast<signed char>(max(-128, min(127, __float2int_rn(v[j][1] * inv))));
-    q.z = static_cast<signed char>(max(-128, min(127, __float2int_rn(v[j][2] * inv))));
-    q.w = static_cast<signed char>(max(-128, min(127, __float2int_rn(v[j][3] * inv))));
-    *reinterpret_cast<char4*>(dst + 128 * j) = q;
+    for (int j = 0; j < J; ++j)
+      dst[32 * j] = codes4_fast(__fmul_rn(v[j][0], inv), __fmul_rn(v[j][1], inv), __fmul_rn(v[j][2], inv),
+                                __fmul_rn(v[j][3], inv));
+  } else {
+#pragma unroll
+    for (int j = 0; j < J; ++j)
+      dst[32 * j] = codes4_ref(v[j][0] * inv, v[j][1] * inv, v[j][2] * inv, v[j][3] * inv);
   }
   }
 }

@@ -67,6 +67,15 @@ def _act(M, K, seed, scale=1.0):
         x[1, 7] *= 1000.0
     if M > 2:
         x[2] = 1e-39  # subnormal row: flushed to zero like the reference (fast math)
+    if M > 3:
+        x[3, 5] = float("nan")  # NaN: the reference's max ignores it, its code is 0
+    if M > 4:
+        x[4, 9] = float("inf")  # infinite element (and the NaNs the transform makes of it)
+    if M > 5:
+        x[5] = 0.0
+        x[5, 3] = 1e-36  # tiny maximum: 127 / max overflows to infinity
+    if M > 6:
+        x[6] = -0.0
     return x
 
 
