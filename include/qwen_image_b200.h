@@ -181,6 +181,24 @@ int qi_ctx_check(qi_ctx* ctx);
 #define QI_COMM_ID_BYTES 128
 int qi_comm_unique_id(void* id_out);
 int qi_ctx_set_comm(qi_ctx* ctx, const void* id, int rank, int nranks);
+/* Failure detection of the group (new: the reference has no multi-GPU path;
+ * its errors print and exit, tensor.h:15-37).  The communicator is
+ * non-blocking: every collective step the library takes (joining the group,
+ * the exchanges of a forward, the output gather) waits at most timeout_ms
+ * (default 60000) for NCCL; on an asynchronous NCCL error or a missed
+ * deadline the communicator is aborted, the call returns QI_ERR_NCCL, and
+ * multi-GPU calls on the context keep returning QI_ERR_NCCL until
+ * qi_ctx_set_comm forms a group again (nranks = 1 returns it to one GPU).
+ * A rank that never joins makes qi_ctx_set_comm return QI_ERR_NCCL after
+ * the deadline instead of blocking.                                          */
+int qi_ctx_set_comm_timeout(qi_ctx* ctx, int timeout_ms);
+/* Waits, polling, until the work queued on `stream` has finished, at most
+ * timeout_ms (<= 0: the context's collective deadline).  If the group's
+ * communicator reports an error, or the deadline passes with a group set, the
+ * communicator is aborted (its pending collectives end) and QI_ERR_NCCL is
+ * returned; a missed deadline without a group is QI_ERR_DEVICE.  Otherwise it
+ * returns what qi_ctx_check returns.                                         */
+int qi_ctx_sync(qi_ctx* ctx, void* stream, int timeout_ms);
 /* The per-peer byte offsets and sizes a rank uses in the two all-to-all
  * exchanges of a head-parallel block (which = 0: Q/K/V before attention,
  * which = 1: attention output after it), for a joint sequence of n_txt text

@@ -29,7 +29,9 @@
 #include <nccl.h>
 
 #include <atomic>
+#include <chrono>
 #include <cstdlib>
+#include <thread>
 #include <map>
 #include <mutex>
 #include <string>
@@ -102,8 +104,10 @@ struct qi_ctx {
   int device = 0;
   int num_sms = 148;
   int* err = nullptr;  // device error word
-  ncclComm_t comm = nullptr;  // head-parallel group (qi_ctx_set_comm)
+  ncclComm_t comm = nullptr;  // head-parallel group (qi_ctx_set_comm), non-blocking
   int urank = 0, usize = 1;
+  bool comm_failed = false;   // the group's communicator was aborted; multi-GPU calls fail
+  int comm_timeout_ms = 60000;  // deadline of every collective step (qi_ctx_set_comm_timeout)
   // direct exchanges over peer memory: the group's buffers mapped here (CUDA
   // IPC), set up for one forward shape (peer_key) at a time
   PeerSet peers = {};
@@ -191,6 +195,67 @@ struct qi_model {
   }
 };
 
+// ------------------------------------------------------------------ collectives
+// The head-parallel communicator is non-blocking (ncclConfig_t.blocking = 0):
+// no NCCL call can hold the host thread.  A call that returns ncclInProgress
+// is polled (ncclCommGetAsyncError) until it settles or the context's
+// deadline passes; on an error or a missed deadline the communicator is
+// aborted (ncclCommAbort ends its pending operations) and the call returns
+// QI_ERR_NCCL.  The reference has no multi-GPU path; its CUDA errors print
+// and exit (tensor.h:15-37).
+namespace {
+
+double now_ms() {
+  return std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now().time_since_epoch()).count();
+}
+
+void abort_comm(qi_ctx* c) {
+  if (c->comm) ncclCommAbort(c->comm);
+  c->comm = nullptr;
+  c->comm_failed = true;
+}
+
+// Orderly teardown of a healthy communicator: finalize (non-blocking, so
+// polled with the deadline), then destroy; aborted if it does not settle.
+void destroy_comm(qi_ctx* c) {
+  if (!c->comm) return;
+  ncclResult_t r = ncclCommFinalize(c->comm);
+  const double deadline = now_ms() + c->comm_timeout_ms;
+  while (r == ncclInProgress && now_ms() < deadline) {
+    std::this_thread::sleep_for(std::chrono::microseconds(50));
+    if (ncclCommGetAsyncError(c->comm, &r) != ncclSuccess) r = ncclSystemError;
+  }
+  if (r == ncclSuccess)
+    ncclCommDestroy(c->comm);
+  else
+    ncclCommAbort(c->comm);
+  c->comm = nullptr;
+}
+
+// Waits for the communicator's current call (which returned `r`) to settle.
+int nccl_settle(qi_ctx* c, ncclResult_t r) {
+  if (r == ncclSuccess) return QI_OK;
+  if (r != ncclInProgress || !c->comm) {
+    abort_comm(c);
+    return QI_ERR_NCCL;
+  }
+  const double deadline = now_ms() + c->comm_timeout_ms;
+  while (true) {
+    ncclResult_t st = ncclSuccess;
+    if (ncclCommGetAsyncError(c->comm, &st) != ncclSuccess) st = ncclSystemError;
+    if (st == ncclSuccess) return QI_OK;
+    if (st != ncclInProgress || now_ms() > deadline) {
+      abort_comm(c);
+      return QI_ERR_NCCL;
+    }
+    std::this_thread::sleep_for(std::chrono::microseconds(50));
+  }
+}
+
+}  // namespace
+
+#define QI_NCCL(c, call) QI_TRY(nccl_settle((c), (call)))
+
 extern "C" {
 
 const char* qi_status_string(int st) {
@@ -240,9 +305,45 @@ int qi_ctx_destroy(qi_ctx* c) {
   c->close_peers();
   if (c->flags) cudaFree(c->flags);
   if (c->handles) cudaFree(c->handles);
-  if (c->comm) ncclCommDestroy(c->comm);
+  destroy_comm(c);
   delete c;
   return QI_OK;
+}
+
+int qi_ctx_set_comm_timeout(qi_ctx* c, int timeout_ms) {
+  if (!c || timeout_ms <= 0) return QI_ERR_ARG;
+  c->comm_timeout_ms = timeout_ms;
+  return QI_OK;
+}
+
+int qi_ctx_sync(qi_ctx* c, void* stream, int timeout_ms) {
+  if (!c) return QI_ERR_ARG;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const double deadline = now_ms() + (timeout_ms > 0 ? timeout_ms : c->comm_timeout_ms);
+  while (true) {
+    const cudaError_t q = cudaStreamQuery(s);
+    if (q == cudaSuccess) break;
+    if (q != cudaErrorNotReady) return QI_ERR_CUDA;
+    if (c->comm) {
+      ncclResult_t st = ncclSuccess;
+      if (ncclCommGetAsyncError(c->comm, &st) != ncclSuccess) st = ncclSystemError;
+      if (st != ncclSuccess && st != ncclInProgress) {
+        abort_comm(c);
+        return QI_ERR_NCCL;
+      }
+    }
+    if (now_ms() > deadline) {
+      // a collective that waits for a peer is the one thing on the stream that
+      // cannot end by itself (the library's own waits are bounded): abort it
+      if (c->comm) {
+        abort_comm(c);
+        return QI_ERR_NCCL;
+      }
+      return QI_ERR_DEVICE;
+    }
+    std::this_thread::sleep_for(std::chrono::microseconds(20));
+  }
+  return qi_ctx_check(c);
 }
 
 int qi_comm_unique_id(void* id_out) {
@@ -257,10 +358,8 @@ int qi_comm_unique_id(void* id_out) {
 int qi_ctx_set_comm(qi_ctx* c, const void* id, int rank, int nranks) {
   if (!c || nranks < 1 || nranks > kMaxRanks || kHeads % nranks || rank < 0 || rank >= nranks) return QI_ERR_ARG;
   c->close_peers();
-  if (c->comm) {
-    ncclCommDestroy(c->comm);
-    c->comm = nullptr;
-  }
+  destroy_comm(c);
+  c->comm_failed = false;
   c->urank = 0;
   c->usize = 1;
   // a new group starts its barrier epochs from zero on every rank
@@ -271,10 +370,11 @@ int qi_ctx_set_comm(qi_ctx* c, const void* id, int rank, int nranks) {
   if (cudaSetDevice(c->device) != cudaSuccess) return QI_ERR_CUDA;
   ncclUniqueId uid;
   memcpy(&uid, id, sizeof(uid));
-  if (ncclCommInitRank(&c->comm, nranks, uid, rank) != ncclSuccess) {
-    c->comm = nullptr;
-    return QI_ERR_NCCL;
-  }
+  ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
+  cfg.blocking = 0;  // every call returns at once; nccl_settle waits with a deadline
+  const ncclResult_t r = ncclCommInitRankConfig(&c->comm, nranks, uid, rank, &cfg);
+  // a rank that never joins: the initialisation misses the deadline and is aborted
+  QI_NCCL(c, r);
   c->urank = rank;
   c->usize = nranks;
   return QI_OK;
@@ -640,13 +740,14 @@ int exchange(qi_ctx* c, int which, int nb, const ShardMap& mp, const void* send,
   const int me = c->urank;
   if (sb[me] && cudaMemcpyAsync(rp + ro[me], sp + so[me], sb[me], cudaMemcpyDeviceToDevice, s) != cudaSuccess)
     return QI_ERR_CUDA;
-  if (ncclGroupStart() != ncclSuccess) return QI_ERR_NCCL;
+  QI_NCCL(c, ncclGroupStart());
   for (int q = 0; q < mp.P; ++q) {
     if (q == me) continue;
-    if (sb[q] && ncclSend(sp + so[q], sb[q], ncclUint8, q, c->comm, s) != ncclSuccess) return QI_ERR_NCCL;
-    if (rb[q] && ncclRecv(rp + ro[q], rb[q], ncclUint8, q, c->comm, s) != ncclSuccess) return QI_ERR_NCCL;
+    if (sb[q]) QI_NCCL(c, ncclSend(sp + so[q], sb[q], ncclUint8, q, c->comm, s));
+    if (rb[q]) QI_NCCL(c, ncclRecv(rp + ro[q], rb[q], ncclUint8, q, c->comm, s));
   }
-  return ncclGroupEnd() == ncclSuccess ? QI_OK : QI_ERR_NCCL;
+  QI_NCCL(c, ncclGroupEnd());
+  return QI_OK;
 }
 
 // Shapes and workspace views of one forward; the stages below share it.
@@ -694,7 +795,7 @@ int setup_peers(Fwd& f) {
            cudaIpcGetMemHandle(&mine[2], c->flags) == cudaSuccess;
   char* hd = static_cast<char*>(c->handles);  // [mine 3][all P x 3][ok, ok_min]
   if (cudaMemcpyAsync(hd, mine, 3 * kH, cudaMemcpyHostToDevice, f.s) != cudaSuccess) return QI_ERR_CUDA;
-  if (ncclAllGather(hd, hd + 3 * kH, 3 * kH, ncclUint8, c->comm, f.s) != ncclSuccess) return QI_ERR_NCCL;
+  QI_NCCL(c, ncclAllGather(hd, hd + 3 * kH, 3 * kH, ncclUint8, c->comm, f.s));
   std::vector<cudaIpcMemHandle_t> all(static_cast<size_t>(P) * 3);
   if (cudaMemcpyAsync(all.data(), hd + 3 * kH, static_cast<size_t>(P) * 3 * kH, cudaMemcpyDeviceToHost, f.s) !=
           cudaSuccess ||
@@ -728,7 +829,7 @@ int setup_peers(Fwd& f) {
   int* okd = reinterpret_cast<int*>(hd + (kMaxRanks + 1) * 3 * kH);
   int ok_all = 0;
   if (cudaMemcpyAsync(okd, &ok, sizeof(int), cudaMemcpyHostToDevice, f.s) != cudaSuccess) return QI_ERR_CUDA;
-  if (ncclAllReduce(okd, okd + 1, 1, ncclInt32, ncclMin, c->comm, f.s) != ncclSuccess) return QI_ERR_NCCL;
+  QI_NCCL(c, ncclAllReduce(okd, okd + 1, 1, ncclInt32, ncclMin, c->comm, f.s));
   if (cudaMemcpyAsync(&ok_all, okd + 1, sizeof(int), cudaMemcpyDeviceToHost, f.s) != cudaSuccess ||
       cudaStreamSynchronize(f.s) != cudaSuccess)
     return QI_ERR_CUDA;
@@ -769,6 +870,7 @@ int fwd_init(Fwd& f, qi_ctx* c, const qi_model* m, int nb, int n_img, int n_txt,
   f.n_img = n_img;
   f.n_txt = n_txt;
   f.S = n_img + n_txt;
+  if (c->comm_failed) return QI_ERR_NCCL;  // the group was aborted: rejoin with qi_ctx_set_comm
   f.P = c->usize;
   f.rank = c->urank;
   f.Hl = kHeads / f.P;
@@ -985,20 +1087,20 @@ int fwd_output(Fwd& f, const float* x_img, int H, int W, void* out) {
                           proj + static_cast<size_t>(b) * f.n_img_l * kPatchDim, f.n_img_l * rowb,
                           cudaMemcpyDeviceToDevice, s) != cudaSuccess)
         return QI_ERR_CUDA;
-    if (ncclGroupStart() != ncclSuccess) return QI_ERR_NCCL;
+    QI_NCCL(c, ncclGroupStart());
     for (int q = 0; q < f.P; ++q) {
       if (q == f.rank) continue;
       const int nq = f.map.n_img_l(q);
       for (int b = 0; b < f.nb; ++b) {
-        if (f.n_img_l && ncclSend(proj + static_cast<size_t>(b) * f.n_img_l * kPatchDim,
-                                  static_cast<size_t>(f.n_img_l) * kPatchDim, ncclFloat32, q, c->comm, s) != ncclSuccess)
-          return QI_ERR_NCCL;
-        if (nq && ncclRecv(full + (static_cast<size_t>(b) * f.n_img + f.map.img_lo[q]) * kPatchDim,
-                           static_cast<size_t>(nq) * kPatchDim, ncclFloat32, q, c->comm, s) != ncclSuccess)
-          return QI_ERR_NCCL;
+        if (f.n_img_l)
+          QI_NCCL(c, ncclSend(proj + static_cast<size_t>(b) * f.n_img_l * kPatchDim,
+                              static_cast<size_t>(f.n_img_l) * kPatchDim, ncclFloat32, q, c->comm, s));
+        if (nq)
+          QI_NCCL(c, ncclRecv(full + (static_cast<size_t>(b) * f.n_img + f.map.img_lo[q]) * kPatchDim,
+                              static_cast<size_t>(nq) * kPatchDim, ncclFloat32, q, c->comm, s));
       }
     }
-    if (ncclGroupEnd() != ncclSuccess) return QI_ERR_NCCL;
+    QI_NCCL(c, ncclGroupEnd());
     proj = full;
   }
   QI_LAUNCH(QI_PROF_POST, 1, unpatchify_launch(proj, out, f.nb, H, W, s));

@@ -51,11 +51,16 @@ def bench_gemm(iters, res):
         sa = torch.rand(M, device="cuda") * 1e-3
         sw = torch.rand(N, device="cuda") * 1e-3
         b = torch.zeros(N, dtype=torch.bfloat16, device="cuda")
-        out = torch.empty(M, N, device="cuda")
-        epi = Q.EPI_GELU if name == "fc1" else Q.EPI_STORE
-        ms = time_it(lambda: Q.linear_i8(a, sa, w, sw, b, epi, out=out), iters)
+        out = torch.zeros(M, N, device="cuda")
+        gate = torch.rand(N, device="cuda") * 1e-3
+        # the epilogue each layer runs in the forward: QKV store, out-projection
+        # and fc2 the gated residual update, fc1 GELU
+        epi = {"qkv": Q.EPI_STORE, "out": Q.EPI_RESIDUAL, "fc1": Q.EPI_GELU, "fc2": Q.EPI_RESIDUAL}[name]
+        g = gate if epi == Q.EPI_RESIDUAL else None
+        ms = time_it(lambda: Q.linear_i8(a, sa, w, sw, b, epi, gate=g, out=out), iters)
         tf = 2.0 * M * N * K / (ms * 1e-3) / 1e12
-        res[f"gemm_{name}"] = {"M": M, "N": N, "K": K, "ms": round(ms, 4), "tops": round(tf, 1)}
+        res[f"gemm_{name}"] = {"M": M, "N": N, "K": K, "epilogue": ["store", "gelu", "residual"][epi], "ms": round(ms, 4),
+                               "tops": round(tf, 1)}
         # cuBLASLt INT8 GEMM on the same operands (INT32 output, no epilogue),
         # for reference: the library's rate on this B200 for this shape
         wt = w.t()

@@ -102,6 +102,8 @@ def lib():
             "qi_ctx_profile": ([vp, vp, vp, i], i),
             "qi_comm_unique_id": ([vp], i),
             "qi_ctx_set_comm": ([vp, vp, i, i], i),
+            "qi_ctx_set_comm_timeout": ([vp, i], i),
+            "qi_ctx_sync": ([vp, vp, i], i),
             "qi_exchange_plan": ([i, i, i, i, i, i, vp, vp, vp, vp], i),
             "qi_rope_table": ([i, i, i, vp], i),
             "qi_synth_fill": ([vp, ll, ull, f, f, i, vp], i),
@@ -337,6 +339,15 @@ class Context:
         rank 0) as `rank` of `nranks`; collective over the group."""
         buf = ctypes.create_string_buffer(bytes(uid), COMM_ID_BYTES) if uid is not None else None
         check(lib().qi_ctx_set_comm(self.h, buf, rank, nranks))
+
+    def set_comm_timeout(self, ms):
+        check(lib().qi_ctx_set_comm_timeout(self.h, int(ms)))
+
+    def sync(self, timeout_ms=0):
+        """Bounded wait for this context's work on the current stream; raises
+        QIError (QI_ERR_NCCL) if the group's collectives failed or missed the
+        deadline."""
+        check(lib().qi_ctx_sync(self.h, _stream(), int(timeout_ms)))
 
     def close(self):
         if self.h:

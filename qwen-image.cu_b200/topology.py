@@ -41,3 +41,64 @@ def shard_map(P, n_txt, n_img):
     """Token ranges per Ulysses rank: lists txt_lo, img_lo of length P + 1
     (the same even split the library uses)."""
     return [r * n_txt // P for r in range(P + 1)], [r * n_img // P for r in range(P + 1)]
+
+
+class RankFailure(RuntimeError):
+    """Ranks of the job that did not finish a step in time, or left."""
+
+    def __init__(self, step, missing, left):
+        self.step, self.missing, self.left = step, sorted(missing), sorted(left)
+        super().__init__(f"step {step}: rank(s) {self.missing} did not finish step {step - 1} in time"
+                         + (f"; rank(s) {self.left} left the job" if self.left else ""))
+
+
+class StepMonitor:
+    """Liveness of the ranks of a job between steps, on the host.
+
+    Before a rank launches step k (and with it the collectives that wait for
+    every peer), it checks through the process group's key-value store that
+    every rank has finished step k - 1.  A rank that left (announced with
+    leave(), or simply gone) or stopped reporting is found within
+    `timeout_s` on every other rank, which then raise RankFailure instead of
+    launching a collective that would wait for it.  The library's own
+    collectives have a deadline too (qi_ctx_set_comm_timeout); this check
+    keeps a whole job from reaching one."""
+
+    def __init__(self, store, rank, world, timeout_s=10.0, prefix="qi_step"):
+        self.store, self.rank, self.world = store, rank, world
+        self.timeout_s, self.prefix = float(timeout_s), prefix
+
+    def _key(self, step, rank):
+        return f"{self.prefix}/{step}/{rank}"
+
+    def finished(self, step):
+        """This rank has finished `step` (its collectives included)."""
+        self.store.set(self._key(step, self.rank), "1")
+
+    def leave(self):
+        """This rank leaves the job between steps."""
+        self.store.set(f"{self.prefix}/left/{self.rank}", "1")
+
+    def check(self, step):
+        """Raises RankFailure unless every rank finished step - 1 within the
+        timeout.  Step 0 needs nothing."""
+        if step == 0:
+            return
+        import datetime
+        import time
+        keys = [self._key(step - 1, r) for r in range(self.world)]
+        deadline = time.monotonic() + self.timeout_s
+        while True:
+            missing = [r for r, k in enumerate(keys) if not self.store.check([k])]
+            left = [r for r in range(self.world) if self.store.check([f"{self.prefix}/left/{r}"])]
+            if not missing:
+                return
+            gone = set(left) & set(missing)
+            if gone:  # known to have left: no need to wait out the deadline for it
+                raise RankFailure(step, gone, left)
+            if time.monotonic() > deadline:
+                raise RankFailure(step, missing, left)
+            try:
+                self.store.wait([keys[missing[0]]], datetime.timedelta(milliseconds=50))
+            except Exception:
+                pass

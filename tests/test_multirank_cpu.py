@@ -200,3 +200,48 @@ def test_exchange_plan_sizes_match_shard_map():
             so, sb, ro, rb = Q.exchange_plan(1, 1, 256, 6889, P, r)
             assert sb == [(24 // P) * L[q] * 256 for q in range(P)]
             assert rb == [(24 // P) * L[r] * 256] * P
+
+
+# ------------------------------------------------------------------ failure detection
+# Host-side: a rank that never reports a step, or leaves between steps, is
+# found by every other rank through the store before it launches the next
+# step's collectives (topology.StepMonitor).  The failures are made on the
+# host (a rank that stops reporting or exits); no device is involved.
+def _monitor_worker(rank, world, port, mode, out):
+    import time
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        import datetime
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=20))
+        store = dist.distributed_c10d._get_default_store()
+        mon = T.StepMonitor(store, rank, world, timeout_s=2.0, prefix=f"t_{mode}")
+        t0 = time.monotonic()
+        for step in range(4):
+            mon.check(step)
+            t = torch.full((4,), float(rank + step))
+            dist.all_reduce(t)  # the step's collective: every rank reaches it only after the check
+            assert t[0].item() == sum(r + step for r in range(world))
+            if mode == "silent" and rank == world - 1 and step == 1:
+                time.sleep(6.0)  # never reports step 1; alive, but stuck on the host
+                out.put((rank, "ok"))
+                return
+            if mode == "leave" and rank == world - 1 and step == 1:
+                mon.leave()
+                out.put((rank, "ok"))
+                return  # leaves between steps, nothing in flight
+            mon.finished(step)
+        out.put((rank, "ok" if mode == "none" else "no failure seen"))
+    except T.RankFailure as e:
+        dt = time.monotonic() - t0
+        expect = e.step == 2 and e.missing == [world - 1] and (mode == "silent" or e.left == [world - 1])
+        out.put((rank, "ok" if expect and dt < 10.0 else f"wrong failure {e} after {dt:.1f} s"))
+    except BaseException as e:
+        out.put((rank, repr(e)))
+    finally:
+        if dist.is_initialized() and mode == "none":
+            dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("mode,world", [("none", 2), ("silent", 2), ("leave", 2), ("leave", 3)])
+def test_step_monitor_finds_failed_rank(mode, world):
+    _run(_monitor_worker, world, mode)
