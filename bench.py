@@ -416,6 +416,89 @@ def cpu_baseline(args):
                       f"(FLOP ratio to one C4 CFG step)"}
 
 
+# ------------------------------------------------------------------ loader
+def _write_checkpoint(path, blocks):
+    """A quantize.cu-format INT8 checkpoint (transformer.h:407-563 names) of
+    `blocks` double-stream blocks, streamed tensor by tensor (every block
+    carries the same synthetic tensors)."""
+    import qib200 as Q
+    g, bl = Q.make_weight_table(1, base_seed=0)
+    dt = {torch.int8: "I8", torch.float32: "F32", torch.bfloat16: "BF16"}
+    entries = [(name, t) for (name, kind), t in zip(Q.G_NAMES, g)]
+    for i in range(blocks):
+        pre = f"transformer_blocks.{i}."
+        for li, (lname, N, K) in enumerate(Q.L_NAMES):
+            c, sc, b = bl[0][3 * li:3 * li + 3]
+            entries += [(pre + lname + ".weight", c), (pre + lname + ".weight.__scales__", sc),
+                        (pre + lname + ".bias", b)]
+        for k, nname in enumerate(Q.B_NORMS):
+            entries.append((pre + nname, bl[0][3 * len(Q.L_NAMES) + k]))
+    header, off = {}, 0
+    for name, t in entries:
+        nbytes = t.numel() * t.element_size()
+        header[name] = {"dtype": dt[t.dtype], "shape": list(t.shape), "data_offsets": [off, off + nbytes]}
+        off += nbytes
+    h = json.dumps(header).encode()
+    h += b" " * ((8 - len(h) % 8) % 8)
+    import struct
+    with open(path, "wb") as f:
+        f.write(struct.pack("<Q", len(h)))
+        f.write(h)
+        host = {}
+        for name, t in entries:
+            key = t.data_ptr()
+            if key not in host:
+                host[key] = (t.view(torch.int16) if t.dtype == torch.bfloat16 else t).cpu().numpy().tobytes()
+            f.write(host[key])
+    return 8 + len(h) + off
+
+
+def run_loader(args):
+    """Checkpoint load throughput: the product's loader (qi_model_load_safetensors:
+    pinned chunked upload, then the kernels' layout) against the reference's
+    per-tensor path (safetensors.h:174-212) on the same file, page cache warm
+    for both; GB of file per second."""
+    import shutil
+    import tempfile
+    import qib200 as Q
+    import qi_ref as R
+    torch.cuda.set_device(0)
+    tmp = tempfile.mkdtemp(prefix="qi_ckpt_")
+    try:
+        free = shutil.disk_usage(tmp).free
+        blocks = max(1, min(args.loader_blocks, int(free * 0.25 // 345e6)))
+        path = os.path.join(tmp, "transformer_int8.safetensors")
+        size = _write_checkpoint(path, blocks)
+        with open(path, "rb") as f:  # warm the page cache
+            while f.read(1 << 26):
+                pass
+        ctx = Q.Context(0)
+        res = {"metric": "INT8 safetensors checkpoint load, GB/s of file (page cache warm)", "file_gb": round(size / 1e9, 3),
+               "blocks": blocks}
+        best = {}
+        for _ in range(2):
+            for arm in ("product", "reference"):
+                torch.cuda.synchronize()
+                t0 = time.time()
+                if arm == "product":
+                    m = Q.Model.from_safetensors(ctx, path)
+                    torch.cuda.synchronize()
+                    dt = time.time() - t0
+                    m.close()
+                else:
+                    if not R.available():
+                        continue
+                    R.load_all(path)
+                    dt = time.time() - t0
+                best[arm] = min(best.get(arm, 1e9), dt)
+        for arm, dt in best.items():
+            res[arm] = {"seconds": round(dt, 3), "gbs": round(size / dt / 1e9, 2)}
+        ctx.close()
+        print(json.dumps(res), flush=True)
+    finally:
+        shutil.rmtree(tmp, ignore_errors=True)
+
+
 # ------------------------------------------------------------------ reference arm
 def run_reference(args):
     rank, world, local = dist_env()
@@ -493,6 +576,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--loader", action="store_true",
+                    help="time the checkpoint loader against the reference's instead of the step")
+    ap.add_argument("--loader-blocks", type=int, default=8, help="blocks in the --loader checkpoint")
     ap.add_argument("--workload", default="c4", choices=["c4", "c5"],
                     help="c4: 1328x1328 (the headline metric); c5: 2048x2048, 20 steps (scaling study)")
     args = ap.parse_args()
@@ -505,7 +591,9 @@ def main():
     if args.warmup < 3:
         print("warmup < 3 is not a valid measurement; using 3", file=sys.stderr)
         args.warmup = 3
-    if args.impl == "reference":
+    if args.loader:
+        run_loader(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)

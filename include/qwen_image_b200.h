@@ -121,6 +121,19 @@ long long qi_alloc_count(void);
 int qi_sage_attention(const void* q_f16, const void* k_f16, const void* v_f16, float* out, float scale, int BH,
                       int S, int D, void* stream);
 
+/* The FP8 P.V variant of qi_sage_attention (same arguments and output
+ * layout): Q and K INT8 with one scale per 128 queries / 64 keys (after K
+ * mean smoothing), V as E4M3 codes with one scale per (batch-head, dim)
+ * (max |V| / 448), P as E4M3 codes of 448 P with the running max updated at
+ * every increase, P.V on tcgen05.mma.kind::f8f6f4.  The reference ships the
+ * FP8 building blocks of this scheme (sageattention_mma.cuh:521-680,
+ * sageattention_numeric_conversion.cuh:46-140,
+ * sageattention_attn_utils.cuh:141-168) but launches only the FP16 P.V
+ * kernel; this variant is checked against exact attention, not against the
+ * reference.  head_dim must be 128.                                          */
+int qi_sage_attention_fp8pv(const void* q_f16, const void* k_f16, const void* v_f16, float* out, float scale, int BH,
+                            int S, int D, void* stream);
+
 /* The Sage quantizers alone, for bit-exact checks against the reference:
  * k_mean [BH,128]; Q codes [BH,S,128] + scales [BH, ceil(S/128)*32];
  * K codes [BH,S,128] + scales [BH, ceil(S/64)*4]
@@ -167,6 +180,12 @@ int qi_ctx_destroy(qi_ctx* ctx);
 /* Reads (and clears) the device error word a kernel raised; QI_ERR_DEVICE if
  * any kernel gave up a bounded wait since the last call.  Synchronous.      */
 int qi_ctx_check(qi_ctx* ctx);
+
+/* Selects the FP8 P.V variant for the attention of qi_forward /
+ * qi_forward_blocks on this context (enable != 0), or the FP16 P.V kernel the
+ * reference launches (0, the default).  Off the reference's numerics: its
+ * outputs are checked against exact attention, not against the reference.   */
+int qi_ctx_set_attention_fp8pv(qi_ctx* ctx, int enable);
 
 /* Head-parallel (Ulysses) group.  New: the reference runs on one GPU
  * (its main.cu:761-773 calls transformer_forward for cond and uncond in

@@ -39,6 +39,7 @@ def lib():
             "ref_rope_table": [i, i, i, vp],
             "ref_rope_fp16": [vp, vp, vp, i, i],
             "ref_gate_add": [vp, vp, vp, vp, i, i],
+            "ref_load_all": [ctypes.c_char_p, vp],
             "ref_transformer_forward": [vp, vp, vp, f, vp, i, vp, i, i, i, vp],
         }
         for name, args in sig.items():
@@ -140,6 +141,14 @@ def gate_add(inp, gate, x):
     out = torch.empty_like(inp)
     _ok(lib().ref_gate_add(_p(inp), _p(gate), _p(x), _p(out), inp.shape[0], inp.shape[1]))
     return out
+
+
+def load_all(path):
+    """The reference's per-tensor upload of every tensor in a safetensors
+    checkpoint (each freed after upload); returns the bytes uploaded."""
+    n = ctypes.c_longlong(0)
+    _ok(lib().ref_load_all(path.encode(), ctypes.byref(n)))
+    return n.value
 
 
 def rope_table(h, w, n_txt):

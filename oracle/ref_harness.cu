@@ -184,6 +184,24 @@ int ref_gate_add(const float* input, const float* gate, const float* x, float* o
   return sync_status();
 }
 
+// The reference's checkpoint upload path (SafeTensorsLoader::load_tensor,
+// safetensors.h:174-212: per tensor fopen / fseek / fread into a host vector,
+// cudaMalloc, synchronous cudaMemcpy) over every tensor of `path`, each freed
+// after its upload.  Returns the bytes uploaded.  Timing baseline of the
+// product's loader.
+int ref_load_all(const char* path, long long* bytes) {
+  SafeTensorsLoader L;
+  L.load(path);
+  long long total = 0;
+  for (const auto& kv : L.tensors) {
+    Tensor t = L.load_tensor(kv.first);
+    total += static_cast<long long>(kv.second.nbytes);
+    t.free_data();
+  }
+  *bytes = total;
+  return sync_status();
+}
+
 // RoPE table from the reference's own host code (rope.h:175).
 int ref_rope_table(int h, int w, int n_txt, float* pe_host) {
   std::vector<float> pe = RoPE::gen_qwen_image_pe(h, w, 2, 1, n_txt, 10000, {16, 56, 56});

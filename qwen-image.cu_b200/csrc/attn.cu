@@ -52,8 +52,10 @@ constexpr int OFF_K = OFF_Q + NT * Q_BYTES;
 constexpr int OFF_V = OFF_K + STAGES * K_BYTES;
 constexpr int OFF_BAR = OFF_V + STAGES * V_BYTES;
 constexpr int OFF_KS = OFF_BAR + 256;  // this batch-head's K scales (FP32), loaded once
+constexpr int V8_BYTES = BKV * D;     // fp8 e4m3 V^T tile (FP8 P.V variant)
 constexpr int MAX_S = kAttnMaxS;
-constexpr int smem_bytes(int ngk) { return OFF_KS + ngk * 4 + 1024; }
+// K scales, then the 128 per-dimension V factors of the FP8 P.V variant
+constexpr int smem_bytes(int ngk) { return OFF_KS + ngk * 4 + 512 + 1024; }
 constexpr int THREADS = 384;  // warpgroup 0: TMA warp, MMA warp, 2 idle; warpgroups 1, 2: softmax of tiles 0, 1
 // Register split (setmaxnreg): launched at 168 per thread (384 x 168 = 64512);
 // warpgroup 0 keeps 88 (the MMA warp holds its descriptors in every lane),
@@ -69,6 +71,7 @@ struct alignas(64) AttnArgsDev {
   CUtensorMap tmQ, tmK, tmV;
   const float* qs;
   const float* ks;
+  const float* vs;  // FP8 P.V: per (batch-head, dim) output factor v_scale / 448
   void* out;
   int BH, S, heads, out_mode, nb, n_img, n_txt, ngq, ngk;
   float qk_scale;  // sm_scale * log2(e)
@@ -145,6 +148,23 @@ __device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity) {
   }
 }
 
+// E4M3 codes of four values, the first in the lowest byte (cvt.rn.satfinite
+// puts its first operand in the upper byte of each pair).
+__device__ __forceinline__ uint32_t pack_e4m3x4(float a, float b, float c, float d) {
+  uint16_t lo, hi;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(lo) : "f"(b), "f"(a));
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(hi) : "f"(d), "f"(c));
+  return static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
+}
+
+// FP8 = true: the FP8 P.V variant (SageAttention2's scheme, the FP8 e4m3
+// helpers of sageattention_mma.cuh:521-680 and
+// sageattention_numeric_conversion.cuh:46-140, which the reference ships but
+// does not launch): V arrives as E4M3 codes of V / v_scale transposed to
+// [dim][token], P is rescaled at every row-max increase (P <= 1), stored as
+// E4M3 codes of 448 P, and P.V runs as tcgen05.mma.kind::f8f6f4; the output
+// factor per dimension is v_scale / 448.
+template <bool FP8>
 __global__ void __launch_bounds__(attn::THREADS, 1) sage_attn_kernel(const __grid_constant__ AttnArgsDev args) {
   using namespace attn;
   extern __shared__ uint8_t smem_raw[];
@@ -153,6 +173,7 @@ __global__ void __launch_bounds__(attn::THREADS, 1) sage_attn_kernel(const __gri
   uint8_t* sK = smem + OFF_K;
   uint8_t* sV = smem + OFF_V;
   float* sKS = reinterpret_cast<float*>(smem + OFF_KS);
+  float* sVS = sKS + args.ngk;  // FP8: this batch-head's 128 V factors
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
   uint64_t* q_full = bars + 0;
   uint64_t* k_full = bars + 1;                // [STAGES]
@@ -200,6 +221,7 @@ __global__ void __launch_bounds__(attn::THREADS, 1) sage_attn_kernel(const __gri
   if (warp >= 4) {  // K scales of this batch-head into shared memory
     const float* ks = args.ks + static_cast<size_t>(bh) * args.ngk;
     for (int i = threadIdx.x - 128; i < args.ngk; i += THREADS - 128) sKS[i] = ks[i];
+    if (FP8 && threadIdx.x - 128 < D) sVS[threadIdx.x - 128] = args.vs[static_cast<size_t>(bh) * D + threadIdx.x - 128];
   }
   tc_fence_before();
   __syncthreads();
@@ -223,9 +245,14 @@ __global__ void __launch_bounds__(attn::THREADS, 1) sage_attn_kernel(const __gri
           kmask |= 1u << st;
           kpar = (kpar & ~(1u << st)) | (ph << st);
           if (!mbar_wait(&v_empty[st], ph ^ 1u, abort_flag)) { ok = false; break; }
-          mbar_expect_tx(&v_full[st], V_BYTES);
-          tma_load_3d(sV + st * V_BYTES, &args.tmV, 0, j * BKV, bh, &v_full[st]);
-          tma_load_3d(sV + st * V_BYTES + V_BYTES / 2, &args.tmV, 64, j * BKV, bh, &v_full[st]);
+          if (FP8) {  // V^T codes [dim][token]: 128 dims x 128 keys, K-major
+            mbar_expect_tx(&v_full[st], V8_BYTES);
+            tma_load_3d(sV + st * V_BYTES, &args.tmV, j * BKV, 0, bh, &v_full[st]);
+          } else {
+            mbar_expect_tx(&v_full[st], V_BYTES);
+            tma_load_3d(sV + st * V_BYTES, &args.tmV, 0, j * BKV, bh, &v_full[st]);
+            tma_load_3d(sV + st * V_BYTES + V_BYTES / 2, &args.tmV, 64, j * BKV, bh, &v_full[st]);
+          }
           vmask |= 1u << st;
           vpar = (vpar & ~(1u << st)) | (ph << st);
         }
@@ -247,14 +274,15 @@ __global__ void __launch_bounds__(attn::THREADS, 1) sage_attn_kernel(const __gri
         };
         bool ok = wait_all(q_full, 0);
         const uint32_t id_qk = idesc_i8(BQ, BKV);
-        const uint32_t id_pv = idesc_f16(BQ, D, false, true);
+        // P.V: FP16 P with MN-major FP16 V, or E4M3 P with K-major E4M3 V^T
+        const uint32_t id_pv = idesc_f16(BQ, D, false, !FP8);
         const uint32_t q_addr = smem_u32(sQ);
         // Shared-memory descriptors are built once; an operand at a byte offset is
         // the base descriptor plus offset / 16 in its address field (no carry: shared
         // addresses stay below 2^18).
         const uint64_t qd0 = umma_desc_sw128(q_addr, 16, 1024);
         const uint64_t kd0 = umma_desc_sw128(smem_u32(sK), 16, 1024);
-        const uint64_t vd0 = umma_desc_sw128(smem_u32(sV), V_BYTES / 2, 1024);
+        const uint64_t vd0 = FP8 ? umma_desc_sw128(smem_u32(sV), 16, 1024) : umma_desc_sw128(smem_u32(sV), V_BYTES / 2, 1024);
         // S_t = Q_t . K^T for the block in stage st
         auto qk = [&](int t, int st) {
           const uint64_t qa = qd0 + static_cast<uint64_t>(t * (Q_BYTES >> 4));
@@ -268,10 +296,19 @@ __global__ void __launch_bounds__(attn::THREADS, 1) sage_attn_kernel(const __gri
         auto pv_half = [&](int t, int st, int j, int h) {
           const uint64_t vb = vd0 + static_cast<uint64_t>((st * V_BYTES) >> 4);
           const uint32_t d = tmem + TM_O + 128 * t, a = tmem + TM_S + 128 * t;
+          if (FP8) {
+            // 32 keys per instruction: 8 TMEM columns of P, 32 bytes along V^T's K
   #pragma unroll
-          for (int k4 = 0; k4 < BKV / 32; ++k4) {
-            const int kk = h * (BKV / 32) + k4;
-            mma_f16_ts_elect(d, a + kk * 8, vb + 128 * kk, id_pv, (j > 0 || kk > 0) ? 1u : 0u);
+            for (int k2 = 0; k2 < 2; ++k2) {
+              const int kk = 2 * h + k2;
+              mma_f8_ts_elect(d, a + kk * 8, vb + 2 * kk, id_pv, (j > 0 || kk > 0) ? 1u : 0u);
+            }
+          } else {
+  #pragma unroll
+            for (int k4 = 0; k4 < BKV / 32; ++k4) {
+              const int kk = h * (BKV / 32) + k4;
+              mma_f16_ts_elect(d, a + kk * 8, vb + 128 * kk, id_pv, (j > 0 || kk > 0) ? 1u : 0u);
+            }
           }
         };
         if (ok) ok = wait_all(&k_full[0], 0);
@@ -378,7 +415,8 @@ __global__ void __launch_bounds__(attn::THREADS, 1) sage_attn_kernel(const __gri
       // grows by more than 8 (P stays <= 2^8, exact in FP16 range); O and l are
       // rescaled with it, so O / l is unchanged in exact arithmetic.
       const float m_new = fmaxf(m, mloc);
-      const bool grow = m_new > m + 8.0f;
+      // (FP8: at every increase, so that P <= 1 and 448 P fits E4M3)
+      const bool grow = FP8 ? (m_new > m) : (m_new > m + 8.0f);
       const float alpha = grow ? ex2_approx(m - m_new) : 1.0f;
       const float m_use = grow ? m_new : m;
       if (j > 0 && __any_sync(0xffffffffu, grow)) {
@@ -406,6 +444,26 @@ __global__ void __launch_bounds__(attn::THREADS, 1) sage_attn_kernel(const __gri
       auto exp_half = [&](auto tail_tag, int h) {
         const int hbase = 64 * h;
         constexpr bool TAIL = decltype(tail_tag)::value;
+        if constexpr (FP8) {
+          // four keys per TMEM column: E4M3 codes of 448 P
+          uint32_t p8[16];
+#pragma unroll
+          for (int c = 0; c < 16; ++c) {
+            float p4[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const int i = hbase + 4 * c + e;
+              const int g = (i >> 6) * 4 + ((i & 7) >> 1);
+              const float x = fmaf(__int_as_float(static_cast<int>(r[i]) + 0x4B400000), kf[g], kb[g]);
+              float p = ex2_approx(x);
+              if (TAIL && i >= valid) p = 0.0f;
+              lp[(4 * c + e) & 7] += p;
+              p4[e] = p * 448.0f;
+            }
+            p8[c] = pack_e4m3x4(p4[0], p4[1], p4[2], p4[3]);
+          }
+          tmem_st16(s_tm + hbase / 4, p8);
+        } else {
         uint32_t pk[32];
 #pragma unroll
         for (int c = 0; c < 32; ++c) {
@@ -425,6 +483,7 @@ __global__ void __launch_bounds__(attn::THREADS, 1) sage_attn_kernel(const __gri
           pk[c] = *reinterpret_cast<uint32_t*>(&h2);
         }
         tmem_st32(s_tm + hbase / 2, pk);
+        }
         // publish this half (and, for h = 0, the rescaled O) to the MMA warp
         tmem_st_wait();
         tc_fence_before();
@@ -495,6 +554,10 @@ __global__ void __launch_bounds__(attn::THREADS, 1) sage_attn_kernel(const __gri
         tmem_ld_wait();
         tmem_reg_fence32(r);
         if (!valid) continue;
+        if (FP8) {  // the per-dimension V factor folded into the accumulator
+#pragma unroll
+          for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * sVS[c + i]);
+        }
         if (args.out_mode == 0) {
           float* dst = reinterpret_cast<float*>(args.out) + (static_cast<size_t>(bh) * S + qrow) * D + c;
 #pragma unroll
@@ -602,8 +665,29 @@ __global__ void __launch_bounds__(256) sage_kmean_kernel(const __half* __restric
     if (warp < DPC / 32) {
       const int n = min(T, S - c * T);
       const __half* col = km_tile + static_cast<size_t>(c % NB) * T * DPC + warp * 32 + lane;
+      if (n == T) {
+        // software-pipelined: the next 16 tokens are read from shared memory
+        // while the chain adds the current 16, so only the adds' latency is
+        // on the chain's path (same token order, same sum)
+        float a[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) a[i] = __half2float(col[i * DPC]);
+#pragma unroll 1
+        for (int t = 16; t < T; t += 16) {
+          float b[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) b[i] = __half2float(col[(t + i) * DPC]);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) sum += a[i];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) a[i] = b[i];
+        }
+#pragma unroll
+        for (int i = 0; i < 16; ++i) sum += a[i];
+      } else {
 #pragma unroll 8
-      for (int t = 0; t < n; ++t) sum += __half2float(col[t * DPC]);
+        for (int t = 0; t < n; ++t) sum += __half2float(col[t * DPC]);
+      }
     }
   }
   asm volatile("cp.async.wait_group 0;" ::: "memory");
@@ -677,9 +761,10 @@ __global__ void __launch_bounds__(256) sage_quant_q_kernel(const __half* __restr
 
 // K per-thread INT8 after mean smoothing (sageattention_sm80.cu:826-886): one
 // CTA per (128 keys, batch-head); warp w handles scale group w % 4 of 64-key
-// block w / 4, tokens 2 (w % 4) + 8i + {0, 1}, i = 0..7, lane = 4 dims.  Two
-// passes over the group's 4 KB: the absolute max, then (from L1) the codes --
-// few registers, so many warps per SM keep enough loads in flight.
+// block w / 4, tokens 2 (w % 4) + 8i + {0, 1}, i = 0..7, lane = 4 dims.  One
+// pass: the group's 16 tokens are loaded at once (all loads in flight
+// together), held in registers through the absolute max, then scaled and
+// stored.
 __global__ void __launch_bounds__(256) sage_quant_k_kernel(const __half* __restrict__ k, const float* __restrict__ kmean,
                                                            int8_t* __restrict__ kc, float* __restrict__ ks, int S) {
   const int bh = blockIdx.y;
@@ -690,25 +775,26 @@ __global__ void __launch_bounds__(256) sage_quant_k_kernel(const __half* __restr
   int8_t* out = kc + static_cast<size_t>(bh) * S * 128 + lane * 4;
   const float4 mean = *reinterpret_cast<const float4*>(kmean + bh * 128 + lane * 4);
   const int token_base = blk * 64 + g * 2;
-  auto load = [&](int i, float (&v)[4]) {
+  uint2 raw[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
     const int t = token_base + (i >> 1) * 8 + (i & 1);
-    const bool in = t < S;
-    uint2 raw = make_uint2(0, 0);
-    if (in) raw = *reinterpret_cast<const uint2*>(hp + static_cast<size_t>(t) * 128);
-    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
-    const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
-    v[0] = in ? a.x - mean.x : 0.0f;
-    v[1] = in ? a.y - mean.y : 0.0f;
-    v[2] = in ? b.x - mean.z : 0.0f;
-    v[3] = in ? b.y - mean.w : 0.0f;
-  };
+    raw[i] = t < S ? __ldg(reinterpret_cast<const uint2*>(hp + static_cast<size_t>(t) * 128)) : make_uint2(0, 0);
+  }
+  float v[16][4];
   float am[4] = {1e-7f, 1e-7f, 1e-7f, 1e-7f};
 #pragma unroll
   for (int i = 0; i < 16; ++i) {
-    float v[4];
-    load(i, v);
+    const int t = token_base + (i >> 1) * 8 + (i & 1);
+    const bool in = t < S;
+    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&raw[i].x));
+    const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&raw[i].y));
+    v[i][0] = in ? a.x - mean.x : 0.0f;
+    v[i][1] = in ? a.y - mean.y : 0.0f;
+    v[i][2] = in ? b.x - mean.z : 0.0f;
+    v[i][3] = in ? b.y - mean.w : 0.0f;
 #pragma unroll
-    for (int e = 0; e < 4; ++e) am[i & 3] = fmaxf(am[i & 3], fabsf(v[e]));
+    for (int e = 0; e < 4; ++e) am[i & 3] = fmaxf(am[i & 3], fabsf(v[i][e]));
   }
   const float block_amax = warp_max_f(fmaxf(fmaxf(am[0], am[1]), fmaxf(am[2], am[3])));
   const float block_scale = block_amax / 127.0f + 1e-7f;
@@ -718,15 +804,167 @@ __global__ void __launch_bounds__(256) sage_quant_k_kernel(const __half* __restr
   for (int i = 0; i < 16; ++i) {
     const int t = token_base + (i >> 1) * 8 + (i & 1);
     if (t >= S) continue;
-    float v[4];
-    load(i, v);
     char4 c;
-    c.x = cvt_rni_sat_s8(v[0] * inv_scale);
-    c.y = cvt_rni_sat_s8(v[1] * inv_scale);
-    c.z = cvt_rni_sat_s8(v[2] * inv_scale);
-    c.w = cvt_rni_sat_s8(v[3] * inv_scale);
+    c.x = cvt_rni_sat_s8(v[i][0] * inv_scale);
+    c.y = cvt_rni_sat_s8(v[i][1] * inv_scale);
+    c.z = cvt_rni_sat_s8(v[i][2] * inv_scale);
+    c.w = cvt_rni_sat_s8(v[i][3] * inv_scale);
     *reinterpret_cast<char4*>(out + static_cast<size_t>(t) * 128) = c;
   }
+}
+
+// ------------------------------------------------ FP8 P.V variant quantizers
+// Per-block INT8 of Q (TOK = 128 queries) or of K - mean (TOK = 64 keys): one
+// CTA per (block, batch-head), 8 warps, warp w on tokens w * TOK/8 .. , lane =
+// 4 dims; scale = max|x| / 127 + 1e-7 (the per-thread quantizer's
+// expressions over the whole block), written to the GROUPS entries of the
+// block in the per-thread scale layout.
+template <int TOK, int GROUPS>
+__global__ void __launch_bounds__(256) sage_quant_block_kernel(const __half* __restrict__ x, const float* __restrict__ mean,
+                                                               int8_t* __restrict__ codes, float* __restrict__ scales,
+                                                               int S) {
+  constexpr int TPW = TOK / 8;  // tokens per warp
+  __shared__ float red[8];
+  const int blk = blockIdx.x, bh = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const __half* hp = x + static_cast<size_t>(bh) * S * 128 + lane * 4;
+  int8_t* out = codes + static_cast<size_t>(bh) * S * 128 + lane * 4;
+  float4 mu = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (mean) mu = *reinterpret_cast<const float4*>(mean + bh * 128 + lane * 4);
+  float v[TPW][4];
+  float am = 1e-7f;
+#pragma unroll
+  for (int i = 0; i < TPW; ++i) {
+    const int t = blk * TOK + warp * TPW + i;
+    uint2 raw = make_uint2(0, 0);
+    if (t < S) raw = __ldg(reinterpret_cast<const uint2*>(hp + static_cast<size_t>(t) * 128));
+    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
+    const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
+    const bool in = t < S;
+    v[i][0] = in ? a.x - mu.x : 0.0f;
+    v[i][1] = in ? a.y - mu.y : 0.0f;
+    v[i][2] = in ? b.x - mu.z : 0.0f;
+    v[i][3] = in ? b.y - mu.w : 0.0f;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) am = fmaxf(am, fabsf(v[i][e]));
+  }
+  am = warp_max_f(am);
+  if (lane == 0) red[warp] = am;
+  __syncthreads();
+  am = red[0];
+#pragma unroll
+  for (int w = 1; w < 8; ++w) am = fmaxf(am, red[w]);
+  const float scale = am / 127.0f + 1e-7f;
+  if (threadIdx.x < GROUPS) scales[static_cast<size_t>(bh) * (((S + TOK - 1) / TOK) * GROUPS) + blk * GROUPS + threadIdx.x] = scale;
+  const float inv = 1.0f / scale;
+#pragma unroll
+  for (int i = 0; i < TPW; ++i) {
+    const int t = blk * TOK + warp * TPW + i;
+    if (t >= S) continue;
+    char4 c;
+    c.x = cvt_rni_sat_s8(v[i][0] * inv);
+    c.y = cvt_rni_sat_s8(v[i][1] * inv);
+    c.z = cvt_rni_sat_s8(v[i][2] * inv);
+    c.w = cvt_rni_sat_s8(v[i][3] * inv);
+    *reinterpret_cast<char4*>(out + static_cast<size_t>(t) * 128) = c;
+  }
+}
+
+// max |V| per (batch-head, dim) over the tokens: 256-token slices per CTA,
+// combined with atomicMax on the (non-negative) float bits.
+__global__ void __launch_bounds__(256) sage_v_amax_kernel(const __half* __restrict__ v, float* __restrict__ vamax, int S) {
+  __shared__ float red[8][128];
+  const int bh = blockIdx.y, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const __half* hp = v + static_cast<size_t>(bh) * S * 128 + lane * 4;
+  float am[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 4
+  for (int i = 0; i < 32; ++i) {
+    const int t = blockIdx.x * 256 + warp + 8 * i;
+    if (t >= S) break;
+    const uint2 raw = __ldg(reinterpret_cast<const uint2*>(hp + static_cast<size_t>(t) * 128));
+    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
+    const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
+    am[0] = fmaxf(am[0], fabsf(a.x));
+    am[1] = fmaxf(am[1], fabsf(a.y));
+    am[2] = fmaxf(am[2], fabsf(b.x));
+    am[3] = fmaxf(am[3], fabsf(b.y));
+  }
+#pragma unroll
+  for (int e = 0; e < 4; ++e) red[warp][lane * 4 + e] = am[e];
+  __syncthreads();
+  if (threadIdx.x < 128) {
+    float m = red[0][threadIdx.x];
+#pragma unroll
+    for (int w = 1; w < 8; ++w) m = fmaxf(m, red[w][threadIdx.x]);
+    atomicMax(reinterpret_cast<int*>(vamax) + bh * 128 + threadIdx.x, __float_as_int(m));
+  }
+}
+
+// E4M3 codes of V / v_scale (v_scale = max|V| / 448 per dim) transposed to
+// [BH][128][s_pad]: one CTA per 64 tokens of a batch-head; tokens in
+// [S, s_pad) are zero.  vs = v_scale / 448, the output factor of 448 P . V.
+__global__ void __launch_bounds__(256) sage_v_fp8_kernel(const __half* __restrict__ v, const float* __restrict__ vamax,
+                                                         uint8_t* __restrict__ vt, float* __restrict__ vs, int S,
+                                                         int s_pad) {
+  __shared__ uint8_t tile[128][64 + 16];
+  const int bh = blockIdx.y, t0 = blockIdx.x * 64;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const float4 am = *reinterpret_cast<const float4*>(vamax + bh * 128 + lane * 4);
+  const float inv[4] = {am.x > 0.f ? 448.0f / am.x : 0.f, am.y > 0.f ? 448.0f / am.y : 0.f,
+                        am.z > 0.f ? 448.0f / am.z : 0.f, am.w > 0.f ? 448.0f / am.w : 0.f};
+  if (blockIdx.x == 0 && warp == 0) {
+    vs[bh * 128 + lane * 4 + 0] = am.x / (448.0f * 448.0f);
+    vs[bh * 128 + lane * 4 + 1] = am.y / (448.0f * 448.0f);
+    vs[bh * 128 + lane * 4 + 2] = am.z / (448.0f * 448.0f);
+    vs[bh * 128 + lane * 4 + 3] = am.w / (448.0f * 448.0f);
+  }
+  const __half* hp = v + static_cast<size_t>(bh) * S * 128 + lane * 4;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int tl = warp * 8 + i, t = t0 + tl;
+    float x[4] = {0.f, 0.f, 0.f, 0.f};
+    if (t < S) {
+      const uint2 raw = __ldg(reinterpret_cast<const uint2*>(hp + static_cast<size_t>(t) * 128));
+      const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
+      const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
+      x[0] = a.x * inv[0];
+      x[1] = a.y * inv[1];
+      x[2] = b.x * inv[2];
+      x[3] = b.y * inv[3];
+    }
+    const uint32_t c = pack_e4m3x4(x[0], x[1], x[2], x[3]);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) tile[lane * 4 + e][tl] = static_cast<uint8_t>(c >> (8 * e));
+  }
+  __syncthreads();
+  // row d of the tile: 64 bytes = four 16-byte pieces
+  for (int i = threadIdx.x; i < 128 * 4; i += 256) {
+    const int d = i >> 2, piece = i & 3, t = t0 + piece * 16;
+    if (t >= s_pad) continue;
+    const uint4 val = *reinterpret_cast<const uint4*>(&tile[d][piece * 16]);
+    *reinterpret_cast<uint4*>(vt + (static_cast<size_t>(bh) * 128 + d) * s_pad + t) = val;
+  }
+}
+
+int sage_quantize_fp8pv_launch(const void* q, const void* k, const void* v, int BH, int S, float* kmean, int8_t* qc,
+                               float* qs, int8_t* kc, float* ks, uint8_t* vt, int s_pad, float* vamax, float* vs,
+                               cudaStream_t stream) {
+  if (BH <= 0 || S <= 0 || s_pad < S || s_pad % 16) return QI_ERR_ARG;
+  const int sms = device_num_sms();
+  const __half* kh = reinterpret_cast<const __half*>(k);
+  const __half* vh = reinterpret_cast<const __half*>(v);
+  const int st = (BH * 4 <= sms) ? kmean_launch<32>(kh, kmean, BH, S, stream)
+                 : (BH * 2 <= sms) ? kmean_launch<64>(kh, kmean, BH, S, stream)
+                                   : kmean_launch<128>(kh, kmean, BH, S, stream);
+  if (st != QI_OK) return st;
+  sage_quant_block_kernel<128, 32><<<dim3((S + 127) / 128, BH), 256, 0, stream>>>(
+      reinterpret_cast<const __half*>(q), nullptr, qc, qs, S);
+  sage_quant_block_kernel<64, 4><<<dim3((S + 63) / 64, BH), 256, 0, stream>>>(kh, kmean, kc, ks, S);
+  if (cudaMemsetAsync(vamax, 0, static_cast<size_t>(BH) * 128 * sizeof(float), stream) != cudaSuccess)
+    return QI_ERR_CUDA;
+  sage_v_amax_kernel<<<dim3((S + 255) / 256, BH), 256, 0, stream>>>(vh, vamax, S);
+  sage_v_fp8_kernel<<<dim3((s_pad + 63) / 64, BH), 256, 0, stream>>>(vh, vamax, vt, vs, S, s_pad);
+  return cudaGetLastError() == cudaSuccess ? QI_OK : QI_ERR_CUDA;
 }
 
 int sage_quantize_launch(const void* q, const void* k, int BH, int S, float* kmean, int8_t* qc, float* qs, int8_t* kc,
@@ -757,6 +995,19 @@ static int encode_3d(CUtensorMap* tm, CUtensorMapDataType dt, int esize, const v
   return r == CUDA_SUCCESS ? QI_OK : QI_ERR_CUDA;
 }
 
+// E4M3 V^T codes [BH][128 dims][s_pad tokens]: 128-key x 128-dim boxes
+// (128 bytes along the tokens, the K dimension of P.V), 128-byte swizzle.
+static int encode_vt(CUtensorMap* tm, const void* base, int s_pad, int BH) {
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(s_pad), 128, static_cast<cuuint64_t>(BH)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(s_pad), static_cast<cuuint64_t>(s_pad) * 128};
+  cuuint32_t box[3] = {128, 128, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = qi_encode_tiled(tm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box,
+                               estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? QI_OK : QI_ERR_CUDA;
+}
+
 int attention_launch(const AttnArgs& a, cudaStream_t stream, int* err_dev) {
   if (a.BH <= 0 || a.S <= 0) return QI_ERR_ARG;
   if ((reinterpret_cast<uintptr_t>(a.qc) & 15) || (reinterpret_cast<uintptr_t>(a.kc) & 15) ||
@@ -766,22 +1017,29 @@ int attention_launch(const AttnArgs& a, cudaStream_t stream, int* err_dev) {
   // The setmaxnreg split assumes the kernel was built for exactly LAUNCH_REGS
   // registers per thread; with fewer, the softmax warpgroups' increase could
   // never be granted.  Refuse to launch rather than risk that.
-  static int regs_checked = 0;
-  if (!regs_checked) {
+  if (a.fp8 && (!a.vs || a.s_pad < a.S || a.s_pad % 16)) return QI_ERR_ARG;
+  const void* kfn = a.fp8 ? reinterpret_cast<const void*>(sage_attn_kernel<true>)
+                          : reinterpret_cast<const void*>(sage_attn_kernel<false>);
+  static int regs_checked[2] = {0, 0};
+  if (!regs_checked[a.fp8 ? 1 : 0]) {
     cudaFuncAttributes fa;
-    if (cudaFuncGetAttributes(&fa, sage_attn_kernel) != cudaSuccess) return QI_ERR_CUDA;
+    if (cudaFuncGetAttributes(&fa, kfn) != cudaSuccess) return QI_ERR_CUDA;
     if (fa.numRegs != attn::LAUNCH_REGS) return QI_ERR_UNSUPPORTED;
-    regs_checked = 1;
+    regs_checked[a.fp8 ? 1 : 0] = 1;
   }
-  static unsigned long long attr_done = 0;
-  if (smem_optin(reinterpret_cast<const void*>(sage_attn_kernel), attn::smem_bytes(((attn::MAX_S + 63) / 64) * 4),
-                 &attr_done) != QI_OK)
+  static unsigned long long attr_done[2] = {0, 0};
+  if (smem_optin(kfn, attn::smem_bytes(((attn::MAX_S + 63) / 64) * 4), &attr_done[a.fp8 ? 1 : 0]) != QI_OK)
     return QI_ERR_CUDA;
   AttnArgsDev d;
   memset(&d, 0, sizeof(d));
   if (encode_3d(&d.tmQ, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a.qc, a.S, a.BH, 128) != QI_OK) return QI_ERR_CUDA;
   if (encode_3d(&d.tmK, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a.kc, a.S, a.BH, 128) != QI_OK) return QI_ERR_CUDA;
-  if (encode_3d(&d.tmV, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, a.v, a.S, a.BH, 64) != QI_OK) return QI_ERR_CUDA;
+  if (a.fp8) {
+    if (encode_vt(&d.tmV, a.v, a.s_pad, a.BH) != QI_OK) return QI_ERR_CUDA;
+  } else if (encode_3d(&d.tmV, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, a.v, a.S, a.BH, 64) != QI_OK) {
+    return QI_ERR_CUDA;
+  }
+  d.vs = a.vs;
   d.qs = a.qs;
   d.ks = a.ks;
   d.out = a.out;
@@ -801,7 +1059,10 @@ int attention_launch(const AttnArgs& a, cudaStream_t stream, int* err_dev) {
   d.head_base = a.head_base;
   if (a.out_mode >= 2 && (a.map.P < 1 || a.map.P > kMaxRanks)) return QI_ERR_ARG;
   dim3 grid((a.S + attn::NT * attn::BQ - 1) / (attn::NT * attn::BQ), a.BH);
-  sage_attn_kernel<<<grid, attn::THREADS, attn::smem_bytes(d.ngk), stream>>>(d);
+  if (a.fp8)
+    sage_attn_kernel<true><<<grid, attn::THREADS, attn::smem_bytes(d.ngk), stream>>>(d);
+  else
+    sage_attn_kernel<false><<<grid, attn::THREADS, attn::smem_bytes(d.ngk), stream>>>(d);
   return cudaGetLastError() == cudaSuccess ? QI_OK : QI_ERR_CUDA;
 }
 

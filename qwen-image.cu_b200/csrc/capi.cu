@@ -97,7 +97,7 @@ static inline cudaStream_t S_(void* s) { return reinterpret_cast<cudaStream_t>(s
 enum BufId {
   B_PATCH, B_TEMB256, B_TACT, B_TACT_S, B_T1, B_TEMB, B_TSILU, B_MODS, B_ADA, B_X, B_TXTN, B_ACT, B_ACT_S, B_QKV,
   B_QKVH, B_QC, B_KC, B_QS, B_KS, B_KMEAN, B_O, B_H, B_FIN, B_PROJ, B_SEND1, B_RECV1, B_SEND2, B_RECV2,
-  B_PROJF, B_COUNT
+  B_PROJF, B_V8, B_VAMAX, B_VS, B_COUNT
 };
 
 struct qi_ctx {
@@ -107,6 +107,7 @@ struct qi_ctx {
   ncclComm_t comm = nullptr;  // head-parallel group (qi_ctx_set_comm), non-blocking
   int urank = 0, usize = 1;
   bool comm_failed = false;   // the group's communicator was aborted; multi-GPU calls fail
+  bool attn_fp8 = false;      // forward attention: FP8 P.V variant (qi_ctx_set_attention_fp8pv)
   int comm_timeout_ms = 60000;  // deadline of every collective step (qi_ctx_set_comm_timeout)
   // direct exchanges over peer memory: the group's buffers mapped here (CUDA
   // IPC), set up for one forward shape (peer_key) at a time
@@ -307,6 +308,12 @@ int qi_ctx_destroy(qi_ctx* c) {
   if (c->handles) cudaFree(c->handles);
   destroy_comm(c);
   delete c;
+  return QI_OK;
+}
+
+int qi_ctx_set_attention_fp8pv(qi_ctx* c, int enable) {
+  if (!c) return QI_ERR_ARG;
+  c->attn_fp8 = enable != 0;
   return QI_OK;
 }
 
@@ -515,6 +522,34 @@ int qi_sage_attention(const void* q_f16, const void* k_f16, const void* v_f16, f
                               c->p<int8_t>(B_KC), c->p<float>(B_KS), S_(stream)));
   AttnArgs a{c->p<int8_t>(B_QC), c->p<float>(B_QS), c->p<int8_t>(B_KC), c->p<float>(B_KS), v_f16, out, BH, S, BH,
              scale, 0, 1, 0, 0};
+  return attention_launch(a, S_(stream), c->err);
+}
+
+int qi_sage_attention_fp8pv(const void* q_f16, const void* k_f16, const void* v_f16, float* out, float scale, int BH,
+                            int S, int D, void* stream) {
+  if (D != 128) return QI_ERR_UNSUPPORTED;
+  if (!q_f16 || !k_f16 || !v_f16 || !out || BH <= 0 || S <= 0) return QI_ERR_ARG;
+  if (S > kAttnMaxS) return QI_ERR_UNSUPPORTED;
+  qi_ctx* c = default_ctx();
+  if (!c) return QI_ERR_CUDA;
+  const size_t n = static_cast<size_t>(BH) * S * 128;
+  const int s_pad = (S + 15) & ~15;
+  QI_TRY(c->ensure(B_QC, n));
+  QI_TRY(c->ensure(B_KC, n));
+  QI_TRY(c->ensure(B_QS, static_cast<size_t>(BH) * ((S + 127) / 128) * 32 * 4));
+  QI_TRY(c->ensure(B_KS, static_cast<size_t>(BH) * ((S + 63) / 64) * 4 * 4));
+  QI_TRY(c->ensure(B_KMEAN, static_cast<size_t>(BH) * 128 * 4));
+  QI_TRY(c->ensure(B_V8, static_cast<size_t>(BH) * 128 * s_pad));
+  QI_TRY(c->ensure(B_VAMAX, static_cast<size_t>(BH) * 128 * 4));
+  QI_TRY(c->ensure(B_VS, static_cast<size_t>(BH) * 128 * 4));
+  QI_TRY(sage_quantize_fp8pv_launch(q_f16, k_f16, v_f16, BH, S, c->p<float>(B_KMEAN), c->p<int8_t>(B_QC),
+                                    c->p<float>(B_QS), c->p<int8_t>(B_KC), c->p<float>(B_KS), c->p<uint8_t>(B_V8), s_pad,
+                                    c->p<float>(B_VAMAX), c->p<float>(B_VS), S_(stream)));
+  AttnArgs a{c->p<int8_t>(B_QC), c->p<float>(B_QS), c->p<int8_t>(B_KC), c->p<float>(B_KS), c->buf[B_V8], out, BH, S, BH,
+             scale, 0, 1, 0, 0};
+  a.fp8 = 1;
+  a.vs = c->p<float>(B_VS);
+  a.s_pad = s_pad;
   return attention_launch(a, S_(stream), c->err);
 }
 
@@ -904,6 +939,12 @@ int fwd_init(Fwd& f, qi_ctx* c, const qi_model* m, int nb, int n_img, int n_txt,
   QI_TRY(c->ensure(B_QS, static_cast<size_t>(f.BH) * ((f.S + 127) / 128) * 32 * 4));
   QI_TRY(c->ensure(B_KS, static_cast<size_t>(f.BH) * ((f.S + 63) / 64) * 4 * 4));
   QI_TRY(c->ensure(B_KMEAN, static_cast<size_t>(f.BH) * kHeadDim * 4));
+  if (c->attn_fp8) {
+    const int s_pad = (f.S + 15) & ~15;
+    QI_TRY(c->ensure(B_V8, static_cast<size_t>(f.BH) * kHeadDim * s_pad));
+    QI_TRY(c->ensure(B_VAMAX, static_cast<size_t>(f.BH) * kHeadDim * 4));
+    QI_TRY(c->ensure(B_VS, static_cast<size_t>(f.BH) * kHeadDim * 4));
+  }
   QI_TRY(c->ensure(B_O, f.Ma * kDim * 2));
   QI_TRY(c->ensure(B_H, f.Ma * kMlp * 4));
   QI_TRY(c->ensure(B_FIN, f.Mi * kDim * 2));
@@ -1020,15 +1061,29 @@ int fwd_blocks(Fwd& f, float* x_img, float* x_txt, const float* pe, int b0, int 
       QI_LAUNCH(QI_PROF_EXCHANGE, 0, exchange(c, 0, nb, f.map, c->buf[B_SEND1], c->buf[B_RECV1], s));
       QI_LAUNCH(QI_PROF_EXCHANGE, 1, ulysses_gather_qkv_launch(c->buf[B_RECV1], qkvh, nb, f.Hl, n_txt, f.map, s));
     }
-    QI_LAUNCH(QI_PROF_SAGE_QUANT, 3,
-              sage_quantize_launch(qkvh, qkvh + hs, BH, S, c->p<float>(B_KMEAN), c->p<int8_t>(B_QC),
-                                   c->p<float>(B_QS), c->p<int8_t>(B_KC), c->p<float>(B_KS), s));
+    const int s_pad = (S + 15) & ~15;
+    if (c->attn_fp8)
+      QI_LAUNCH(QI_PROF_SAGE_QUANT, 6,
+                sage_quantize_fp8pv_launch(qkvh, qkvh + hs, qkvh + 2 * hs, BH, S, c->p<float>(B_KMEAN),
+                                           c->p<int8_t>(B_QC), c->p<float>(B_QS), c->p<int8_t>(B_KC),
+                                           c->p<float>(B_KS), c->p<uint8_t>(B_V8), s_pad, c->p<float>(B_VAMAX),
+                                           c->p<float>(B_VS), s));
+    else
+      QI_LAUNCH(QI_PROF_SAGE_QUANT, 3,
+                sage_quantize_launch(qkvh, qkvh + hs, BH, S, c->p<float>(B_KMEAN), c->p<int8_t>(B_QC),
+                                     c->p<float>(B_QS), c->p<int8_t>(B_KC), c->p<float>(B_KS), s));
     AttnArgs aa{c->p<int8_t>(B_QC), c->p<float>(B_QS), c->p<int8_t>(B_KC), c->p<float>(B_KS), qkvh + 2 * hs,
                 par && !direct ? c->buf[B_SEND2] : c->buf[B_O], BH, S, f.Hl, 1.0f / sqrtf(128.0f),
                 direct ? 3 : (par ? 2 : 1), nb, n_img, n_txt, f.map};
     if (direct) {
       for (int q = 0; q < f.P; ++q) aa.peer_o[q] = c->peers.o[q];
       aa.head_base = f.rank * f.Hl;
+    }
+    if (c->attn_fp8) {
+      aa.v = c->buf[B_V8];
+      aa.fp8 = 1;
+      aa.vs = c->p<float>(B_VS);
+      aa.s_pad = s_pad;
     }
     QI_LAUNCH(QI_PROF_ATTENTION, 1, attention_launch(aa, s, c->err));
     if (direct) {  // every rank has stored its heads of this rank's rows

@@ -22,6 +22,11 @@
 #include "qi_internal.h"
 #include "sm100.cuh"
 
+// Smallest K that runs on CTA pairs (a build-time knob for measurements).
+#ifndef QI_GEMM_PAIR_MIN_K
+#define QI_GEMM_PAIR_MIN_K 0
+#endif
+
 namespace qi {
 
 namespace gemm {
@@ -81,18 +86,19 @@ template <bool BF16>
 __device__ __forceinline__ bool epilogue_tile(const GemmArgsDev& args, const GemmProblemDev& P, int row0, int n0,
                                               int buf, uint32_t acc_phase, uint32_t tmem_base, uint8_t* ebuf,
                                               uint64_t* xb, uint64_t* tfull, EpiState& es, volatile int* abort_flag,
-                                              int quarter, int lane) {
+                                              int quarter, int lane, int c_begin, int c_limit) {
   using namespace gemm;
   constexpr int NCH = BN / 32;
   const int r0 = row0 + quarter * 32;  // first output row of this warp
   const bool resid = args.epi == kEpiResidual;
-  const int nch = min(NCH, (P.N - n0 + 31) / 32);
-  // residual: fetch chunk 0 before waiting for the accumulator
-  if (resid && r0 < P.M && lane == 0) {
+  // this warp's 32-column chunks of the tile: [c_begin, nch)
+  const int nch = min(min(NCH, c_limit), (P.N - n0 + 31) / 32);
+  // residual: fetch the first chunk before waiting for the accumulator
+  if (resid && r0 < P.M && c_begin < nch && lane == 0) {
     bulk_wait_read<0>();
-    mbar_expect_tx(&xb[0], EPI_BUF);
-    tma_load_2d(ebuf, &P.tmO, n0, r0, &xb[0]);
-    es.xpending |= 1u;
+    mbar_expect_tx(&xb[c_begin & 1], EPI_BUF);
+    tma_load_2d(ebuf + (c_begin & 1) * EPI_BUF, &P.tmO, n0 + 32 * c_begin, r0, &xb[c_begin & 1]);
+    es.xpending |= 1u << (c_begin & 1);
   }
   bool w = mbar_wait(&tfull[buf], acc_phase, abort_flag);
   if (!__all_sync(0xffffffffu, w)) return false;
@@ -178,10 +184,11 @@ __device__ __forceinline__ bool epilogue_tile(const GemmArgsDev& args, const Gem
   };
   // TMEM loads run one chunk ahead of the dequant: chunk c + 1 is in flight
   // while chunk c is computed (two register buffers, unrolled by two).
+  if (c_begin >= nch) return true;
   uint32_t acc0[32], acc1[32];
-  tmem_ld32(taddr_row, acc0);
+  tmem_ld32(taddr_row + c_begin * 32, acc0);
 #pragma unroll 1
-  for (int c = 0; c < nch; c += 2) {
+  for (int c = c_begin; c < nch; c += 2) {
     tmem_ld_wait();
     tmem_reg_fence32(acc0);
     if (c + 1 < nch) tmem_ld32(taddr_row + (c + 1) * 32, acc1);
@@ -399,7 +406,7 @@ __global__ void __launch_bounds__(gemm::THREADS, 1) gemm_kernel(const __grid_con
       locate(t, pi, m0, n0);
       const int buf = local & 1;
       ok = epilogue_tile<BF16>(args, args.p[pi], m0, n0, buf, (local >> 1) & 1, tmem_base, ebuf, xb, tfull, es,
-                               abort_flag, quarter, lane);
+                               abort_flag, quarter, lane, 0, BN / 32);
       if (!ok) break;
       tc_fence_before();
       __syncwarp();
@@ -431,15 +438,22 @@ __global__ void __launch_bounds__(gemm::THREADS, 1) gemm_kernel(const __grid_con
 // block instead of 16 + 32).  Both CTAs run the producer and the epilogue;
 // stage and accumulator hand-offs use multicast commits (to both CTAs) and
 // remote arrivals on the even CTA's barriers.
+// The shared memory the smaller B slice frees holds staging for eight
+// epilogue warps: two per TMEM lane quarter, each owning half of the tile's
+// 256 columns, so a tile's epilogue takes about half as long as with four
+// and stays shorter than its main loop.
 namespace gemm2 {
-constexpr int BM = 256, BN = 256, BK = 128, STAGES = 6;
+constexpr int BM = 256, BN = 256, BK = 128, STAGES = 5;
 constexpr int A_BYTES = 128 * BK;                // this CTA's 128 rows of A: 16 KB
 constexpr int B_BYTES = 128 * BK;                // this CTA's half of B: 16 KB
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;   // 32 KB per CTA, 64 KB per pair
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + gemm::EPI_BYTES + 1024 + 256;
+constexpr int EPI_WARPS = 8;
+constexpr int THREADS = 64 + 32 * EPI_WARPS;     // producer, MMA issuer, 8 epilogue warps
+constexpr int EPI_BYTES = EPI_WARPS * 2 * gemm::EPI_BUF;  // double buffered per warp: 64 KB
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + EPI_BYTES + 1024 + 256;
 }  // namespace gemm2
 
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(gemm::THREADS, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(gemm2::THREADS, 1)
     gemm_pair_kernel(const __grid_constant__ GemmArgsDev args) {
   using gemm2::A_BYTES;
   using gemm2::B_BYTES;
@@ -454,12 +468,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(gemm::THREADS, 1)
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * A_BYTES;
   uint8_t* sE = smem + STAGES * STAGE_BYTES;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sE + gemm::EPI_BYTES);  // used in the even CTA
+  uint64_t* full = reinterpret_cast<uint64_t*>(sE + gemm2::EPI_BYTES);  // used in the even CTA
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
-  uint64_t* tempty = tfull + 2;  // used in the even CTA: 4 epilogue warps x 2 CTAs
+  uint64_t* tempty = tfull + 2;  // used in the even CTA: 8 epilogue warps x 2 CTAs
   uint64_t* xfull = tempty + 2;
-  uint64_t* drain = xfull + 2 * gemm::EPI_WARPS;
+  uint64_t* drain = xfull + 2 * gemm2::EPI_WARPS;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -476,9 +490,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(gemm::THREADS, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], 2 * gemm::EPI_WARPS);
+      mbar_init(&tempty[b], 2 * gemm2::EPI_WARPS);
     }
-    for (int b = 0; b < 2 * gemm::EPI_WARPS; ++b) mbar_init(&xfull[b], 1);
+    for (int b = 0; b < 2 * gemm2::EPI_WARPS; ++b) mbar_init(&xfull[b], 1);
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -605,6 +619,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(gemm::THREADS, 1)
     // ------------------------------------------------------------ epilogue (both CTAs)
     const int quarter = warp & 3;
     const int ew = warp - 2;
+    const int half = ew >> 2;  // columns 128 * half .. + 127 of each tile
     uint8_t* ebuf = sE + ew * 2 * gemm::EPI_BUF;
     uint64_t* xb = xfull + ew * 2;
     const uint32_t tempty0 = mapa_shared(&tempty[0], 0);
@@ -616,7 +631,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(gemm::THREADS, 1)
       locate(t, pi, m0, n0);
       const int buf = local & 1;
       ok = epilogue_tile<false>(args, args.p[pi], m0 + 128 * static_cast<int>(cr), n0, buf, (local >> 1) & 1,
-                                tmem_base, ebuf, xb, tfull, es, abort_flag, quarter, lane);
+                                tmem_base, ebuf, xb, tfull, es, abort_flag, quarter, lane, 4 * half, 4 * half + 4);
       if (!ok) break;
       tc_fence_before();
       __syncwarp();
@@ -693,7 +708,7 @@ static int launch_pair(GemmArgsDev& args, cudaStream_t stream, int num_sms) {
   if (smem_optin(reinterpret_cast<const void*>(gemm_pair_kernel), gemm2::SMEM_BYTES, &attr_done) != QI_OK)
     return QI_ERR_CUDA;
   const int clusters = args.total_tiles < num_sms / 2 ? args.total_tiles : num_sms / 2;
-  gemm_pair_kernel<<<2 * clusters, gemm::THREADS, gemm2::SMEM_BYTES, stream>>>(args);
+  gemm_pair_kernel<<<2 * clusters, gemm2::THREADS, gemm2::SMEM_BYTES, stream>>>(args);
   return cudaGetLastError() == cudaSuccess ? QI_OK : QI_ERR_CUDA;
 }
 
@@ -702,17 +717,15 @@ int gemm_i8_launch(const GemmDesc* descs, int n, int epi, cudaStream_t stream, i
   GemmArgsDev args;
   memset(&args, 0, sizeof(args));
   int tiles = 0;
-  // CTA pairs (256-row tiles) for long-K layers with enough rows to fill
-  // them: measured on B200, they speed up the K = 12288 fc2 GEMM by ~15 %,
-  // while the K = 3072 layers are limited by their epilogue, not by operand
-  // reads, and do not gain
+  // CTA pairs (256-row tiles, eight epilogue warps) whenever there are rows
+  // enough to fill them; the one-CTA kernel for short problems
   long long rows = 0;
   int kmin = 1 << 30;
   for (int i = 0; i < n; ++i) {
     rows += descs[i].M;
     if (descs[i].M > 0 && descs[i].K < kmin) kmin = descs[i].K;
   }
-  const bool pair = rows >= 512 && kmin >= 8192 && num_sms >= 2;
+  const bool pair = rows >= 512 && kmin >= QI_GEMM_PAIR_MIN_K && num_sms >= 2;
   const int bm = pair ? gemm2::BM : gemm::BM;
   for (int i = 0; i < n; ++i) {
     const GemmDesc& d = descs[i];

@@ -200,8 +200,22 @@ struct AttnArgs {
   // memory), columns (head_base + head) * 128
   void* peer_o[kMaxRanks];
   int head_base;
+  // FP8 P.V variant: v is then the E4M3 V^T codes [BH][128][s_pad] (token
+  // stride s_pad, a multiple of 16) and vs the per (batch-head, dim) output
+  // factors v_scale / 448
+  int fp8;
+  const float* vs;
+  int s_pad;
 };
 int attention_launch(const AttnArgs& a, cudaStream_t stream, int* err_dev);
+// Per-block Q / K INT8 (one scale per 128 queries / 64 keys, after K mean
+// smoothing), written in the per-thread scale layout the attention kernel
+// reads (every entry of a block the same), and V as E4M3 codes of
+// V / v_scale transposed to [BH][128][s_pad] with v_scale = max |V| / 448 per
+// (batch-head, dim); vs receives v_scale / 448.  vamax is [BH][128] scratch.
+int sage_quantize_fp8pv_launch(const void* q, const void* k, const void* v, int BH, int S, float* kmean, int8_t* qc,
+                               float* qs, int8_t* kc, float* ks, uint8_t* vt, int s_pad, float* vamax, float* vs,
+                               cudaStream_t stream);
 
 int cfg_euler_launch(float* x, const void* cond, const void* uncond, float cfg, float sigma, float sigma_next, int H,
                      int W, void* x_bf16, cudaStream_t stream);

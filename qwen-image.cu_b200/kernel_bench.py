@@ -82,6 +82,10 @@ def bench_attn(iters, res, config):
     res["sage_quant"] = {"BH": BH, "S": S, "ms": round(ms_q, 4)}
     res["attention_incl_quant"] = {"BH": BH, "S": S, "ms": round(ms, 4),
                                    "tflops": round(flops / ((ms - ms_q) * 1e-3) / 1e12, 1)}
+    # the FP8 P.V variant (its quantizers included; per-block Q/K, E4M3 V^T)
+    ms8 = time_it(lambda: Q.sage_attention_fp8pv(q, k, v), iters)
+    res["attention_fp8pv_incl_quant"] = {"BH": BH, "S": S, "ms": round(ms8, 4),
+                                         "tflops_incl_quant": round(flops / (ms8 * 1e-3) / 1e12, 1)}
 
 
 def bench_quant(iters, res):

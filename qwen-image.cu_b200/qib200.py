@@ -81,6 +81,7 @@ def lib():
             "qi_linear_i8_f32in_noalloc_selftest": ([i, vp], i),
             "qi_alloc_count": ([], ll),
             "qi_sage_attention": ([vp, vp, vp, vp, f, i, i, i, vp], i),
+            "qi_sage_attention_fp8pv": ([vp, vp, vp, vp, f, i, i, i, vp], i),
             "qi_sage_quantize": ([vp, vp, i, i, vp, vp, vp, vp, vp, vp], i),
             "qi_layer_norm_modulate": ([vp, vp, vp, vp, i, i, f, vp], i),
             "qi_rms_norm": ([vp, vp, vp, i, i, f, vp], i),
@@ -103,6 +104,7 @@ def lib():
             "qi_comm_unique_id": ([vp], i),
             "qi_ctx_set_comm": ([vp, vp, i, i], i),
             "qi_ctx_set_comm_timeout": ([vp, i], i),
+            "qi_ctx_set_attention_fp8pv": ([vp, i], i),
             "qi_ctx_sync": ([vp, vp, i], i),
             "qi_exchange_plan": ([i, i, i, i, i, i, vp, vp, vp, vp], i),
             "qi_rope_table": ([i, i, i, vp], i),
@@ -185,6 +187,13 @@ def sage_attention(q, k, v, scale=1.0 / np.sqrt(128.0)):
     BH, S, D = q.shape
     out = torch.empty(BH, S, D, dtype=torch.float32, device=q.device)
     check(lib().qi_sage_attention(_p(q), _p(k), _p(v), _p(out), float(scale), BH, S, D, _stream()))
+    return out
+
+
+def sage_attention_fp8pv(q, k, v, scale=1.0 / np.sqrt(128.0)):
+    BH, S, D = q.shape
+    out = torch.empty(BH, S, D, dtype=torch.float32, device=q.device)
+    check(lib().qi_sage_attention_fp8pv(_p(q), _p(k), _p(v), _p(out), float(scale), BH, S, D, _stream()))
     return out
 
 

@@ -1,4 +1,5 @@
-"""Head-parallel (Ulysses) forward on 2 GPUs against the single-GPU forward.
+"""Head-parallel (Ulysses) forward on 2, 4 and 8 GPUs (12, 6 and 3 heads per
+GPU) against the single-GPU forward.
 
 Every per-token computation (linears, norms, quantizers) and every per-head
 computation (K mean, Sage quantization, attention over the full joint
@@ -62,7 +63,8 @@ def _worker(rank, P, H, W, n_txt, nb, blocks, exchange, uid_q, out_q):
 
 
 @pytest.mark.parametrize("exchange", ["peer", "nccl"])
-@pytest.mark.parametrize("P,H,W,n_txt,nb", [(2, 66, 66, 77, 1), (2, 32, 48, 30, 2), (4, 66, 66, 77, 2)])
+@pytest.mark.parametrize("P,H,W,n_txt,nb", [(2, 66, 66, 77, 1), (2, 32, 48, 30, 2), (4, 66, 66, 77, 2),
+                                             (8, 64, 64, 64, 1), (8, 66, 70, 37, 2)])
 def test_head_parallel_forward_equals_single_gpu(P, H, W, n_txt, nb, exchange):
     if _gpus() < P:
         pytest.skip(f"needs {P} GPUs")
