@@ -42,13 +42,13 @@ namespace qi {
 
 namespace attn {
 constexpr int BQ = 128, BKV = 128, D = 128;
-constexpr int NT = 2;                 // query tiles per CTA
+constexpr int NT_MAX = 2;             // query tiles per CTA (the tail of a launch may use 1)
 constexpr int STAGES = 3;             // K/V ring depth
 constexpr int Q_BYTES = BQ * D;       // int8, one tile
 constexpr int K_BYTES = BKV * D;      // int8
 constexpr int V_BYTES = BKV * D * 2;  // fp16
 constexpr int OFF_Q = 0;
-constexpr int OFF_K = OFF_Q + NT * Q_BYTES;
+constexpr int OFF_K = OFF_Q + NT_MAX * Q_BYTES;
 constexpr int OFF_V = OFF_K + STAGES * K_BYTES;
 constexpr int OFF_BAR = OFF_V + STAGES * V_BYTES;
 constexpr int OFF_KS = OFF_BAR + 256;  // this batch-head's K scales (FP32), loaded once
@@ -62,9 +62,7 @@ constexpr int THREADS = 384;  // warpgroup 0: TMA warp, MMA warp, 2 idle; warpgr
 // the two softmax warpgroups take 208: 128 x 88 + 256 x 208 = 64512.
 constexpr int LAUNCH_REGS = 168, PRODUCER_REGS = 88, SOFTMAX_REGS = 208;
 static_assert(128 * PRODUCER_REGS + 256 * SOFTMAX_REGS <= THREADS * LAUNCH_REGS, "register split exceeds the launch");
-constexpr int TMEM_COLS = 512;
-constexpr int TM_S = 0;    // S / P of tile t at column 128 t
-constexpr int TM_O = 256;  // O of tile t at column 256 + 128 t
+constexpr int TM_S = 0;  // S / P of tile t at column 128 t; O of tile t at 128 (NT + t)
 }  // namespace attn
 
 struct alignas(64) AttnArgsDev {
@@ -79,6 +77,7 @@ struct alignas(64) AttnArgsDev {
   ShardMap map;
   void* peer_o[kMaxRanks];
   int head_base;
+  int q_tile0;  // first 128-query tile of this launch (the grid's x covers the tiles from there)
 };
 
 // Not volatile: a pure function of its input, so the compiler may schedule
@@ -164,9 +163,17 @@ __device__ __forceinline__ uint32_t pack_e4m3x4(float a, float b, float c, float
 // [dim][token], P is rescaled at every row-max increase (P <= 1), stored as
 // E4M3 codes of 448 P, and P.V runs as tcgen05.mma.kind::f8f6f4; the output
 // factor per dimension is v_scale / 448.
-template <bool FP8>
+//
+// NT = query tiles per CTA: 2 normally; 1 for the last, partial wave of a
+// launch (attention_launch), where one-tile CTAs spread the remaining tiles
+// over more SMs (warpgroup 2 then idles).  A query row's arithmetic is the
+// same either way.
+template <bool FP8, int NT>
 __global__ void __launch_bounds__(attn::THREADS, 1) sage_attn_kernel(const __grid_constant__ AttnArgsDev args) {
   using namespace attn;
+  static_assert(NT == 1 || NT == 2, "one or two query tiles per CTA");
+  constexpr int TMEM_COLS = 256 * NT;  // S and O of NT tiles
+  constexpr int TM_O = 128 * NT;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem + OFF_Q;
@@ -188,7 +195,7 @@ __global__ void __launch_bounds__(attn::THREADS, 1) sage_attn_kernel(const __gri
   volatile int* abort_flag = reinterpret_cast<volatile int*>(drain + 2);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int q0 = blockIdx.x * (NT * BQ);
+  const int q0 = (args.q_tile0 + static_cast<int>(blockIdx.x) * NT) * BQ;
   const int bh = blockIdx.y;
   const int S = args.S;
   const int nkb = (S + BKV - 1) / BKV;
@@ -357,6 +364,7 @@ __global__ void __launch_bounds__(attn::THREADS, 1) sage_attn_kernel(const __gri
     asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(SOFTMAX_REGS));
     // -------------------------------------------------------------- softmax
     const int t = (warp - 4) >> 2;
+    if (t < NT) {  // with one tile per CTA, warpgroup 2 has no tile
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;
     const int qrow = q0 + t * BQ + row;
@@ -599,6 +607,7 @@ __global__ void __launch_bounds__(attn::THREADS, 1) sage_attn_kernel(const __gri
         }
       }
     }
+    }  // t < NT
   }
 
   tc_fence_before();
@@ -1018,18 +1027,24 @@ int attention_launch(const AttnArgs& a, cudaStream_t stream, int* err_dev) {
   // registers per thread; with fewer, the softmax warpgroups' increase could
   // never be granted.  Refuse to launch rather than risk that.
   if (a.fp8 && (!a.vs || a.s_pad < a.S || a.s_pad % 16)) return QI_ERR_ARG;
-  const void* kfn = a.fp8 ? reinterpret_cast<const void*>(sage_attn_kernel<true>)
-                          : reinterpret_cast<const void*>(sage_attn_kernel<false>);
-  static int regs_checked[2] = {0, 0};
-  if (!regs_checked[a.fp8 ? 1 : 0]) {
-    cudaFuncAttributes fa;
-    if (cudaFuncGetAttributes(&fa, kfn) != cudaSuccess) return QI_ERR_CUDA;
-    if (fa.numRegs != attn::LAUNCH_REGS) return QI_ERR_UNSUPPORTED;
-    regs_checked[a.fp8 ? 1 : 0] = 1;
+  // the four instantiations: [fp8][tiles per CTA - 1]
+  const void* kfns[2][2] = {{reinterpret_cast<const void*>(sage_attn_kernel<false, 1>),
+                             reinterpret_cast<const void*>(sage_attn_kernel<false, 2>)},
+                            {reinterpret_cast<const void*>(sage_attn_kernel<true, 1>),
+                             reinterpret_cast<const void*>(sage_attn_kernel<true, 2>)}};
+  static int regs_checked[2][2] = {{0, 0}, {0, 0}};
+  static unsigned long long attr_done[2][2] = {{0, 0}, {0, 0}};
+  const int f8 = a.fp8 ? 1 : 0;
+  for (int nt = 0; nt < 2; ++nt) {
+    if (!regs_checked[f8][nt]) {
+      cudaFuncAttributes fa;
+      if (cudaFuncGetAttributes(&fa, kfns[f8][nt]) != cudaSuccess) return QI_ERR_CUDA;
+      if (fa.numRegs != attn::LAUNCH_REGS) return QI_ERR_UNSUPPORTED;
+      regs_checked[f8][nt] = 1;
+    }
+    if (smem_optin(kfns[f8][nt], attn::smem_bytes(((attn::MAX_S + 63) / 64) * 4), &attr_done[f8][nt]) != QI_OK)
+      return QI_ERR_CUDA;
   }
-  static unsigned long long attr_done[2] = {0, 0};
-  if (smem_optin(kfn, attn::smem_bytes(((attn::MAX_S + 63) / 64) * 4), &attr_done[a.fp8 ? 1 : 0]) != QI_OK)
-    return QI_ERR_CUDA;
   AttnArgsDev d;
   memset(&d, 0, sizeof(d));
   if (encode_3d(&d.tmQ, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a.qc, a.S, a.BH, 128) != QI_OK) return QI_ERR_CUDA;
@@ -1058,11 +1073,48 @@ int attention_launch(const AttnArgs& a, cudaStream_t stream, int* err_dev) {
   for (int i = 0; i < kMaxRanks; ++i) d.peer_o[i] = a.peer_o[i];
   d.head_base = a.head_base;
   if (a.out_mode >= 2 && (a.map.P < 1 || a.map.P > kMaxRanks)) return QI_ERR_ARG;
-  dim3 grid((a.S + attn::NT * attn::BQ - 1) / (attn::NT * attn::BQ), a.BH);
-  if (a.fp8)
-    sage_attn_kernel<true><<<grid, attn::THREADS, attn::smem_bytes(d.ngk), stream>>>(d);
-  else
-    sage_attn_kernel<false><<<grid, attn::THREADS, attn::smem_bytes(d.ngk), stream>>>(d);
+  // Two-tile CTAs (one per SM), except that in a launch of a few waves the
+  // last, partial wave is run as one-tile CTAs when that shortens it: x1
+  // two-tile CTAs per batch-head cover tiles [0, 2 x1), then one-tile CTAs
+  // the rest, if those fit in one wave and the estimate (a one-tile CTA takes
+  // ~0.55 of a two-tile one) beats the two-tile grid alone.  Measured at the
+  // C4 sequence on one B200: 6 heads (8-GPU share) 3.4 % and 12 heads 2 %
+  // faster; 48 heads (ten waves, whose sparse last wave runs uncontended)
+  // 3 % slower, hence the limit of four waves.  QI_ATTN_TAIL=0 turns the
+  // split off (measurements).
+  static int tail_split = -1;
+  if (tail_split < 0) {
+    const char* e = getenv("QI_ATTN_TAIL");
+    tail_split = (e && atoi(e) == 0) ? 0 : 1;
+  }
+  const int ntiles = (a.S + attn::BQ - 1) / attn::BQ;
+  const int pairs = (ntiles + 1) / 2;
+  const int sms = device_num_sms();
+  int x1 = pairs;
+  if (tail_split) {
+    const long long cover = static_cast<long long>(ntiles) * a.BH - sms;  // tiles the two-tile CTAs must take
+    const int x = cover <= 0 ? 0 : static_cast<int>((cover + 2LL * a.BH - 1) / (2LL * a.BH));
+    const long long waves = (static_cast<long long>(pairs) * a.BH + sms - 1) / sms;
+    if (x < pairs && waves <= 4) {
+      const long long waves1 = (static_cast<long long>(x) * a.BH + sms - 1) / sms;
+      if (waves1 * 100 + 55 < waves * 100) x1 = x;
+    }
+  }
+  auto launch = [&](int nt, int tile0, int nx) {
+    if (nx <= 0) return;
+    d.q_tile0 = tile0;
+    dim3 grid(nx, a.BH);
+    const size_t smem = attn::smem_bytes(d.ngk);
+    if (a.fp8) {
+      if (nt == 2) sage_attn_kernel<true, 2><<<grid, attn::THREADS, smem, stream>>>(d);
+      else sage_attn_kernel<true, 1><<<grid, attn::THREADS, smem, stream>>>(d);
+    } else {
+      if (nt == 2) sage_attn_kernel<false, 2><<<grid, attn::THREADS, smem, stream>>>(d);
+      else sage_attn_kernel<false, 1><<<grid, attn::THREADS, smem, stream>>>(d);
+    }
+  };
+  launch(2, 0, x1);
+  launch(1, 2 * x1, ntiles - 2 * x1);
   return cudaGetLastError() == cudaSuccess ? QI_OK : QI_ERR_CUDA;
 }
 

@@ -442,27 +442,40 @@ __global__ void __launch_bounds__(gemm::THREADS, 1) gemm_kernel(const __grid_con
 // epilogue warps: two per TMEM lane quarter, each owning half of the tile's
 // 256 columns, so a tile's epilogue takes about half as long as with four
 // and stays shorter than its main loop.
+//
+// Tile width BN = 256, or 128 where the 256-wide tiles leave most of a wave
+// idle (out and fc2 with few rows per rank): the narrower tiles use the same
+// per-element arithmetic, so the outputs are identical.
 namespace gemm2 {
-constexpr int BM = 256, BN = 256, BK = 128, STAGES = 5;
+constexpr int BM = 256, BK = 128;
 constexpr int A_BYTES = 128 * BK;                // this CTA's 128 rows of A: 16 KB
-constexpr int B_BYTES = 128 * BK;                // this CTA's half of B: 16 KB
-constexpr int STAGE_BYTES = A_BYTES + B_BYTES;   // 32 KB per CTA, 64 KB per pair
+template <int BN>
+constexpr int b_bytes() { return (BN / 2) * BK; }  // this CTA's half of B: 16 / 8 KB
+template <int BN>
+constexpr int stages() { return BN == 256 ? 5 : 6; }
+template <int BN>
+constexpr int stage_bytes() { return A_BYTES + b_bytes<BN>(); }
 constexpr int EPI_WARPS = 8;
 constexpr int THREADS = 64 + 32 * EPI_WARPS;     // producer, MMA issuer, 8 epilogue warps
 constexpr int EPI_BYTES = EPI_WARPS * 2 * gemm::EPI_BUF;  // double buffered per warp: 64 KB
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + EPI_BYTES + 1024 + 256;
+template <int BN>
+constexpr int smem_bytes() { return stages<BN>() * stage_bytes<BN>() + EPI_BYTES + 1024 + 256; }
+static_assert(smem_bytes<256>() <= 232448 && smem_bytes<128>() <= 232448, "shared memory per CTA");
+constexpr int TMEM_COLS = 512;  // two accumulator buffers, 256 columns apart (BN = 128 uses half of each)
 }  // namespace gemm2
 
+template <int BN>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(gemm2::THREADS, 1)
     gemm_pair_kernel(const __grid_constant__ GemmArgsDev args) {
+  static_assert(BN == 256 || BN == 128, "pair tile width");
   using gemm2::A_BYTES;
-  using gemm2::B_BYTES;
   using gemm2::BK;
   using gemm2::BM;
-  using gemm2::BN;
-  using gemm2::STAGE_BYTES;
-  using gemm2::STAGES;
-  constexpr int TMEM_COLS = 2 * BN;
+  using gemm2::TMEM_COLS;
+  constexpr int B_BYTES = gemm2::b_bytes<BN>();
+  constexpr int STAGE_BYTES = gemm2::stage_bytes<BN>();
+  constexpr int STAGES = gemm2::stages<BN>();
+  constexpr int TMEM_BUF = 256;  // column stride of the two accumulator buffers
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
@@ -540,7 +553,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(gemm2::THREADS, 1)
           if (leader) mbar_expect_tx(&full[stage], 2 * STAGE_BYTES);  // both CTAs' bytes
           const uint32_t fb = full0 + stage * 8;
           tma_load_2d_pair(sA + stage * A_BYTES, &P.tmA, kb * BK, m0 + 128 * static_cast<int>(cr), fb);
-          tma_load_2d_pair(sB + stage * B_BYTES, &P.tmB, kb * BK, n0 + 128 * static_cast<int>(cr), fb);
+          tma_load_2d_pair(sB + stage * B_BYTES, &P.tmB, kb * BK, n0 + (BN / 2) * static_cast<int>(cr), fb);
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1u;
@@ -583,7 +596,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(gemm2::THREADS, 1)
           break;
         }
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + buf * BN;
+        const uint32_t d_tmem = tmem_base + buf * TMEM_BUF;
         for (int kb = 0; kb < kblocks; ++kb) {
           if (!wait_all(&full[stage], phase)) {
             ok = false;
@@ -619,7 +632,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(gemm2::THREADS, 1)
     // ------------------------------------------------------------ epilogue (both CTAs)
     const int quarter = warp & 3;
     const int ew = warp - 2;
-    const int half = ew >> 2;  // columns 128 * half .. + 127 of each tile
+    const int half = ew >> 2;  // columns (BN / 2) * half .. of each tile
+    constexpr int HCH = BN / 64;  // 32-column chunks per half
     uint8_t* ebuf = sE + ew * 2 * gemm::EPI_BUF;
     uint64_t* xb = xfull + ew * 2;
     const uint32_t tempty0 = mapa_shared(&tempty[0], 0);
@@ -631,7 +645,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(gemm2::THREADS, 1)
       locate(t, pi, m0, n0);
       const int buf = local & 1;
       ok = epilogue_tile<false>(args, args.p[pi], m0 + 128 * static_cast<int>(cr), n0, buf, (local >> 1) & 1,
-                                tmem_base, ebuf, xb, tfull, es, abort_flag, quarter, lane, 4 * half, 4 * half + 4);
+                                tmem_base, ebuf, xb, tfull, es, abort_flag, quarter, lane, HCH * half,
+                                HCH * half + HCH);
       if (!ok) break;
       tc_fence_before();
       __syncwarp();
@@ -691,25 +706,54 @@ static int launch_args(GemmArgsDev& args, cudaStream_t stream, int num_sms) {
   return cudaGetLastError() == cudaSuccess ? QI_OK : QI_ERR_CUDA;
 }
 
-static void fill_problem(GemmProblemDev& P, int M, int N, int K, int ldo, int& tiles, int bm = gemm::BM) {
+static void fill_problem(GemmProblemDev& P, int M, int N, int K, int ldo, int& tiles, int bm = gemm::BM,
+                         int bn = gemm::BN) {
   P.M = M;
   P.N = N;
   P.K = K;
   P.ldo = ldo;
-  P.tiles_n = (N + gemm::BN - 1) / gemm::BN;
+  P.tiles_n = (N + bn - 1) / bn;
   const int tm = (M + bm - 1) / bm;
   P.tile_begin = tiles;
   tiles += tm * P.tiles_n;
   P.tile_end = tiles;
 }
 
+template <int BN>
 static int launch_pair(GemmArgsDev& args, cudaStream_t stream, int num_sms) {
   static unsigned long long attr_done = 0;
-  if (smem_optin(reinterpret_cast<const void*>(gemm_pair_kernel), gemm2::SMEM_BYTES, &attr_done) != QI_OK)
+  if (smem_optin(reinterpret_cast<const void*>(gemm_pair_kernel<BN>), gemm2::smem_bytes<BN>(), &attr_done) != QI_OK)
     return QI_ERR_CUDA;
   const int clusters = args.total_tiles < num_sms / 2 ? args.total_tiles : num_sms / 2;
-  gemm_pair_kernel<<<2 * clusters, gemm2::THREADS, gemm2::SMEM_BYTES, stream>>>(args);
+  gemm_pair_kernel<BN><<<2 * clusters, gemm2::THREADS, gemm2::smem_bytes<BN>(), stream>>>(args);
   return cudaGetLastError() == cudaSuccess ? QI_OK : QI_ERR_CUDA;
+}
+
+// Pair tile width: 128 when the narrower tiles finish sooner on the SM pairs.
+// A 256 x 128 tile takes 0.62-0.68 of a 256 x 256 tile's time (measured at
+// the forward's shapes: per MAC it moves 1.5x the operand bytes through L2
+// and shared memory), so they win only where wide tiles leave one wave of
+// pairs mostly idle (few rows).  QI_GEMM_PAIR_BN=128 / 256 forces a width
+// (measurements).
+static int pair_tile_width(const GemmDesc* descs, int n, int clusters) {
+  static int forced = -1;
+  if (forced < 0) {
+    const char* e = getenv("QI_GEMM_PAIR_BN");
+    forced = e ? atoi(e) : 0;
+    if (forced != 128 && forced != 256) forced = 0;
+  }
+  if (forced) return forced;
+  long long wide = 0, narrow = 0;
+  for (int i = 0; i < n; ++i) {
+    if (descs[i].M <= 0) continue;
+    const long long tm = (descs[i].M + gemm2::BM - 1) / gemm2::BM;
+    wide += tm * ((descs[i].N + 255) / 256);
+    narrow += tm * ((descs[i].N + 127) / 128);
+  }
+  constexpr double kNarrowCost = 0.18;
+  const double t_wide = static_cast<double>((wide + clusters - 1) / clusters);
+  const double t_narrow = static_cast<double>((narrow + clusters - 1) / clusters) * (0.5 + kNarrowCost);
+  return t_narrow < t_wide ? 128 : 256;
 }
 
 int gemm_i8_launch(const GemmDesc* descs, int n, int epi, cudaStream_t stream, int* err_dev, int num_sms) {
@@ -727,6 +771,7 @@ int gemm_i8_launch(const GemmDesc* descs, int n, int epi, cudaStream_t stream, i
   }
   const bool pair = rows >= 512 && kmin >= QI_GEMM_PAIR_MIN_K && num_sms >= 2;
   const int bm = pair ? gemm2::BM : gemm::BM;
+  const int bn = pair ? pair_tile_width(descs, n, num_sms / 2) : gemm::BN;
   for (int i = 0; i < n; ++i) {
     const GemmDesc& d = descs[i];
     if (d.M < 0 || d.N <= 0 || d.K <= 0) return QI_ERR_ARG;
@@ -739,7 +784,7 @@ int gemm_i8_launch(const GemmDesc* descs, int n, int epi, cudaStream_t stream, i
     GemmProblemDev& P = args.p[i];
     if (d.M > 0) {
       if (encode_kmajor(&P.tmA, d.a, d.M, d.K, 128, false) != QI_OK) return QI_ERR_CUDA;
-      if (encode_kmajor(&P.tmB, d.w, d.N, d.K, pair ? 128 : gemm::BN, false) != QI_OK) return QI_ERR_CUDA;
+      if (encode_kmajor(&P.tmB, d.w, d.N, d.K, pair ? bn / 2 : gemm::BN, false) != QI_OK) return QI_ERR_CUDA;
       if (encode_out(&P.tmO, d.out, d.M, d.N, d.ldo) != QI_OK) return QI_ERR_CUDA;
     }
     P.sa = d.sa;
@@ -747,14 +792,15 @@ int gemm_i8_launch(const GemmDesc* descs, int n, int epi, cudaStream_t stream, i
     P.bias = reinterpret_cast<const __nv_bfloat16*>(d.bias);
     P.out = d.out;
     P.gate = d.gate;
-    fill_problem(P, d.M, d.N, d.K, d.ldo, tiles, bm);
+    fill_problem(P, d.M, d.N, d.K, d.ldo, tiles, bm, bn);
   }
   if (tiles == 0) return QI_OK;
   args.nprob = n;
   args.total_tiles = tiles;
   args.epi = epi;
   args.err = err_dev;
-  return pair ? launch_pair(args, stream, num_sms) : launch_args<false>(args, stream, num_sms);
+  if (!pair) return launch_args<false>(args, stream, num_sms);
+  return bn == 128 ? launch_pair<128>(args, stream, num_sms) : launch_pair<256>(args, stream, num_sms);
 }
 
 int gemm_bf16_launch(const GemmBf16Desc& d, cudaStream_t stream, int* err_dev, int num_sms) {

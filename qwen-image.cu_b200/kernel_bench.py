@@ -3,11 +3,14 @@ CUDA events on the launching stream).  Also the target of the ncu captures
 summarised in profiles/.
 
     python qwen-image.cu_b200/kernel_bench.py [--which gemm,attn,quant,peaks] [--iters N] [--config c4|c2]
+                                              [--gpus 1|2|4|8]
 
 GEMM shapes are those of one CFG-batched C4 forward (M = 2 x 6889 image +
 2 x 256 text tokens): fused QKV (N 9216), out-projection (N 3072), fc1
 (N 12288), fc2 (K 12288).  Attention: the Sage microbenchmark configuration
 (B 2, 24 heads, 4352 tokens) or the C4 joint sequence (7145 tokens).
+`--gpus N` times one rank's share of an N-GPU job instead: the CFG halves on
+separate ranks (batch 1) and 24 / (N / 2) heads, (6889 + 256) / (N / 2) rows.
 Quantizers: LayerNorm-modulate + FWHT-1024 (K 3072), the attention output
 (FP16, K 3072) and the MLP hidden (FWHT-4096, K 12288) at the C4 rows.
 `peaks`: the dense tensor-core rates of this GPU through the libraries
@@ -43,9 +46,16 @@ def time_it(fn, iters, warmup=3):
     return e0.elapsed_time(e1) / iters
 
 
-def bench_gemm(iters, res):
+def shard(n_gpus):
+    """(CFG batch nb, head-parallel degree P) of one rank in an n_gpus job:
+    1 GPU runs both CFG halves batched; more split CFG, then heads."""
+    return (2, 1) if n_gpus == 1 else (1, n_gpus // 2)
+
+
+def bench_gemm(iters, res, n_gpus=1):
+    nb, P = shard(n_gpus)
     for name, (N, K) in GEMMS.items():
-        M = M_IMG + M_TXT
+        M = nb * ((M_IMG // 2 + P - 1) // P + (M_TXT // 2 + P - 1) // P)
         a = torch.randint(-127, 128, (M, K), dtype=torch.int8, device="cuda")
         w = torch.randint(-127, 128, (N, K), dtype=torch.int8, device="cuda")
         sa = torch.rand(M, device="cuda") * 1e-3
@@ -69,9 +79,10 @@ def bench_gemm(iters, res):
         del a, w, out
 
 
-def bench_attn(iters, res, config):
-    B, S = (2, 4352) if config == "c2" else (2, 7145)
-    BH = B * 24
+def bench_attn(iters, res, config, n_gpus=1):
+    nb, P = shard(n_gpus)
+    S = 4352 if config == "c2" else 7145
+    BH = nb * 24 // P
     q = Q.synth((BH, S, 128), 1, 1.0).half()
     k = Q.synth((BH, S, 128), 2, 1.0).half()
     v = Q.synth((BH, S, 128), 3, 1.0).half()
@@ -137,14 +148,16 @@ def main():
     ap.add_argument("--which", default="gemm,attn,quant")
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--config", default="c2")
+    ap.add_argument("--gpus", type=int, default=1, choices=(1, 2, 4, 8),
+                    help="time one rank's share of an N-GPU job (CFG split, then head-parallel)")
     a = ap.parse_args()
     torch.cuda.set_device(0)
-    res = {}
+    res = {"gpus": a.gpus}
     w = a.which.split(",")
     if "gemm" in w:
-        bench_gemm(a.iters, res)
+        bench_gemm(a.iters, res, a.gpus)
     if "attn" in w:
-        bench_attn(a.iters, res, a.config)
+        bench_attn(a.iters, res, a.config, a.gpus)
     if "quant" in w:
         bench_quant(a.iters, res)
     if "peaks" in w:
