@@ -77,14 +77,58 @@ def flops_per_forward(n_img, n_txt, blocks=BLOCKS):
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons, sampled every 200 ms."""
+    """SM clocks and clock-event (throttle) reasons of this rank's GPU, sampled
+    every 10 ms through NVML on a host thread while the timed region runs
+    (read-only: nothing is set).  The device is found by UUID, so the index
+    under CUDA_VISIBLE_DEVICES does not matter.  Falls back to `nvidia-smi -lms
+    200` if NVML is unavailable."""
 
-    def __init__(self, index):
+    NAMES = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+
+    def __init__(self, index, period_s=0.01):
         self.index = index
-        self.rows = []
+        self.period_s = period_s
+        self.rows = []  # (sm_mhz, max_mhz, set of reason names)
         self.proc = None
+        self.nvml = None
+        self.stop = threading.Event()
+
+    def _nvml_handle(self):
+        import pynvml
+        pynvml.nvmlInit()
+        try:
+            uuid = str(torch.cuda.get_device_properties(self.index).uuid)
+            return pynvml, pynvml.nvmlDeviceGetHandleByUUID(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
+        except Exception:
+            return pynvml, pynvml.nvmlDeviceGetHandleByIndex(self.index)
+
+    def _nvml_sample(self):
+        nv, h = self.nvml
+        sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+        mx = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+        bits = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+        masks = (nv.nvmlClocksEventReasonHwSlowdown, nv.nvmlClocksEventReasonHwThermalSlowdown,
+                 nv.nvmlClocksEventReasonSwThermalSlowdown, nv.nvmlClocksEventReasonSwPowerCap)
+        self.rows.append((float(sm), float(mx), {n for n, m in zip(self.NAMES, masks) if bits & m}))
+
+    def _nvml_loop(self):
+        while not self.stop.is_set():
+            try:
+                self._nvml_sample()
+            except Exception:
+                return
+            self.stop.wait(self.period_s)
 
     def __enter__(self):
+        try:
+            self.nvml = self._nvml_handle()
+            self._nvml_sample()  # fails here, not silently in the thread, if NVML cannot read this GPU
+            self.rows.clear()
+            self.thread = threading.Thread(target=self._nvml_loop, daemon=True)
+            self.thread.start()
+            return self
+        except Exception:
+            self.nvml = None
         q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
@@ -92,17 +136,25 @@ class ClockSampler:
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={q}",
                                           "--format=csv,noheader,nounits", "-lms", "200"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread = threading.Thread(target=self._smi_read, daemon=True)
             self.thread.start()
         except Exception:
             self.proc = None
         return self
 
-    def _read(self):
+    def _smi_read(self):
         for line in self.proc.stdout:
-            self.rows.append([v.strip() for v in line.split(",")])
+            r = [v.strip() for v in line.split(",")]
+            try:
+                self.rows.append((float(r[1]), float(r[2]),
+                                  {n for n, v in zip(self.NAMES, r[5:9]) if v.lower().startswith("active")}))
+            except (ValueError, IndexError):
+                continue
 
     def __exit__(self, *a):
+        if self.nvml:
+            self.stop.set()
+            self.thread.join(timeout=1.0)
         if self.proc:
             self.proc.terminate()
             try:
@@ -111,19 +163,11 @@ class ClockSampler:
                 self.proc.kill()
 
     def summary(self):
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for r in self.rows:
-            try:
-                sm.append(float(r[1]))
-                mx = float(r[2])
-                for n, v in zip(names, r[5:9]):
-                    if v.lower().startswith("active"):
-                        reasons.add(n)
-            except (ValueError, IndexError):
-                continue
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+        sm = [r[0] for r in self.rows]
+        reasons = set().union(*[r[2] for r in self.rows]) if self.rows else set()
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": self.rows[-1][1] if self.rows else None, "reasons": sorted(reasons),
+                "samples": len(sm), "source": "nvml" if self.nvml else "nvidia-smi"}
 
 
 def measured_peaks():

@@ -70,11 +70,23 @@ __device__ __forceinline__ uint32_t codes4_ref(float x0, float x1, float x2, flo
 // 127 / max): adding 1.5 * 2^23 rounds x to the nearest integer, ties to even
 // (the rounding of __float2int_rn), and leaves it in the low mantissa bits in
 // two's complement; no value reaches the clamp.  x must be the rounded
-// product (no fused multiply-add into the addition).
-__device__ __forceinline__ uint32_t codes4_fast(float x0, float x1, float x2, float x3) {
-  const int t0 = __float_as_int(__fadd_rn(x0, 12582912.0f)), t1 = __float_as_int(__fadd_rn(x1, 12582912.0f));
-  const int t2 = __float_as_int(__fadd_rn(x2, 12582912.0f)), t3 = __float_as_int(__fadd_rn(x3, 12582912.0f));
-  return __byte_perm(__byte_perm(t0, t1, 0x0040), __byte_perm(t2, t3, 0x0040), 0x5410);
+// product v * inv: the scalar __fmul_rn / __fadd_rn are never contracted into
+// a fused multiply-add.  (Two-wide FP32 multiply and add were measured to
+// differ here on exact ties, so this step stays scalar.)  Here for J float4s
+// held as FP32 pairs, stored to dst[32 j].
+template <int J>
+__device__ __forceinline__ void dst_codes_fast(const uint64_t (&w)[J][2], float inv, uint32_t* dst) {
+#pragma unroll
+  for (int j = 0; j < J; ++j) {
+    float x0, x1, x2, x3;
+    f2unpack(w[j][0], x0, x1);
+    f2unpack(w[j][1], x2, x3);
+    const int t0 = __float_as_int(__fadd_rn(__fmul_rn(x0, inv), 12582912.0f));
+    const int t1 = __float_as_int(__fadd_rn(__fmul_rn(x1, inv), 12582912.0f));
+    const int t2 = __float_as_int(__fadd_rn(__fmul_rn(x2, inv), 12582912.0f));
+    const int t3 = __float_as_int(__fadd_rn(__fmul_rn(x3, inv), 12582912.0f));
+    dst[32 * j] = __byte_perm(__byte_perm(t0, t1, 0x0040), __byte_perm(t2, t3, 0x0040), 0x5410);
+  }
 }
 
 // Sum over the 1024 threads of a reference reduction block in the order of
@@ -142,7 +154,8 @@ __global__ void __launch_bounds__(NW * 32) rowquant_warp_kernel(RowSegs segs, in
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int base = warp * CH + 4 * lane;
 
-  float v[J][4];
+  // float4 j of this lane as two FP32 pairs: w[j][0] = (x0, x1), w[j][1] = (x2, x3)
+  uint64_t w[J][2];
   if (SRC == kSrcF16) {
     const __half* src = reinterpret_cast<const __half*>(in) + static_cast<long long>(local) * ld + base;
 #pragma unroll
@@ -150,20 +163,16 @@ __global__ void __launch_bounds__(NW * 32) rowquant_warp_kernel(RowSegs segs, in
       const uint2 raw = *reinterpret_cast<const uint2*>(src + 128 * j);
       const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
       const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
-      v[j][0] = a.x;
-      v[j][1] = a.y;
-      v[j][2] = b.x;
-      v[j][3] = b.y;
+      w[j][0] = f2pack(a.x, a.y);
+      w[j][1] = f2pack(b.x, b.y);
     }
   } else {
     const float* src = reinterpret_cast<const float*>(in) + static_cast<long long>(local) * ld + base;
 #pragma unroll
     for (int j = 0; j < J; ++j) {
-      const float4 f = *reinterpret_cast<const float4*>(src + 128 * j);
-      v[j][0] = f.x;
-      v[j][1] = f.y;
-      v[j][2] = f.z;
-      v[j][3] = f.w;
+      const ulonglong2 u = *reinterpret_cast<const ulonglong2*>(src + 128 * j);
+      w[j][0] = u.x;
+      w[j][1] = u.y;
     }
   }
 
@@ -182,40 +191,39 @@ __global__ void __launch_bounds__(NW * 32) rowquant_warp_kernel(RowSegs segs, in
 #pragma unroll
     for (int j = 0; j < J; ++j) {
       const int t = 128 * j + 4 * lane;
-      *reinterpret_cast<float4*>(&xs[warp][t + 4 * (t >> 5)]) = make_float4(v[j][0], v[j][1], v[j][2], v[j][3]);
+      *reinterpret_cast<ulonglong2*>(&xs[warp][t + 4 * (t >> 5)]) = make_ulonglong2(w[j][0], w[j][1]);
     }
     __syncthreads();
     if (warp == 0) {
       const int a0 = 36 * lane;  // padded offset of thread 32 * lane
       // thread partials of threads 32 * lane + 4q .. + 3, in the reference's
       // per-thread order: sum += x[t]; sum += x[t + 1024]; sum += x[t + 2048]
+      // (components two at a time)
       auto sum_part = [&](int q, float (&o)[4]) {
-        const float4 f0 = *reinterpret_cast<const float4*>(&xs[0][a0 + 4 * q]);
-        const float4 f1 = *reinterpret_cast<const float4*>(&xs[1][a0 + 4 * q]);
-        const float4 f2 = *reinterpret_cast<const float4*>(&xs[2][a0 + 4 * q]);
-        o[0] = (f0.x + f1.x) + f2.x;
-        o[1] = (f0.y + f1.y) + f2.y;
-        o[2] = (f0.z + f1.z) + f2.z;
-        o[3] = (f0.w + f1.w) + f2.w;
+        const ulonglong2 f0 = *reinterpret_cast<const ulonglong2*>(&xs[0][a0 + 4 * q]);
+        const ulonglong2 f1 = *reinterpret_cast<const ulonglong2*>(&xs[1][a0 + 4 * q]);
+        const ulonglong2 f2 = *reinterpret_cast<const ulonglong2*>(&xs[2][a0 + 4 * q]);
+        f2unpack(f2add(f2add(f0.x, f1.x), f2.x), o[0], o[1]);
+        f2unpack(f2add(f2add(f0.y, f1.y), f2.y), o[2], o[3]);
       };
       const float mean = ref_block_tree(sum_part) / dim;
-      // var_sum += v * v over the same elements, v = x - mean
+      const uint64_t mean2 = f2pack(mean, mean);
+      // var_sum += v * v over the same elements, v = x - mean (the first
+      // product's += onto 0 is the product itself)
       auto var_part = [&](int q, float (&o)[4]) {
-        const float4 f0 = *reinterpret_cast<const float4*>(&xs[0][a0 + 4 * q]);
-        const float4 f1 = *reinterpret_cast<const float4*>(&xs[1][a0 + 4 * q]);
-        const float4 f2 = *reinterpret_cast<const float4*>(&xs[2][a0 + 4 * q]);
-        const float x0[4] = {f0.x, f0.y, f0.z, f0.w}, x1[4] = {f1.x, f1.y, f1.z, f1.w},
-                    x2[4] = {f2.x, f2.y, f2.z, f2.w};
+        const ulonglong2 f0 = *reinterpret_cast<const ulonglong2*>(&xs[0][a0 + 4 * q]);
+        const ulonglong2 f1 = *reinterpret_cast<const ulonglong2*>(&xs[1][a0 + 4 * q]);
+        const ulonglong2 f2 = *reinterpret_cast<const ulonglong2*>(&xs[2][a0 + 4 * q]);
+        const uint64_t x0[2] = {f0.x, f0.y}, x1[2] = {f1.x, f1.y}, x2[2] = {f2.x, f2.y};
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          float var_sum = 0.0f;
-          float d = x0[e] - mean;
-          var_sum += d * d;
-          d = x1[e] - mean;
-          var_sum += d * d;
-          d = x2[e] - mean;
-          var_sum += d * d;
-          o[e] = var_sum;
+        for (int k = 0; k < 2; ++k) {
+          uint64_t d = f2sub(x0[k], mean2);
+          uint64_t var_sum = f2mul(d, d);
+          d = f2sub(x1[k], mean2);
+          var_sum = f2fma(d, d, var_sum);
+          d = f2sub(x2[k], mean2);
+          var_sum = f2fma(d, d, var_sum);
+          f2unpack(var_sum, o[2 * k], o[2 * k + 1]);
         }
       };
       const float inv_std = rsqrtf(ref_block_tree(var_part) / dim + eps);
@@ -227,48 +235,38 @@ __global__ void __launch_bounds__(NW * 32) rowquant_warp_kernel(RowSegs segs, in
     __syncthreads();
     const float mean = red[0][0];
     const float inv_std = red[1][0];
+    const uint64_t mean2 = f2pack(mean, mean), istd2 = f2pack(inv_std, inv_std), one2 = f2pack(1.0f, 1.0f);
     // this warp's chunk back from shared memory (not held in registers
-    // across the statistics)
+    // across the statistics); (x - mean) * inv_std * (1 + scale) + shift with
+    // the last multiply-add fused, as the reference build contracts it
 #pragma unroll
     for (int j = 0; j < J; ++j) {
       const int t = 128 * j + 4 * lane;
-      const float4 f = *reinterpret_cast<const float4*>(&xs[warp][t + 4 * (t >> 5)]);
-      const float4 sc = __ldg(reinterpret_cast<const float4*>(scale + base + 128 * j));
-      const float4 sh = __ldg(reinterpret_cast<const float4*>(shift + base + 128 * j));
-      v[j][0] = f.x;
-      v[j][1] = f.y;
-      v[j][2] = f.z;
-      v[j][3] = f.w;
-      v[j][0] = (v[j][0] - mean) * inv_std * (1.0f + sc.x) + sh.x;
-      v[j][1] = (v[j][1] - mean) * inv_std * (1.0f + sc.y) + sh.y;
-      v[j][2] = (v[j][2] - mean) * inv_std * (1.0f + sc.z) + sh.z;
-      v[j][3] = (v[j][3] - mean) * inv_std * (1.0f + sc.w) + sh.w;
+      const ulonglong2 f = *reinterpret_cast<const ulonglong2*>(&xs[warp][t + 4 * (t >> 5)]);
+      const ulonglong2 sc = __ldg(reinterpret_cast<const ulonglong2*>(scale + base + 128 * j));
+      const ulonglong2 sh = __ldg(reinterpret_cast<const ulonglong2*>(shift + base + 128 * j));
+      w[j][0] = f2fma(f2mul(f2sub(f.x, mean2), istd2), f2add(one2, sc.x), sh.x);
+      w[j][1] = f2fma(f2mul(f2sub(f.y, mean2), istd2), f2add(one2, sc.y), sh.y);
     }
   }
 
-  // half = 1, 2: within the float4
+  // half = 1: inside each pair; half = 2: the two pairs side by side
   if (had_block > 1) {
 #pragma unroll
-    for (int j = 0; j < J; ++j) {
-      float a = v[j][0], b = v[j][1];
-      v[j][0] = a + b;
-      v[j][1] = a - b;
-      a = v[j][2];
-      b = v[j][3];
-      v[j][2] = a + b;
-      v[j][3] = a - b;
-    }
+    for (int j = 0; j < J; ++j)
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        float a, b;
+        f2unpack(w[j][k], a, b);
+        w[j][k] = f2pack(a + b, a - b);
+      }
   }
   if (had_block > 2) {
 #pragma unroll
     for (int j = 0; j < J; ++j) {
-      float a = v[j][0], b = v[j][2];
-      v[j][0] = a + b;
-      v[j][2] = a - b;
-      a = v[j][1];
-      b = v[j][3];
-      v[j][1] = a + b;
-      v[j][3] = a - b;
+      const uint64_t a = w[j][0], b = w[j][1];
+      w[j][0] = f2add(a, b);
+      w[j][1] = f2sub(a, b);
     }
   }
   // half = 4 .. 64: across lanes
@@ -276,13 +274,16 @@ __global__ void __launch_bounds__(NW * 32) rowquant_warp_kernel(RowSegs segs, in
   for (int m = 1; m < 32; m <<= 1) {
     if (4 * m >= had_block) break;
     const float sgn = (lane & m) ? -1.0f : 1.0f;
+    const uint64_t sgn2 = f2pack(sgn, sgn);
 #pragma unroll
     for (int j = 0; j < J; ++j)
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
+      for (int k = 0; k < 2; ++k) {
         // lower lane: a + b = v + p; upper lane: a - b = p - v; one rounding each
-        const float p = __shfl_xor_sync(0xffffffffu, v[j][e], m);
-        v[j][e] = fmaf(v[j][e], sgn, p);
+        float lo, hi;
+        f2unpack(w[j][k], lo, hi);
+        const float plo = __shfl_xor_sync(0xffffffffu, lo, m), phi = __shfl_xor_sync(0xffffffffu, hi, m);
+        w[j][k] = f2fma(w[j][k], sgn2, f2pack(plo, phi));
       }
   }
   // half = 128 ..: across registers
@@ -293,10 +294,10 @@ __global__ void __launch_bounds__(NW * 32) rowquant_warp_kernel(RowSegs segs, in
     for (int j = 0; j < J; ++j) {
       if (j & jm) continue;
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float a = v[j][e], b = v[j | jm][e];
-        v[j][e] = a + b;
-        v[j | jm][e] = a - b;
+      for (int k = 0; k < 2; ++k) {
+        const uint64_t a = w[j][k], b = w[j | jm][k];
+        w[j][k] = f2add(a, b);
+        w[j | jm][k] = f2sub(a, b);
       }
     }
   }
@@ -304,47 +305,57 @@ __global__ void __launch_bounds__(NW * 32) rowquant_warp_kernel(RowSegs segs, in
   float mx = 0.0f;
   if (had_block > 1) {
     const float norm = rsqrtf(static_cast<float>(had_block));
+    const uint64_t norm2 = f2pack(norm, norm);
 #pragma unroll
     for (int j = 0; j < J; ++j)
 #pragma unroll
-      for (int e = 0; e < 4; ++e) v[j][e] *= norm;
+      for (int k = 0; k < 2; ++k) w[j][k] = f2mul(w[j][k], norm2);
   }
 #pragma unroll
   for (int j = 0; j < J; ++j)
 #pragma unroll
-    for (int e = 0; e < 4; ++e) mx = fmax_nan(mx, fabsf(v[j][e]));
+    for (int k = 0; k < 2; ++k) {
+      float a, b;
+      f2unpack(w[j][k], a, b);
+      mx = fmax_nan(mx, fmax_nan(fabsf(a), fabsf(b)));
+    }
   mx = warp_max_nan(mx);
   if (lane == 0) red[2][warp] = mx;
   __syncthreads();
   mx = red[2][0];
 #pragma unroll
-  for (int w = 1; w < NW; ++w) mx = fmax_nan(mx, red[2][w]);
+  for (int w2 = 1; w2 < NW; ++w2) mx = fmax_nan(mx, red[2][w2]);
   const bool nan_row = mx != mx;  // the same on every thread of the row
   if (nan_row) {  // the reference's maximum ignores NaNs
     mx = 0.0f;
 #pragma unroll
     for (int j = 0; j < J; ++j)
 #pragma unroll
-      for (int e = 0; e < 4; ++e) mx = fmaxf(mx, fabsf(v[j][e]));
+      for (int k = 0; k < 2; ++k) {
+        float a, b;
+        f2unpack(w[j][k], a, b);
+        mx = fmaxf(mx, fmaxf(fabsf(a), fabsf(b)));
+      }
     mx = warp_max(mx);
     if (lane == 0) red[0][warp] = mx;
     __syncthreads();
     mx = red[0][0];
 #pragma unroll
-    for (int w = 1; w < NW; ++w) mx = fmaxf(mx, red[0][w]);
+    for (int w2 = 1; w2 < NW; ++w2) mx = fmaxf(mx, red[0][w2]);
   }
   if (threadIdx.x == 0) scales[row] = mx / 127.0f;
   const float inv = (mx > 0.0f) ? 127.0f / mx : 0.0f;
   uint32_t* dst = reinterpret_cast<uint32_t*>(codes + static_cast<long long>(row) * K + base);
   if (!nan_row && mx <= 3.40282347e38f && inv <= 3.40282347e38f) {
-#pragma unroll
-    for (int j = 0; j < J; ++j)
-      dst[32 * j] = codes4_fast(__fmul_rn(v[j][0], inv), __fmul_rn(v[j][1], inv), __fmul_rn(v[j][2], inv),
-                                __fmul_rn(v[j][3], inv));
+    dst_codes_fast(w, inv, dst);
   } else {
 #pragma unroll
-    for (int j = 0; j < J; ++j)
-      dst[32 * j] = codes4_ref(v[j][0] * inv, v[j][1] * inv, v[j][2] * inv, v[j][3] * inv);
+    for (int j = 0; j < J; ++j) {
+      float x0, x1, x2, x3;
+      f2unpack(w[j][0], x0, x1);
+      f2unpack(w[j][1], x2, x3);
+      dst[32 * j] = codes4_ref(x0 * inv, x1 * inv, x2 * inv, x3 * inv);
+    }
   }
 }
 
@@ -405,38 +416,33 @@ __global__ void __launch_bounds__(96) rowquant_b4096_kernel(RowSegs segs, int ha
     }
     phase ^= 1u;
   }
-  float v[J][4];
+  // float4 j as two FP32 pairs: w[j][0] = (x0, x1), w[j][1] = (x2, x3)
+  uint64_t w[J][2];
 #pragma unroll
   for (int j = 0; j < J; ++j) {
-    const float4 f = pw[32 * j + lane];
-    v[j][0] = f.x;
-    v[j][1] = f.y;
-    v[j][2] = f.z;
-    v[j][3] = f.w;
+    const ulonglong2 u = reinterpret_cast<const ulonglong2*>(pw)[32 * j + lane];
+    w[j][0] = u.x;
+    w[j][1] = u.y;
   }
   fence_proxy_async_smem();  // every lane's reads of the slice come before the copy overwrites it
   __syncwarp();
   if (lane == 0 && row + static_cast<int>(gridDim.x) < rows) prefetch(row + gridDim.x);
   auto stage_components = [&]() {
+    // half = 1: inside each pair, (x0, x1) -> (x0 + x1, x0 - x1)
+#pragma unroll
+    for (int j = 0; j < J; ++j)
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        float a, b;
+        f2unpack(w[j][k], a, b);
+        w[j][k] = f2pack(a + b, a - b);
+      }
+    // half = 2: (x0, x2) and (x1, x3) side by side in the two pairs
 #pragma unroll
     for (int j = 0; j < J; ++j) {
-      float a = v[j][0], b = v[j][1];
-      v[j][0] = a + b;
-      v[j][1] = a - b;
-      a = v[j][2];
-      b = v[j][3];
-      v[j][2] = a + b;
-      v[j][3] = a - b;
-    }
-#pragma unroll
-    for (int j = 0; j < J; ++j) {
-      float a = v[j][0], b = v[j][2];
-      v[j][0] = a + b;
-      v[j][2] = a - b;
-      a = v[j][1];
-      b = v[j][3];
-      v[j][1] = a + b;
-      v[j][3] = a - b;
+      const uint64_t a = w[j][0], b = w[j][1];
+      w[j][0] = f2add(a, b);
+      w[j][1] = f2sub(a, b);
     }
   };
   auto stages_registers = [&]() {  // register-index bits, lowest first
@@ -446,25 +452,24 @@ __global__ void __launch_bounds__(96) rowquant_b4096_kernel(RowSegs segs, int ha
       for (int j = 0; j < J; ++j) {
         if (j & jm) continue;
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float a = v[j][e], b = v[j | jm][e];
-          v[j][e] = a + b;
-          v[j | jm][e] = a - b;
+        for (int k = 0; k < 2; ++k) {
+          const uint64_t a = w[j][k], b = w[j | jm][k];
+          w[j][k] = f2add(a, b);
+          w[j | jm][k] = f2sub(a, b);
         }
       }
   };
   // transpose: (row j, col lane) <-> (row lane, col j) of the 32 x 32 float4 grid
+  ulonglong2* tw2 = reinterpret_cast<ulonglong2*>(tw);
   auto transpose = [&]() {
 #pragma unroll
-    for (int j = 0; j < J; ++j) tw[j * 32 + (lane ^ j)] = make_float4(v[j][0], v[j][1], v[j][2], v[j][3]);
+    for (int j = 0; j < J; ++j) tw2[j * 32 + (lane ^ j)] = make_ulonglong2(w[j][0], w[j][1]);
     __syncwarp();
 #pragma unroll
     for (int c = 0; c < J; ++c) {
-      const float4 f = tw[lane * 32 + (c ^ lane)];
-      v[c][0] = f.x;
-      v[c][1] = f.y;
-      v[c][2] = f.z;
-      v[c][3] = f.w;
+      const ulonglong2 u = tw2[lane * 32 + (c ^ lane)];
+      w[c][0] = u.x;
+      w[c][1] = u.y;
     }
     __syncwarp();
   };
@@ -475,13 +480,16 @@ __global__ void __launch_bounds__(96) rowquant_b4096_kernel(RowSegs segs, int ha
   stages_registers();  // half = 128 .. 2048
 
   const float norm = rsqrtf(static_cast<float>(had_block));  // had_block == 4096, evaluated at run time
+  const uint64_t norm2 = f2pack(norm, norm);
   float mx = 0.0f;
 #pragma unroll
   for (int j = 0; j < J; ++j)
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      v[j][e] *= norm;
-      mx = fmax_nan(mx, fabsf(v[j][e]));
+    for (int k = 0; k < 2; ++k) {
+      w[j][k] = f2mul(w[j][k], norm2);
+      float a, b;
+      f2unpack(w[j][k], a, b);
+      mx = fmax_nan(mx, fmax_nan(fabsf(a), fabsf(b)));
     }
   mx = warp_max_nan(mx);
   if (lane == 0) red[it & 1][warp] = mx;  // double buffered: the next row's writes go to the other slot
@@ -493,7 +501,11 @@ __global__ void __launch_bounds__(96) rowquant_b4096_kernel(RowSegs segs, int ha
 #pragma unroll
     for (int j = 0; j < J; ++j)
 #pragma unroll
-      for (int e = 0; e < 4; ++e) mx = fmaxf(mx, fabsf(v[j][e]));
+      for (int k = 0; k < 2; ++k) {
+        float a, b;
+        f2unpack(w[j][k], a, b);
+        mx = fmaxf(mx, fmaxf(fabsf(a), fabsf(b)));
+      }
     mx = warp_max(mx);
     if (lane == 0) red_nan[warp] = mx;
     __syncthreads();
@@ -503,14 +515,15 @@ __global__ void __launch_bounds__(96) rowquant_b4096_kernel(RowSegs segs, int ha
   const float inv = (mx > 0.0f) ? 127.0f / mx : 0.0f;
   uint32_t* dst = reinterpret_cast<uint32_t*>(codes + static_cast<long long>(row) * K + base);
   if (!nan_row && mx <= 3.40282347e38f && inv <= 3.40282347e38f) {
-#pragma unroll
-    for (int j = 0; j < J; ++j)
-      dst[32 * j] = codes4_fast(__fmul_rn(v[j][0], inv), __fmul_rn(v[j][1], inv), __fmul_rn(v[j][2], inv),
-                                __fmul_rn(v[j][3], inv));
+    dst_codes_fast(w, inv, dst);
   } else {
 #pragma unroll
-    for (int j = 0; j < J; ++j)
-      dst[32 * j] = codes4_ref(v[j][0] * inv, v[j][1] * inv, v[j][2] * inv, v[j][3] * inv);
+    for (int j = 0; j < J; ++j) {
+      float x0, x1, x2, x3;
+      f2unpack(w[j][0], x0, x1);
+      f2unpack(w[j][1], x2, x3);
+      dst[32 * j] = codes4_ref(x0 * inv, x1 * inv, x2 * inv, x3 * inv);
+    }
   }
   }
 }
