@@ -61,6 +61,11 @@ struct alignas(64) GemmArgsDev {
   int total_tiles;
   int epi;
   int* err;
+  // L2 eviction hints on the CTA-pair kernel's copies: 0 none; 1 the output
+  // (and residual) tiles and, for K >= 8192, the A panels evict_first (each is
+  // used once or by the tiles running at the same time), so the weight panels
+  // that every row block re-reads stay in L2; 2 also the weights evict_last
+  int l2;
 };
 
 __device__ __forceinline__ float gelu_tanh_dev(float v) {
@@ -94,10 +99,17 @@ __device__ __forceinline__ bool epilogue_tile(const GemmArgsDev& args, const Gem
   // this warp's 32-column chunks of the tile: [c_begin, nch)
   const int nch = min(min(NCH, c_limit), (P.N - n0 + 31) / 32);
   // residual: fetch the first chunk before waiting for the accumulator
+  const uint64_t pol_out = args.l2 ? l2_policy_evict_first() : 0ull;  // output / residual tiles
+  auto load_out = [&](void* dst, int col, uint64_t* bar) {
+    if (args.l2)
+      tma_load_2d_hint(dst, &P.tmO, col, r0, bar, pol_out);
+    else
+      tma_load_2d(dst, &P.tmO, col, r0, bar);
+  };
   if (resid && r0 < P.M && c_begin < nch && lane == 0) {
     bulk_wait_read<0>();
     mbar_expect_tx(&xb[c_begin & 1], EPI_BUF);
-    tma_load_2d(ebuf + (c_begin & 1) * EPI_BUF, &P.tmO, n0 + 32 * c_begin, r0, &xb[c_begin & 1]);
+    load_out(ebuf + (c_begin & 1) * EPI_BUF, n0 + 32 * c_begin, &xb[c_begin & 1]);
     es.xpending |= 1u << (c_begin & 1);
   }
   bool w = mbar_wait(&tfull[buf], acc_phase, abort_flag);
@@ -118,7 +130,7 @@ __device__ __forceinline__ bool epilogue_tile(const GemmArgsDev& args, const Gem
       if (lane == 0 && c + 1 < nch) {
         bulk_wait_read<0>();
         mbar_expect_tx(&xb[b ^ 1], EPI_BUF);
-        tma_load_2d(ebuf + (b ^ 1) * EPI_BUF, &P.tmO, gcol + 32, r0, &xb[b ^ 1]);
+        load_out(ebuf + (b ^ 1) * EPI_BUF, gcol + 32, &xb[b ^ 1]);
         es.xpending |= 1u << (b ^ 1);
       }
       w = mbar_wait(&xb[b], (es.xphase >> b) & 1, abort_flag);
@@ -177,7 +189,10 @@ __device__ __forceinline__ bool epilogue_tile(const GemmArgsDev& args, const Gem
     fence_proxy_async_smem();
     __syncwarp();
     if (lane == 0) {
-      tma_store_2d(&P.tmO, sbuf, gcol, r0);
+      if (args.l2)
+        tma_store_2d_hint(&P.tmO, sbuf, gcol, r0, pol_out);
+      else
+        tma_store_2d(&P.tmO, sbuf, gcol, r0);
       bulk_commit();
     }
     return true;
@@ -537,6 +552,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(gemm2::THREADS, 1)
     // ------------------------------------------------------------ producer (both CTAs)
     if (lane == 0) {
       const uint32_t full0 = mapa_shared(&full[0], 0);  // the even CTA's stage barriers
+      const uint64_t pol_first = l2_policy_evict_first(), pol_normal = l2_policy_evict_normal(),
+                     pol_last = l2_policy_evict_last();
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
@@ -552,8 +569,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(gemm2::THREADS, 1)
           }
           if (leader) mbar_expect_tx(&full[stage], 2 * STAGE_BYTES);  // both CTAs' bytes
           const uint32_t fb = full0 + stage * 8;
-          tma_load_2d_pair(sA + stage * A_BYTES, &P.tmA, kb * BK, m0 + 128 * static_cast<int>(cr), fb);
-          tma_load_2d_pair(sB + stage * B_BYTES, &P.tmB, kb * BK, n0 + (BN / 2) * static_cast<int>(cr), fb);
+          if (args.l2) {
+            tma_load_2d_pair_hint(sA + stage * A_BYTES, &P.tmA, kb * BK, m0 + 128 * static_cast<int>(cr), fb,
+                                  P.K >= 8192 ? pol_first : pol_normal);
+            tma_load_2d_pair_hint(sB + stage * B_BYTES, &P.tmB, kb * BK, n0 + (BN / 2) * static_cast<int>(cr), fb,
+                                  args.l2 >= 2 ? pol_last : pol_normal);
+          } else {
+            tma_load_2d_pair(sA + stage * A_BYTES, &P.tmA, kb * BK, m0 + 128 * static_cast<int>(cr), fb);
+            tma_load_2d_pair(sB + stage * B_BYTES, &P.tmB, kb * BK, n0 + (BN / 2) * static_cast<int>(cr), fb);
+          }
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1u;
@@ -799,6 +823,13 @@ int gemm_i8_launch(const GemmDesc* descs, int n, int epi, cudaStream_t stream, i
   args.total_tiles = tiles;
   args.epi = epi;
   args.err = err_dev;
+  static int l2_mode = -1;
+  if (l2_mode < 0) {  // QI_GEMM_L2 = 0 / 1 / 2 (measurements); default 2
+    const char* e = getenv("QI_GEMM_L2");
+    l2_mode = e ? atoi(e) : 2;
+    if (l2_mode < 0 || l2_mode > 2) l2_mode = 2;
+  }
+  args.l2 = pair ? l2_mode : 0;
   if (!pair) return launch_args<false>(args, stream, num_sms);
   return bn == 128 ? launch_pair<128>(args, stream, num_sms) : launch_pair<256>(args, stream, num_sms);
 }
