@@ -13,7 +13,8 @@
 //   fc1 cuBLAS + dequant+GELU; FWHT+quant      ->   GEMM GELU epilogue (1) + rowquant (1)
 //   fc2 cuBLAS + dequant; gate_add             ->   GEMM, residual epilogue (1)
 // The 120 modulation linears of a forward depend only on the timestep
-// (transformer.cu:506-515) and run as one GEMV over the stacked weights.
+// (transformer.cu:506-515) and run as one GEMV over the stacked weights
+// (split over the ranks of a head-parallel group, then all-gathered).
 // `nb` batch elements (CFG cond/uncond) share every launch.
 //
 // Head-parallel (Ulysses) forward over the P ranks of a communicator
@@ -984,8 +985,21 @@ int fwd_modulation(Fwd& f, float timestep) {
   QI_LAUNCH(QI_PROF_PRE, 1, silu_launch(c->p<float>(B_TEMB), c->p<float>(B_TSILU), kDim, s));
   RowSeg seg3{c->buf[B_TSILU], kDim, nullptr, nullptr, 1};
   QI_LAUNCH(QI_PROF_PRE, 1, rowquant_launch(kSrcF32, kDim, 1024, &seg3, 1, tact, tact_s, 0.0f, s));
-  GemvJob jm{m->mod.w, m->mod.s, m->mod.b, c->p<float>(B_MODS), m->mod.N};
-  QI_LAUNCH(QI_PROF_PRE, 1, gemv_i8_launch(tact, tact_s, kDim, &jm, 1, s));
+  // The stacked modulation GEMV (6.8 GB of weights) is the same on every rank
+  // of a head-parallel group: each rank computes 1/P of its rows and the group
+  // all-gathers them.  Every row's arithmetic is unchanged, so the vectors are
+  // bit-identical to one GPU's.
+  float* mods = c->p<float>(B_MODS);
+  if (f.P > 1 && m->mod.N % f.P == 0) {
+    const long long cnt = m->mod.N / f.P, lo = cnt * f.rank;
+    GemvJob jm{m->mod.w + lo * kDim, m->mod.s + lo, m->mod.b ? m->mod.b + lo : nullptr, mods + lo,
+               static_cast<int>(cnt)};
+    QI_LAUNCH(QI_PROF_PRE, 1, gemv_i8_launch(tact, tact_s, kDim, &jm, 1, s));
+    QI_LAUNCH(QI_PROF_EXCHANGE, 0, nccl_settle(c, ncclAllGather(mods + lo, mods, cnt, ncclFloat32, c->comm, s)));
+  } else {
+    GemvJob jm{m->mod.w, m->mod.s, m->mod.b, mods, m->mod.N};
+    QI_LAUNCH(QI_PROF_PRE, 1, gemv_i8_launch(tact, tact_s, kDim, &jm, 1, s));
+  }
   QI_LAUNCH(QI_PROF_PRE, 1,
             gemv_bf16_launch(c->p<float>(B_TSILU), m->norm_out_w, m->norm_out_b, c->p<float>(B_ADA), 2 * kDim, kDim, s));
   return QI_OK;

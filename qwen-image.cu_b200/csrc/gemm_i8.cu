@@ -458,8 +458,8 @@ __global__ void __launch_bounds__(gemm::THREADS, 1) gemm_kernel(const __grid_con
 // 256 columns, so a tile's epilogue takes about half as long as with four
 // and stays shorter than its main loop.
 //
-// Tile width BN = 256, or 128 where the 256-wide tiles leave most of a wave
-// idle (out and fc2 with few rows per rank): the narrower tiles use the same
+// Tile width BN = 256, or 192 / 128 where the 256-wide tiles would leave much
+// of their last wave idle (few rows per rank): the narrower tiles use the same
 // per-element arithmetic, so the outputs are identical.
 namespace gemm2 {
 constexpr int BM = 256, BK = 128;
@@ -467,7 +467,7 @@ constexpr int A_BYTES = 128 * BK;                // this CTA's 128 rows of A: 16
 template <int BN>
 constexpr int b_bytes() { return (BN / 2) * BK; }  // this CTA's half of B: 16 / 8 KB
 template <int BN>
-constexpr int stages() { return BN == 256 ? 5 : 6; }
+constexpr int stages() { return BN == 128 ? 6 : 5; }
 template <int BN>
 constexpr int stage_bytes() { return A_BYTES + b_bytes<BN>(); }
 constexpr int EPI_WARPS = 8;
@@ -475,14 +475,15 @@ constexpr int THREADS = 64 + 32 * EPI_WARPS;     // producer, MMA issuer, 8 epil
 constexpr int EPI_BYTES = EPI_WARPS * 2 * gemm::EPI_BUF;  // double buffered per warp: 64 KB
 template <int BN>
 constexpr int smem_bytes() { return stages<BN>() * stage_bytes<BN>() + EPI_BYTES + 1024 + 256; }
-static_assert(smem_bytes<256>() <= 232448 && smem_bytes<128>() <= 232448, "shared memory per CTA");
-constexpr int TMEM_COLS = 512;  // two accumulator buffers, 256 columns apart (BN = 128 uses half of each)
+static_assert(smem_bytes<256>() <= 232448 && smem_bytes<192>() <= 232448 && smem_bytes<128>() <= 232448,
+              "shared memory per CTA");
+constexpr int TMEM_COLS = 512;  // two accumulator buffers, 256 columns apart (narrower tiles use part of each)
 }  // namespace gemm2
 
 template <int BN>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(gemm2::THREADS, 1)
     gemm_pair_kernel(const __grid_constant__ GemmArgsDev args) {
-  static_assert(BN == 256 || BN == 128, "pair tile width");
+  static_assert(BN == 256 || BN == 192 || BN == 128, "pair tile width");
   using gemm2::A_BYTES;
   using gemm2::BK;
   using gemm2::BM;
@@ -753,31 +754,39 @@ static int launch_pair(GemmArgsDev& args, cudaStream_t stream, int num_sms) {
   return cudaGetLastError() == cudaSuccess ? QI_OK : QI_ERR_CUDA;
 }
 
-// Pair tile width: 128 when the narrower tiles finish sooner on the SM pairs.
-// A 256 x 128 tile takes 0.62-0.68 of a 256 x 256 tile's time (measured at
-// the forward's shapes: per MAC it moves 1.5x the operand bytes through L2
-// and shared memory), so they win only where wide tiles leave one wave of
-// pairs mostly idle (few rows).  QI_GEMM_PAIR_BN=128 / 256 forces a width
-// (measurements).
+// Pair tile width: the one whose waves of tiles over the SM pairs, times the
+// tile's cost relative to a 256 x 256 tile, finish first.  Costs measured at
+// the forward's shapes (per MAC a narrower tile moves more operand bytes
+// through L2 and shared memory): 256 x 192 0.84-0.86, 256 x 128 0.62-0.68.
+// Narrow tiles therefore win only where wide ones leave much of their last
+// wave idle (few rows per rank).  QI_GEMM_PAIR_BN=256 / 192 / 128 forces a
+// width (measurements).
 static int pair_tile_width(const GemmDesc* descs, int n, int clusters) {
   static int forced = -1;
   if (forced < 0) {
     const char* e = getenv("QI_GEMM_PAIR_BN");
     forced = e ? atoi(e) : 0;
-    if (forced != 128 && forced != 256) forced = 0;
+    if (forced != 128 && forced != 192 && forced != 256) forced = 0;
   }
   if (forced) return forced;
-  long long wide = 0, narrow = 0;
-  for (int i = 0; i < n; ++i) {
-    if (descs[i].M <= 0) continue;
-    const long long tm = (descs[i].M + gemm2::BM - 1) / gemm2::BM;
-    wide += tm * ((descs[i].N + 255) / 256);
-    narrow += tm * ((descs[i].N + 127) / 128);
+  constexpr int kWidths[3] = {256, 192, 128};
+  constexpr double kCost[3] = {1.0, 0.85, 0.68};
+  int best = 256;
+  double best_t = 0.0;
+  for (int c = 0; c < 3; ++c) {
+    long long tiles = 0;
+    for (int i = 0; i < n; ++i) {
+      if (descs[i].M <= 0) continue;
+      tiles += static_cast<long long>((descs[i].M + gemm2::BM - 1) / gemm2::BM) *
+               ((descs[i].N + kWidths[c] - 1) / kWidths[c]);
+    }
+    const double t = static_cast<double>((tiles + clusters - 1) / clusters) * kCost[c];
+    if (c == 0 || t < best_t * 0.97) {  // a narrower width must win clearly
+      best = kWidths[c];
+      best_t = t;
+    }
   }
-  constexpr double kNarrowCost = 0.18;
-  const double t_wide = static_cast<double>((wide + clusters - 1) / clusters);
-  const double t_narrow = static_cast<double>((narrow + clusters - 1) / clusters) * (0.5 + kNarrowCost);
-  return t_narrow < t_wide ? 128 : 256;
+  return best;
 }
 
 int gemm_i8_launch(const GemmDesc* descs, int n, int epi, cudaStream_t stream, int* err_dev, int num_sms) {
@@ -831,7 +840,9 @@ int gemm_i8_launch(const GemmDesc* descs, int n, int epi, cudaStream_t stream, i
   }
   args.l2 = pair ? l2_mode : 0;
   if (!pair) return launch_args<false>(args, stream, num_sms);
-  return bn == 128 ? launch_pair<128>(args, stream, num_sms) : launch_pair<256>(args, stream, num_sms);
+  if (bn == 128) return launch_pair<128>(args, stream, num_sms);
+  if (bn == 192) return launch_pair<192>(args, stream, num_sms);
+  return launch_pair<256>(args, stream, num_sms);
 }
 
 int gemm_bf16_launch(const GemmBf16Desc& d, cudaStream_t stream, int* err_dev, int num_sms) {

@@ -1,8 +1,8 @@
-"""The CTA-pair INT8 GEMM in both tile widths (256 x 256 and 256 x 128).
+"""The CTA-pair INT8 GEMM in its three tile widths (256 x 256, 256 x 192, 256 x 128).
 
 The library picks the width per launch from the tile count (narrow tiles when
 the wide ones would leave most of a wave of SM pairs idle); QI_GEMM_PAIR_BN
-forces one.  Both widths must give exact INT32 accumulators and the same
+forces one.  Every width must give exact INT32 accumulators and the same
 dequantized (+ GELU / gated residual) outputs bit for bit, so a child process
 per width runs the same seeded problems and the parent compares digests."""
 import json
@@ -61,8 +61,8 @@ def _run(width):
 
 
 def test_pair_tile_widths_agree_bit_for_bit():
-    wide, narrow = _run(256), _run(128)
-    for key in wide:
-        assert wide[key][0], f"{key}: 256-wide tiles, accumulators not exact"
-        assert narrow[key][0], f"{key}: 128-wide tiles, accumulators not exact"
-        assert wide[key][1] == narrow[key][1], f"{key}: outputs differ between tile widths"
+    runs = {w: _run(w) for w in (256, 192, 128)}
+    for key in runs[256]:
+        for w, r in runs.items():
+            assert r[key][0], f"{key}: {w}-wide tiles, accumulators not exact"
+            assert r[key][1] == runs[256][key][1], f"{key}: {w}-wide tile outputs differ from the 256-wide ones"
