@@ -955,19 +955,40 @@ __global__ void __launch_bounds__(256) sage_v_fp8_kernel(const __half* __restric
   }
 }
 
+// The K mean on `side` (when given) while the main stream quantizes Q; the
+// main stream waits for it before the K quantizer.
+static int kmean_forked(const __half* kh, float* kmean, int BH, int S, cudaStream_t stream, const SideStream* side) {
+  cudaStream_t ks = stream;
+  if (side) {
+    if (cudaEventRecord(side->fork, stream) != cudaSuccess || cudaStreamWaitEvent(side->s, side->fork, 0) != cudaSuccess)
+      return QI_ERR_CUDA;
+    ks = side->s;
+  }
+  // one wave of CTAs: 32, 64 or 128 dims per CTA
+  const int sms = device_num_sms();
+  const int st = (BH * 4 <= sms) ? kmean_launch<32>(kh, kmean, BH, S, ks)
+                 : (BH * 2 <= sms) ? kmean_launch<64>(kh, kmean, BH, S, ks)
+                                   : kmean_launch<128>(kh, kmean, BH, S, ks);
+  if (st != QI_OK) return st;
+  if (side && cudaEventRecord(side->join, side->s) != cudaSuccess) return QI_ERR_CUDA;
+  return QI_OK;
+}
+static int kmean_joined(cudaStream_t stream, const SideStream* side) {
+  if (side && cudaStreamWaitEvent(stream, side->join, 0) != cudaSuccess) return QI_ERR_CUDA;
+  return QI_OK;
+}
+
 int sage_quantize_fp8pv_launch(const void* q, const void* k, const void* v, int BH, int S, float* kmean, int8_t* qc,
                                float* qs, int8_t* kc, float* ks, uint8_t* vt, int s_pad, float* vamax, float* vs,
-                               cudaStream_t stream) {
+                               cudaStream_t stream, const SideStream* side) {
   if (BH <= 0 || S <= 0 || s_pad < S || s_pad % 16) return QI_ERR_ARG;
-  const int sms = device_num_sms();
   const __half* kh = reinterpret_cast<const __half*>(k);
   const __half* vh = reinterpret_cast<const __half*>(v);
-  const int st = (BH * 4 <= sms) ? kmean_launch<32>(kh, kmean, BH, S, stream)
-                 : (BH * 2 <= sms) ? kmean_launch<64>(kh, kmean, BH, S, stream)
-                                   : kmean_launch<128>(kh, kmean, BH, S, stream);
+  int st = kmean_forked(kh, kmean, BH, S, stream, side);
   if (st != QI_OK) return st;
   sage_quant_block_kernel<128, 32><<<dim3((S + 127) / 128, BH), 256, 0, stream>>>(
       reinterpret_cast<const __half*>(q), nullptr, qc, qs, S);
+  if ((st = kmean_joined(stream, side)) != QI_OK) return st;
   sage_quant_block_kernel<64, 4><<<dim3((S + 63) / 64, BH), 256, 0, stream>>>(kh, kmean, kc, ks, S);
   if (cudaMemsetAsync(vamax, 0, static_cast<size_t>(BH) * 128 * sizeof(float), stream) != cudaSuccess)
     return QI_ERR_CUDA;
@@ -977,16 +998,13 @@ int sage_quantize_fp8pv_launch(const void* q, const void* k, const void* v, int 
 }
 
 int sage_quantize_launch(const void* q, const void* k, int BH, int S, float* kmean, int8_t* qc, float* qs, int8_t* kc,
-                         float* ks, cudaStream_t stream) {
+                         float* ks, cudaStream_t stream, const SideStream* side) {
   if (BH <= 0 || S <= 0) return QI_ERR_ARG;
-  // one wave of CTAs: 32, 64 or 128 dims per CTA
-  const int sms = device_num_sms();
   const __half* kh = reinterpret_cast<const __half*>(k);
-  const int st = (BH * 4 <= sms) ? kmean_launch<32>(kh, kmean, BH, S, stream)
-                 : (BH * 2 <= sms) ? kmean_launch<64>(kh, kmean, BH, S, stream)
-                                   : kmean_launch<128>(kh, kmean, BH, S, stream);
+  int st = kmean_forked(kh, kmean, BH, S, stream, side);
   if (st != QI_OK) return st;
   sage_quant_q_kernel<<<dim3((S + 127) / 128, BH), 256, 0, stream>>>(reinterpret_cast<const __half*>(q), qc, qs, S);
+  if ((st = kmean_joined(stream, side)) != QI_OK) return st;
   sage_quant_k_kernel<<<dim3((S + 127) / 128, BH), 256, 0, stream>>>(reinterpret_cast<const __half*>(k), kmean, kc, ks,
                                                                      S);
   return cudaGetLastError() == cudaSuccess ? QI_OK : QI_ERR_CUDA;

@@ -116,6 +116,7 @@ struct qi_ctx {
   bool peers_ready = false;
   long long peer_key[3] = {-1, -1, -1};
   std::vector<void*> peer_opened;
+  SideStream side = {nullptr, nullptr, nullptr};  // forward work that overlaps the main stream (K mean)
   unsigned* flags = nullptr;  // this rank's flag words [2][kMaxRanks]
   unsigned epoch = 0;
   void* handles = nullptr;    // device staging for the IPC handle all-gather
@@ -301,6 +302,9 @@ int qi_ctx_destroy(qi_ctx* c) {
     cudaEventDestroy(p.second.second);
   }
   for (cudaEvent_t e : c->pool) cudaEventDestroy(e);
+  if (c->side.s) cudaStreamDestroy(c->side.s);
+  if (c->side.fork) cudaEventDestroy(c->side.fork);
+  if (c->side.join) cudaEventDestroy(c->side.join);
   for (int i = 0; i < B_COUNT; ++i)
     if (c->buf[i]) cudaFree(c->buf[i]);
   if (c->err) cudaFree(c->err);
@@ -907,6 +911,12 @@ int fwd_init(Fwd& f, qi_ctx* c, const qi_model* m, int nb, int n_img, int n_txt,
   f.n_txt = n_txt;
   f.S = n_img + n_txt;
   if (c->comm_failed) return QI_ERR_NCCL;  // the group was aborted: rejoin with qi_ctx_set_comm
+  if (!c->side.s) {
+    if (cudaStreamCreateWithFlags(&c->side.s, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaEventCreateWithFlags(&c->side.fork, cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&c->side.join, cudaEventDisableTiming) != cudaSuccess)
+      return QI_ERR_CUDA;
+  }
   f.P = c->usize;
   f.rank = c->urank;
   f.Hl = kHeads / f.P;
@@ -1081,11 +1091,11 @@ int fwd_blocks(Fwd& f, float* x_img, float* x_txt, const float* pe, int b0, int 
                 sage_quantize_fp8pv_launch(qkvh, qkvh + hs, qkvh + 2 * hs, BH, S, c->p<float>(B_KMEAN),
                                            c->p<int8_t>(B_QC), c->p<float>(B_QS), c->p<int8_t>(B_KC),
                                            c->p<float>(B_KS), c->p<uint8_t>(B_V8), s_pad, c->p<float>(B_VAMAX),
-                                           c->p<float>(B_VS), s));
+                                           c->p<float>(B_VS), s, &c->side));
     else
       QI_LAUNCH(QI_PROF_SAGE_QUANT, 3,
                 sage_quantize_launch(qkvh, qkvh + hs, BH, S, c->p<float>(B_KMEAN), c->p<int8_t>(B_QC),
-                                     c->p<float>(B_QS), c->p<int8_t>(B_KC), c->p<float>(B_KS), s));
+                                     c->p<float>(B_QS), c->p<int8_t>(B_KC), c->p<float>(B_KS), s, &c->side));
     AttnArgs aa{c->p<int8_t>(B_QC), c->p<float>(B_QS), c->p<int8_t>(B_KC), c->p<float>(B_KS), qkvh + 2 * hs,
                 par && !direct ? c->buf[B_SEND2] : c->buf[B_O], BH, S, f.Hl, 1.0f / sqrtf(128.0f),
                 direct ? 3 : (par ? 2 : 1), nb, n_img, n_txt, f.map};

@@ -175,8 +175,17 @@ int qkv_post_launch(const QkvPostArgs& a, cudaStream_t stream);
 // Longest joint sequence the attention kernel takes (its K scales of up to
 // 8192 64-key blocks fit in shared memory).
 constexpr int kAttnMaxS = 131072;
+// A second stream for work that may overlap the main stream's: `fork` is
+// recorded on the main stream before the side work, `join` on the side stream
+// after it; the main stream waits for `join` before it needs the results.
+struct SideStream {
+  cudaStream_t s;
+  cudaEvent_t fork, join;
+};
+// side != nullptr: the K mean (a latency-bound chain over the tokens on a few
+// CTAs) runs on the side stream beside the Q quantizer.
 int sage_quantize_launch(const void* q, const void* k, int BH, int S, float* kmean, int8_t* qc, float* qs,
-                         int8_t* kc, float* ks, cudaStream_t stream);
+                         int8_t* kc, float* ks, cudaStream_t stream, const SideStream* side = nullptr);
 // out_mode 0: FP32 [BH, S, 128] head-major.
 // out_mode 1: FP16 token-major rows for the out-projection: joint position p
 //   of batch b goes to row (p < n_txt ? nb*n_img + b*n_txt + p
@@ -215,7 +224,7 @@ int attention_launch(const AttnArgs& a, cudaStream_t stream, int* err_dev);
 // (batch-head, dim); vs receives v_scale / 448.  vamax is [BH][128] scratch.
 int sage_quantize_fp8pv_launch(const void* q, const void* k, const void* v, int BH, int S, float* kmean, int8_t* qc,
                                float* qs, int8_t* kc, float* ks, uint8_t* vt, int s_pad, float* vamax, float* vs,
-                               cudaStream_t stream);
+                               cudaStream_t stream, const SideStream* side = nullptr);
 
 int cfg_euler_launch(float* x, const void* cond, const void* uncond, float cfg, float sigma, float sigma_next, int H,
                      int W, void* x_bf16, cudaStream_t stream);
