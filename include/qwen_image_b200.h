@@ -283,6 +283,45 @@ int qi_forward(qi_ctx* ctx, const qi_model* model, int nb, const void* x_bf16, f
 int qi_forward_blocks(qi_ctx* ctx, const qi_model* model, int nb, int n_img, int n_txt, float* img, float* txt,
                       float timestep, const float* pe, int block_begin, int block_end, void* stream);
 
+/* ---- Spectrum step skipping (the reference's --spectrum: main.cu:640-748,
+ * 877-885; transformer.cu:864-871, 939-1028; cuda_kernels.cu:5859-6333).
+ *
+ * Every qi_forward on the context copies its final image hidden state (before
+ * norm_out) to hidden_out, [nb][n_img][3072] FP32, 16-byte aligned, until
+ * set to NULL: the reference's transformer_forward spectrum_hidden_out.
+ * Single-GPU contexts only (QI_ERR_UNSUPPORTED with a head-parallel group). */
+int qi_ctx_set_hidden_capture(qi_ctx* ctx, float* hidden_out);
+
+/* The output head on a final image hidden state [nb][n_img][3072] FP32:
+ * timestep MLP, norm_out modulation, AdaLayerNormContinuous, proj_out,
+ * unpatchify -> nb x [16, H, W] BF16.  Replaces transformer_spectrum_output
+ * (transformer.h:627-630, transformer.cu:939-1028); runs the same kernels as
+ * the end of qi_forward, so a captured state gives that forward's output.  */
+int qi_spectrum_output(qi_ctx* ctx, const qi_model* model, int nb, const float* hidden, float timestep, int H, int W,
+                       void* out_bf16, void* stream);
+
+/* Feature forecaster over the states of actual forwards (SpectrumState,
+ * spectrum_init / update / predict / reset, cuda_kernels.cuh:588-645):
+ * feature_elems floats per state (a multiple of 4), at most max_history
+ * states kept (the oldest replaced; at most 128), Chebyshev order (bases
+ * T_0..T_order, at most 16) and ridge lambda.                              */
+typedef struct qi_spectrum qi_spectrum;
+int qi_spectrum_create(long long feature_elems, int max_history, int order, float lambda, qi_spectrum** out);
+int qi_spectrum_destroy(qi_spectrum* s);
+/* Stores the state of an actual forward at `step` (steps must increase);
+ * the copy is enqueued on `stream`.                                        */
+int qi_spectrum_update(qi_spectrum* s, const float* feature, int step, void* stream);
+/* Predicts the state at target_step into out (feature_elems floats, 16-byte
+ * aligned): blend x Chebyshev ridge fit + (1 - blend) x first-order Taylor
+ * extrapolation from the last two states.  Needs two stored states.       */
+int qi_spectrum_predict(qi_spectrum* s, int target_step, float blend, float* out, void* stream);
+/* Number of stored states (SpectrumState::buffer_size).                    */
+int qi_spectrum_history(const qi_spectrum* s);
+int qi_spectrum_reset(qi_spectrum* s);
+/* The K prediction weights of qi_spectrum_predict (host only, double):
+ * out = sum_k w[k] x state_k over stored steps[0..K) (increasing).          */
+int qi_spectrum_weights(const int* steps, int K, int order, float lambda, int target_step, float blend, double* w);
+
 /* RoPE table of rope.h gen_qwen_image_pe (h, w = latent size): host memory,
  * [n_txt + n_img, 64, 2, 2] FP32.                                            */
 int qi_rope_table(int h, int w, int n_txt, float* pe_host);

@@ -277,6 +277,46 @@ def sage_attention(q16, k16, v16, scale):
     return out
 
 
+# ---------------------------------------------------------------- Spectrum
+def spectrum_predict(hist, steps, target, blend=1.0, order=4, lam=0.1):
+    """The reference's spectrum_predict (cuda_kernels.cu:6268-6333) in float64
+    on the stored states hist [K, F] (oldest first) at steps[0..K):
+      tau_k = (t_k - mid) * 2 / range, mid / range over steps[0], steps[K-1]
+        (normalize_tau_kernel, :5890-5904; 0 when range < 1e-6);
+      X[k, m] = T_m(tau_k) by the Chebyshev recurrence (chebyshev_design_kernel,
+        :5865-5886); C = (X^T X + lam I)^-1 X^T H (spectrum_fit_ridge_regression,
+        :6014-6089: SGEMMs, Cholesky, two triangular solves);
+      cheb = row(tau_target) C (build_chebyshev_row_kernel, chebyshev_predict_kernel);
+      taylor = h_i + k (h_i - h_{i-1}), k = (target - t_i) / max(t_i - t_{i-1}, 1e-6)
+        (taylor_predict_kernel with order 1, :6104-6149);
+      out = (1 - blend) taylor + blend cheb (blend_predictions_kernel, :6152-6162)."""
+    hist = np.asarray(hist, dtype=np.float64)
+    t = np.asarray(steps, dtype=np.float64)
+    P = order + 1
+    mid, rng = 0.5 * (t[0] + t[-1]), t[-1] - t[0]
+
+    def tau(v):
+        return 0.0 if rng < 1e-6 else (v - mid) * 2.0 / rng
+
+    def cheb_row(x):
+        r = np.zeros(P)
+        r[0] = 1.0
+        if P > 1:
+            r[1] = x
+        for m in range(2, P):
+            r[m] = 2.0 * x * r[m - 1] - r[m - 2]
+        return r
+
+    X = np.stack([cheb_row(tau(v)) for v in t])
+    A = X.T @ X + lam * np.eye(P)
+    C = np.linalg.solve(A, X.T @ hist)
+    cheb = cheb_row(tau(float(target))) @ C
+    dt = max(t[-1] - t[-2], 1e-6)
+    k = (float(target) - t[-1]) / dt
+    taylor = hist[-1] + k * (hist[-1] - hist[-2])
+    return (1.0 - blend) * taylor + blend * cheb
+
+
 def set_threads(n):
     lib().or_set_num_threads(int(n))
 

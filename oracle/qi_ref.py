@@ -41,6 +41,9 @@ def lib():
             "ref_gate_add": [vp, vp, vp, vp, i, i],
             "ref_load_all": [ctypes.c_char_p, vp],
             "ref_transformer_forward": [vp, vp, vp, f, vp, i, vp, i, i, i, vp],
+            "ref_transformer_forward_capture": [vp, vp, vp, f, vp, i, vp, i, i, i, vp, vp],
+            "ref_transformer_spectrum_output": [vp, vp, vp, f, i, i, vp],
+            "ref_spectrum_predict": [vp, vp, i, ll, i, f, i, f, vp],
         }
         for name, args in sig.items():
             fn = getattr(L, name)
@@ -165,6 +168,30 @@ def transformer_forward(garr, bt, x, t, txt, pe, H, W, sage=True):
     out = torch.empty_like(x)
     _ok(lib().ref_transformer_forward(garr, bt, _p(x), float(t), _p(txt), txt.shape[-2], _p(pe), H, W, int(sage),
                                       _p(out)))
+    return out
+
+
+def transformer_forward_capture(garr, bt, x, t, txt, pe, H, W, sage=True):
+    """transformer_forward with spectrum_hidden_out: (output, final image hidden state [n_img, 3072])."""
+    out = torch.empty_like(x)
+    hidden = torch.empty((H // 2) * (W // 2), 3072, dtype=torch.float32, device=x.device)
+    _ok(lib().ref_transformer_forward_capture(garr, bt, _p(x), float(t), _p(txt), txt.shape[-2], _p(pe), H, W,
+                                              int(sage), _p(out), _p(hidden)))
+    return out, hidden
+
+
+def transformer_spectrum_output(garr, bt, hidden, t, H, W):
+    out = torch.empty(1, 16, H, W, dtype=torch.bfloat16, device=hidden.device)
+    _ok(lib().ref_transformer_spectrum_output(garr, bt, _p(hidden), float(t), H, W, _p(out)))
+    return out
+
+
+def spectrum_predict(hist, steps, target, blend=1.0, order=4, lam=0.1):
+    """The reference's SpectrumState over hist [K, F] (device FP32) stored at `steps`."""
+    K, F = hist.shape
+    st = (ctypes.c_int * K)(*[int(v) for v in steps])
+    out = torch.empty(F, dtype=torch.float32, device=hist.device)
+    _ok(lib().ref_spectrum_predict(_p(hist), st, K, F, int(order), float(lam), int(target), float(blend), _p(out)))
     return out
 
 

@@ -40,16 +40,9 @@ QuantizedWeight qw_bf16(const void* w, int N, int K) {
   return q;
 }
 
-}  // namespace
-
-extern "C" {
-
-// transformer_forward (transformer.cu:234) over a weight table.  The
-// reference loops over exactly 60 blocks; block_tables must hold 60 entries
-// (they may repeat).  x: [1,16,H,W] BF16, ctx: [1,n_txt,3584] BF16,
-// pe: [n_txt+n_img,64,2,2] FP32, out: [1,16,H,W] BF16.
-int ref_transformer_forward(const void* const* g, const void* const* const* bt, const void* x, float t,
-                            const void* ctx, int n_txt, const float* pe, int H, int W, int sage, void* out) {
+// The reference's TransformerWeights over a device weight table (60 blocks;
+// block_tables may repeat entries).
+TransformerWeights make_weights(const void* const* g, const void* const* const* bt) {
   TransformerWeights w;
   w.time_linear1_weight = qw_int8(g[QI_G_T1_W], g[QI_G_T1_S], 3072, 256);
   w.time_linear1_bias = view_of(g[QI_G_T1_B], {3072}, DType::BF16);
@@ -89,11 +82,43 @@ int ref_transformer_forward(const void* const* g, const void* const* const* bt, 
     B.norm_added_q_weight = view_of(tb[QI_B_NORM_ADDED_Q], {128}, DType::BF16);
     B.norm_added_k_weight = view_of(tb[QI_B_NORM_ADDED_K], {128}, DType::BF16);
   }
+  return w;
+}
+
+}  // namespace
+
+extern "C" {
+
+// transformer_forward (transformer.cu:234) over a weight table.  The
+// reference loops over exactly 60 blocks; block_tables must hold 60 entries
+// (they may repeat).  x: [1,16,H,W] BF16, ctx: [1,n_txt,3584] BF16,
+// pe: [n_txt+n_img,64,2,2] FP32, out: [1,16,H,W] BF16; hidden_out (or null):
+// the final image hidden state [n_img, 3072] FP32 (spectrum_hidden_out).
+int ref_transformer_forward_capture(const void* const* g, const void* const* const* bt, const void* x, float t,
+                                    const void* ctx, int n_txt, const float* pe, int H, int W, int sage, void* out,
+                                    float* hidden_out) {
+  TransformerWeights w = make_weights(g, bt);
   const int n_img = (H / 2) * (W / 2);
   Tensor xt = view_of(x, {1, 16, H, W}, DType::BF16);
   Tensor ct = view_of(ctx, {1, n_txt, 3584}, DType::BF16);
   Tensor pt = view_of(pe, {n_txt + n_img, 64, 2, 2}, DType::FP32);
-  Tensor o = transformer_forward(w, xt, t, ct, pt, H, W, nullptr, sage != 0, nullptr);
+  Tensor o = transformer_forward(w, xt, t, ct, pt, H, W, nullptr, sage != 0, hidden_out);
+  cudaMemcpy(out, o.data, static_cast<size_t>(16) * H * W * 2, cudaMemcpyDeviceToDevice);
+  o.free_data();
+  return cudaDeviceSynchronize() == cudaSuccess ? 0 : 3;
+}
+
+int ref_transformer_forward(const void* const* g, const void* const* const* bt, const void* x, float t,
+                            const void* ctx, int n_txt, const float* pe, int H, int W, int sage, void* out) {
+  return ref_transformer_forward_capture(g, bt, x, t, ctx, n_txt, pe, H, W, sage, out, nullptr);
+}
+
+// transformer_spectrum_output (transformer.cu:939-1028) on a final image
+// hidden state [n_img, 3072] FP32; out: [1,16,H,W] BF16.
+int ref_transformer_spectrum_output(const void* const* g, const void* const* const* bt, const float* hidden, float t,
+                                    int H, int W, void* out) {
+  TransformerWeights w = make_weights(g, bt);
+  Tensor o = transformer_spectrum_output(w, hidden, t, H, W);
   cudaMemcpy(out, o.data, static_cast<size_t>(16) * H * W * 2, cudaMemcpyDeviceToDevice);
   o.free_data();
   return cudaDeviceSynchronize() == cudaSuccess ? 0 : 3;

@@ -203,6 +203,20 @@ int ref_load_all(const char* path, long long* bytes) {
 }
 
 // RoPE table from the reference's own host code (rope.h:175).
+// spectrum_init / spectrum_update x K / spectrum_predict (cuda_kernels.cu:
+// 6168-6333) on the states hist [K][F] stored at steps[0..K); out [F].
+int ref_spectrum_predict(const float* hist, const int* steps, int K, long long F, int order, float lambda,
+                         int target, float blend, float* out) {
+  SpectrumState st;
+  spectrum_init(st, static_cast<int>(F), 1, K, order);
+  st.ridge_lambda = lambda;
+  for (int k = 0; k < K; ++k) spectrum_update(st, hist + static_cast<size_t>(k) * F, steps[k]);
+  spectrum_predict(st, out, target, blend);
+  const int rc = sync_status();
+  st.free_all();
+  return rc;
+}
+
 int ref_rope_table(int h, int w, int n_txt, float* pe_host) {
   std::vector<float> pe = RoPE::gen_qwen_image_pe(h, w, 2, 1, n_txt, 10000, {16, 56, 56});
   memcpy(pe_host, pe.data(), pe.size() * sizeof(float));

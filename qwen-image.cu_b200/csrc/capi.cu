@@ -117,6 +117,7 @@ struct qi_ctx {
   long long peer_key[3] = {-1, -1, -1};
   std::vector<void*> peer_opened;
   SideStream side = {nullptr, nullptr, nullptr};  // forward work that overlaps the main stream (K mean)
+  float* capture = nullptr;  // qi_ctx_set_hidden_capture: final image hidden state of every qi_forward
   unsigned* flags = nullptr;  // this rank's flag words [2][kMaxRanks]
   unsigned epoch = 0;
   void* handles = nullptr;    // device staging for the IPC handle all-gather
@@ -976,7 +977,7 @@ int fwd_init(Fwd& f, qi_ctx* c, const qi_model* m, int nb, int n_img, int n_txt,
 // Timestep MLP (transformer.cu:330-349), all modulation vectors of the
 // forward (transformer.cu:506-515: they depend only on t) and the output
 // AdaLN embedding (transformer.cu:874-877).
-int fwd_modulation(Fwd& f, float timestep) {
+int fwd_modulation(Fwd& f, float timestep, bool block_mods = true) {
   qi_ctx* c = f.c;
   const qi_model* m = f.m;
   cudaStream_t s = f.s;
@@ -1000,7 +1001,9 @@ int fwd_modulation(Fwd& f, float timestep) {
   // all-gathers them.  Every row's arithmetic is unchanged, so the vectors are
   // bit-identical to one GPU's.
   float* mods = c->p<float>(B_MODS);
-  if (f.P > 1 && m->mod.N % f.P == 0) {
+  if (!block_mods) {
+    // output head only (qi_spectrum_output): no block modulation vectors
+  } else if (f.P > 1 && m->mod.N % f.P == 0) {
     const long long cnt = m->mod.N / f.P, lo = cnt * f.rank;
     GemvJob jm{m->mod.w + lo * kDim, m->mod.s + lo, m->mod.b ? m->mod.b + lo : nullptr, mods + lo,
                static_cast<int>(cnt)};
@@ -1201,6 +1204,7 @@ extern "C" int qi_forward(qi_ctx* c, const qi_model* m, int nb, const void* x, f
                           int n_txt, const float* pe, int H, int W, void* out, void* stream) {
   if (!c || !m || !x || !ctx_txt || !pe || !out) return QI_ERR_ARG;
   if (nb < 1 || nb > 8 || n_txt < 1 || H < 2 || W < 2 || (H & 1) || (W & 1)) return QI_ERR_ARG;
+  if (c->capture && c->usize > 1) return QI_ERR_UNSUPPORTED;  // each rank holds only its image rows
   Fwd f;
   QI_TRY(fwd_init(f, c, m, nb, (H / 2) * (W / 2), n_txt, stream));
   float* x_img = c->p<float>(B_X);
@@ -1208,7 +1212,37 @@ extern "C" int qi_forward(qi_ctx* c, const qi_model* m, int nb, const void* x, f
   QI_TRY(fwd_inputs(f, x, ctx_txt, H, W, x_img, x_txt));
   QI_TRY(fwd_modulation(f, timestep));
   QI_TRY(fwd_blocks(f, x_img, x_txt, pe, 0, m->nblocks));
+  if (c->capture &&  // the final image hidden state, before norm_out (transformer.cu:864-871)
+      cudaMemcpyAsync(c->capture, x_img, static_cast<size_t>(f.Mi) * kDim * sizeof(float), cudaMemcpyDeviceToDevice,
+                      f.s) != cudaSuccess)
+    return QI_ERR_CUDA;
   QI_TRY(fwd_output(f, x_img, H, W, out));
+  c->launches = f.n;
+  return QI_OK;
+}
+
+extern "C" int qi_ctx_set_hidden_capture(qi_ctx* c, float* hidden_out) {
+  if (!c) return QI_ERR_ARG;
+  if (hidden_out && (reinterpret_cast<uintptr_t>(hidden_out) & 15)) return QI_ERR_ALIGN;
+  c->capture = hidden_out;
+  return QI_OK;
+}
+
+// The output head on a given final image hidden state: timestep MLP,
+// norm_out modulation, AdaLayerNormContinuous, proj_out, unpatchify -- the
+// reference's transformer_spectrum_output (transformer.cu:939-1028), here the
+// same kernels as the end of qi_forward, so a hidden state captured from a
+// forward gives that forward's output bit for bit.
+extern "C" int qi_spectrum_output(qi_ctx* c, const qi_model* m, int nb, const float* hidden, float timestep, int H,
+                                  int W, void* out, void* stream) {
+  if (!c || !m || !hidden || !out) return QI_ERR_ARG;
+  if (nb < 1 || nb > 8 || H < 2 || W < 2 || (H & 1) || (W & 1)) return QI_ERR_ARG;
+  if (c->usize > 1) return QI_ERR_UNSUPPORTED;
+  if (reinterpret_cast<uintptr_t>(hidden) & 15) return QI_ERR_ALIGN;
+  Fwd f;
+  QI_TRY(fwd_init(f, c, m, nb, (H / 2) * (W / 2), 1, stream));
+  QI_TRY(fwd_modulation(f, timestep, false));
+  QI_TRY(fwd_output(f, hidden, H, W, out));
   c->launches = f.n;
   return QI_OK;
 }

@@ -89,6 +89,25 @@ __device__ __forceinline__ void dst_codes_fast(const uint64_t (&w)[J][2], float 
   }
 }
 
+// The reference's mean = sum / dim and inv_std = rsqrtf(var_sum / dim + eps)
+// (cuda_kernels.cu:1827, 1847) under fast math: a division is a times the
+// approximate reciprocal of b, and in the reference build the compiler fuses
+// that product with the following + eps into one FMA.  Whether it does so
+// depends on the surrounding code, so both are written out here as explicit
+// instructions: measured against the reference's LayerNorm-quantizer codes,
+// the fused form matches bit for bit and the separately rounded one does not
+// (tens of flipped codes per million).
+__device__ __forceinline__ float ln_mean(float sum, int dim) {
+  float m;
+  asm("div.approx.ftz.f32 %0, %1, %2;" : "=f"(m) : "f"(sum), "f"(static_cast<float>(dim)));
+  return m;
+}
+__device__ __forceinline__ float ln_inv_std(float var_sum, int dim, float eps) {
+  float r;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(static_cast<float>(dim)));
+  return rsqrtf(__fmaf_rn(var_sum, r, eps));
+}
+
 // Sum over the 1024 threads of a reference reduction block in the order of
 // its two-level shfl_down tree.  The lane stands for reference warp `lane`
 // (threads 32 * lane + L, L = 0..31); part(q, p) gives the partials of threads
@@ -206,7 +225,7 @@ __global__ void __launch_bounds__(NW * 32) rowquant_warp_kernel(RowSegs segs, in
         f2unpack(f2add(f2add(f0.x, f1.x), f2.x), o[0], o[1]);
         f2unpack(f2add(f2add(f0.y, f1.y), f2.y), o[2], o[3]);
       };
-      const float mean = ref_block_tree(sum_part) / dim;
+      const float mean = ln_mean(ref_block_tree(sum_part), dim);
       const uint64_t mean2 = f2pack(mean, mean);
       // var_sum += v * v over the same elements, v = x - mean (the first
       // product's += onto 0 is the product itself)
@@ -226,7 +245,7 @@ __global__ void __launch_bounds__(NW * 32) rowquant_warp_kernel(RowSegs segs, in
           f2unpack(var_sum, o[2 * k], o[2 * k + 1]);
         }
       };
-      const float inv_std = rsqrtf(ref_block_tree(var_part) / dim + eps);
+      const float inv_std = ln_inv_std(ref_block_tree(var_part), dim, eps);
       if (lane == 0) {
         red[0][0] = mean;
         red[1][0] = inv_std;

@@ -109,6 +109,15 @@ def lib():
             "qi_exchange_plan": ([i, i, i, i, i, i, vp, vp, vp, vp], i),
             "qi_rope_table": ([i, i, i, vp], i),
             "qi_synth_fill": ([vp, ll, ull, f, f, i, vp], i),
+            "qi_ctx_set_hidden_capture": ([vp, vp], i),
+            "qi_spectrum_output": ([vp, vp, i, vp, f, i, i, vp, vp], i),
+            "qi_spectrum_create": ([ll, i, i, f, ctypes.POINTER(vp)], i),
+            "qi_spectrum_destroy": ([vp], i),
+            "qi_spectrum_update": ([vp, vp, i, vp], i),
+            "qi_spectrum_predict": ([vp, i, f, vp, vp], i),
+            "qi_spectrum_history": ([vp], i),
+            "qi_spectrum_reset": ([vp], i),
+            "qi_spectrum_weights": ([vp, i, i, f, i, f, vp], i),
             "qi_seed_for": ([ull, ctypes.c_char_p], ull),
         }
         for name, (args, res) in sig.items():
@@ -358,6 +367,11 @@ class Context:
         deadline."""
         check(lib().qi_ctx_sync(self.h, _stream(), int(timeout_ms)))
 
+    def set_hidden_capture(self, hidden):
+        """Every forward copies its final image hidden state [nb*n_img, 3072]
+        FP32 into `hidden` (a device tensor; None stops)."""
+        check(lib().qi_ctx_set_hidden_capture(self.h, _p(hidden) if hidden is not None else None))
+
     def close(self):
         if self.h:
             lib().qi_ctx_destroy(self.h)
@@ -414,6 +428,58 @@ def forward_blocks(ctx, model, img, txt, t, pe, b0, b1, nb=1):
     n_txt = txt.shape[0] // nb
     check(lib().qi_forward_blocks(ctx.h, model.h, nb, n_img, n_txt, _p(img), _p(txt), float(t), _p(pe), b0, b1,
                                   _stream()))
+
+
+def spectrum_output(ctx, model, hidden, t, H, W, nb=1, out=None):
+    """Output head on a final image hidden state [nb*n_img, 3072] FP32 -> [nb,16,H,W] bf16."""
+    if out is None:
+        out = torch.empty(nb, 16, H, W, dtype=torch.bfloat16, device=hidden.device)
+    check(lib().qi_spectrum_output(ctx.h, model.h, nb, _p(hidden), float(t), H, W, _p(out), _stream()))
+    return out
+
+
+def spectrum_weights(steps, order, lam, target, blend):
+    """Prediction weights over stored steps (increasing), as qi_spectrum_predict applies them."""
+    K = len(steps)
+    st = (ctypes.c_int * K)(*[int(v) for v in steps])
+    w = (ctypes.c_double * K)()
+    check(lib().qi_spectrum_weights(st, K, int(order), float(lam), int(target), float(blend), w))
+    return np.array(w[:], dtype=np.float64)
+
+
+class Spectrum:
+    """Feature forecaster over the states of actual forwards (SpectrumState)."""
+
+    def __init__(self, feature_elems, max_history=50, order=4, lam=0.1):
+        self.h = ctypes.c_void_p()
+        check(lib().qi_spectrum_create(int(feature_elems), int(max_history), int(order), float(lam),
+                                       ctypes.byref(self.h)))
+
+    def update(self, feature, step):
+        check(lib().qi_spectrum_update(self.h, _p(feature), int(step), _stream()))
+
+    def predict(self, target_step, blend=1.0, out=None, like=None):
+        if out is None:
+            out = torch.empty_like(like)
+        check(lib().qi_spectrum_predict(self.h, int(target_step), float(blend), _p(out), _stream()))
+        return out
+
+    def history(self):
+        return lib().qi_spectrum_history(self.h)
+
+    def reset(self):
+        check(lib().qi_spectrum_reset(self.h))
+
+    def close(self):
+        if self.h:
+            lib().qi_spectrum_destroy(self.h)
+            self.h = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 def cfg_euler_step(latent, cond, uncond, cfg_scale, sigma, sigma_next, latent_bf16):

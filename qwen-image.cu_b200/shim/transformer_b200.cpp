@@ -20,11 +20,14 @@
 // [1,16,H,W] allocation; odd H or W are zero-padded to the patch size and the
 // output cropped (transformer.cu:266-290, 915-922); the call synchronizes the
 // device before returning (:928); errors print and exit(1), the reference's
-// CUDA_CHECK convention (tensor.h:15-37).  Not supported (exit with a
-// message): calibration capture (cal != nullptr) and Spectrum hidden-state
-// capture, both outside the denoising path; use_sage_attention = false runs
-// the same SageAttention kernels (the reference's materialised-softmax
-// fallback is not rebuilt).
+// CUDA_CHECK convention (tensor.h:15-37).  spectrum_hidden_out receives the
+// final image hidden state [n_img, 3072] FP32 (qi_ctx_set_hidden_capture) and
+// transformer_spectrum_output runs the output head on such a state
+// (qi_spectrum_output), so main.cu's --spectrum schedule works unchanged.  Not
+// supported (exit with a message): calibration capture (cal != nullptr),
+// outside the denoising path; use_sage_attention = false runs the same
+// SageAttention kernels (the reference's materialised-softmax fallback is not
+// rebuilt).
 #include "transformer.h"
 
 #include <cstdio>
@@ -64,6 +67,14 @@ const void* bf16_of(const QuantizedWeight& q) {
     exit(1);
   }
   return q.data.data;
+}
+
+void ensure_ctx() {
+  if (g_ctx) return;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  int st = qi_ctx_create(dev, &g_ctx);
+  if (st != QI_OK) die("qi_ctx_create", st);
 }
 
 // Builds (or keeps) the kernel-layout model for `w`.
@@ -143,17 +154,14 @@ Tensor transformer_forward(const TransformerWeights& w, const Tensor& x_in, floa
       told = true;
     }
   }
-  if (cal || spectrum_hidden_out) {
-    fprintf(stderr, "qwen-image-b200: calibration / Spectrum capture is not supported\n");
+  if (cal) {
+    fprintf(stderr, "qwen-image-b200: calibration capture is not supported\n");
     exit(1);
   }
-  if (!g_ctx) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    int st = qi_ctx_create(dev, &g_ctx);
-    if (st != QI_OK) die("qi_ctx_create", st);
-  }
+  ensure_ctx();
   ensure_model(w);
+  int cst = qi_ctx_set_hidden_capture(g_ctx, spectrum_hidden_out);
+  if (cst != QI_OK) die("qi_ctx_set_hidden_capture", cst);
   const int H_pad = H + (H & 1), W_pad = W + (W & 1);
   const int C = static_cast<int>(x_in.shape[1]);
   const void* x = x_in.data;
@@ -186,9 +194,26 @@ Tensor transformer_forward(const TransformerWeights& w, const Tensor& x_in, floa
   return out;
 }
 
-// Spectrum step skipping (transformer.cu:939-1028) sits outside the denoising
-// path; the symbol is provided so main.cu links, and refuses to run.
-Tensor transformer_spectrum_output(const TransformerWeights&, const float*, float, int, int) {
-  fprintf(stderr, "qwen-image-b200: Spectrum output projection is not supported\n");
-  exit(1);
+// The output head on a Spectrum-predicted hidden state [n_img, 3072] FP32
+// (transformer.cu:939-1028): same padding / cropping and return convention as
+// transformer_forward.
+Tensor transformer_spectrum_output(const TransformerWeights& w, const float* hidden, float timestep, int H, int W) {
+  ensure_ctx();
+  ensure_model(w);
+  const int H_pad = H + (H & 1), W_pad = W + (W & 1);
+  Tensor out = Tensor::alloc({1, 16, H_pad, W_pad}, DType::BF16);
+  int st = qi_spectrum_output(g_ctx, g_model, 1, hidden, timestep, H_pad, W_pad, out.data, nullptr);
+  if (st != QI_OK) die("qi_spectrum_output", st);
+  if (H_pad != H || W_pad != W) {
+    Tensor cropped = Tensor::alloc({1, 16, H, W}, DType::BF16);
+    for (int c = 0; c < 16; ++c)
+      CUDA_CHECK(cudaMemcpy2D(static_cast<char*>(cropped.data) + static_cast<size_t>(c) * H * W * 2, W * 2,
+                              static_cast<const char*>(out.data) + static_cast<size_t>(c) * H_pad * W_pad * 2,
+                              W_pad * 2, W * 2, H, cudaMemcpyDeviceToDevice));
+    out = std::move(cropped);
+  }
+  CUDA_CHECK(cudaDeviceSynchronize());
+  st = qi_ctx_check(g_ctx);
+  if (st != QI_OK) die("device", st);
+  return out;
 }

@@ -15,6 +15,9 @@ Fixtures:
   rope.npz          gen_qwen_image_pe digests + one small table (rope.h:175)
   block0.npz        transformer_forward block-0 stage dumps at a tiny size
                     (the reference's DUMP_TRANSFORMER hooks, transformer.cu:352)
+  spectrum.npz      spectrum_predict on seeded histories (cuda_kernels.cu:6268)
+
+    python tests/golden/make_golden.py [out_dir] --only spectrum   (one fixture)
 """
 import glob
 import hashlib
@@ -29,6 +32,17 @@ ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__)
 sys.path.insert(0, os.path.join(ROOT, "oracle"))
 import qi_ref as R  # noqa: E402
 
+# Spectrum: (K, F, steps, target, order, lambda, blend); histories R.synth((K, F), seed).  Order
+# 4 only: the reference's spectrum_init never stores its max_order argument
+# (cuda_kernels.cu:6168-6196), so its fit always uses T_0..T_4 (SpectrumState's default), and
+# below 4 its buffers are a column short of what spectrum_predict writes.
+SPECTRUM_CASES = [
+    (2, 4096, [5, 6], 7, 4, 0.1, 1.0),
+    (6, 4096, [5, 7, 9, 11, 13, 15], 16, 4, 0.1, 1.0),
+    (12, 4096, [0, 1, 2, 3, 4, 5, 7, 9, 11, 13, 15, 17], 18, 4, 0.1, 0.5),
+    (20, 4096, list(range(5, 45, 2)), 46, 4, 0.01, 0.75),
+    (8, 4096, [10, 12, 14, 16, 18, 20, 22, 24], 23, 4, 1.0, 0.0),
+]
 ACT_CASES = [(8, 3072, 1024), (4, 12288, 4096), (3, 256, 256), (5, 3584, 512)]
 W_CASES = [(16, 3072), (8, 12288), (16, 256), (4, 64), (4, 3584)]
 SAGE_CASES = [(2, 200), (1, 77), (2, 384)]
@@ -50,9 +64,21 @@ def act_input(M, K, seed):
     return x
 
 
+def spectrum(out):
+    d = {}
+    for i, (K, F, steps, target, order, lam, blend) in enumerate(SPECTRUM_CASES):
+        hist = R.synth((K, F), R.seed_for(31, f"spectrum_{i}"), 1.0)
+        d[f"pred_{i}"] = R.spectrum_predict(hist, steps, target, blend, order, lam).cpu().numpy()
+    np.savez_compressed(os.path.join(out, "spectrum.npz"), **d)
+
+
 def main(out):
     os.makedirs(out, exist_ok=True)
     torch.cuda.set_device(0)
+    if "--only" in sys.argv and sys.argv[sys.argv.index("--only") + 1] == "spectrum":
+        spectrum(out)
+        print("wrote spectrum.npz")
+        return
     # --- activation quantizer
     d = {}
     for M, K, B in ACT_CASES:
@@ -129,8 +155,10 @@ def main(out):
     d["rows_img"] = np.array(ROWS_IMG)
     d["rows_txt"] = np.array(ROWS_TXT)
     np.savez_compressed(os.path.join(out, "block0.npz"), **d)
+    spectrum(out)
     print("wrote", sorted(os.listdir(out)))
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else os.path.dirname(os.path.abspath(__file__)))
+    args = [a for a in sys.argv[1:] if not a.startswith("--") and a != "spectrum"]
+    main(args[0] if args else os.path.dirname(os.path.abspath(__file__)))

@@ -115,3 +115,22 @@ def test_block0_stages_golden():
         assert ref.size == ours.size, (gk, ref.size, ours.size)
         cos, maxrel = O.metrics(ours, ref)
         assert cos >= 0.9998 and maxrel <= bar, (gk, cos, maxrel)
+
+
+def test_spectrum_predict_golden():
+    """The float64 restatement of the reference's Spectrum predictor against the
+    reference's own FP32 implementation (SGEMMs, Cholesky, triangular solves):
+    normwise agreement to 1e-4 of the largest predicted value."""
+    import importlib.util
+    spec = importlib.util.spec_from_file_location("make_golden", os.path.join(HERE, "make_golden.py"))
+    mg = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mg)
+    cases = mg.SPECTRUM_CASES
+    g = load("spectrum.npz")
+    for i, (K, F, steps, target, order, lam, blend) in enumerate(cases):
+        hist = O.gen_f32(seed_for(31, f"spectrum_{i}"), (K, F), 1.0)
+        ours = O.spectrum_predict(hist, steps, target, blend, order, lam)
+        ref = g[f"pred_{i}"].astype(np.float64)
+        err = np.abs(ours - ref).max() / np.abs(ref).max()
+        assert err < 1e-4, (i, err)
+
