@@ -2,7 +2,7 @@
 CUDA events on the launching stream).  Also the target of the ncu captures
 summarised in profiles/.
 
-    python qwen-image.cu_b200/kernel_bench.py [--which gemm,attn,quant,peaks] [--iters N] [--config c4|c2]
+    python qwen-image.cu_b200/kernel_bench.py [--which gemm,attn,quant,spectrum,peaks] [--iters N] [--config c4|c2]
                                               [--gpus 1|2|4|8]
 
 GEMM shapes are those of one CFG-batched C4 forward (M = 2 x 6889 image +
@@ -13,6 +13,8 @@ GEMM shapes are those of one CFG-batched C4 forward (M = 2 x 6889 image +
 separate ranks (batch 1) and 24 / (N / 2) heads, (6889 + 256) / (N / 2) rows.
 Quantizers: LayerNorm-modulate + FWHT-1024 (K 3072), the attention output
 (FP16, K 3072) and the MLP hidden (FWHT-4096, K 12288) at the C4 rows.
+`spectrum`: a skipped Spectrum step at C4 (prediction from 28 stored states,
+then the output head).
 `peaks`: the dense tensor-core rates of this GPU through the libraries
 (torch._int_mm INT8 -> INT32, torch.matmul FP16 and BF16 at 8192^3), as a
 burst (best of 10) and sustained (back to back for 4 s); the roofline
@@ -114,6 +116,30 @@ def bench_quant(iters, res):
     res["ln_mod_quant_3072"] = {"M": M, "K": 3072, "ms": round(ms, 4), "gbs": round(gbs, 1)}
 
 
+def bench_spectrum(iters, res, K=28):
+    """Spectrum at C4 (one CFG half): prediction from K stored states (a 50-step
+    run with 5 warm-up steps and window 2 keeps ~28) and the output head; the
+    two together are a skipped step's cost, against a forward for an actual one."""
+    n_img, F = 83 * 83, 83 * 83 * 3072
+    hidden = Q.synth((n_img, 3072), 41, 1.0)
+    sp = Q.Spectrum(F, max_history=50, order=4, lam=0.1)
+    for k in range(K):
+        sp.update(hidden, 5 + 2 * k)
+    out = torch.empty_like(hidden)
+    ms_p = time_it(lambda: sp.predict(5 + 2 * K, 1.0, out=out), iters)
+    res["spectrum_predict"] = {"K": K, "F": F, "ms": round(ms_p, 4),
+                               "gbs": round((K + 1) * F * 4 / (ms_p * 1e-3) / 1e9, 1)}
+    ctx = Q.Context(0)
+    g, blocks = Q.make_weight_table(1, base_seed=0)
+    model = Q.Model(ctx, g, blocks)
+    v = torch.empty(1, 16, 166, 166, dtype=torch.bfloat16, device="cuda")
+    ms_h = time_it(lambda: Q.spectrum_output(ctx, model, out, 500.0, 166, 166, out=v), iters)
+    res["spectrum_output_head"] = {"n_img": n_img, "ms": round(ms_h, 4)}
+    sp.close()
+    model.close()
+    ctx.close()
+
+
 def bench_peaks(res, seconds=4.0):
     n = 8192
     flops = 2.0 * n ** 3
@@ -160,6 +186,8 @@ def main():
         bench_attn(a.iters, res, a.config, a.gpus)
     if "quant" in w:
         bench_quant(a.iters, res)
+    if "spectrum" in w:
+        bench_spectrum(a.iters, res)
     if "peaks" in w:
         bench_peaks(res)
     print(json.dumps(res))
