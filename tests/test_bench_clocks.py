@@ -38,7 +38,7 @@ def test_clock_sampler_reads_reasons(monkeypatch):
     monkeypatch.setitem(sys.modules, "pynvml", _fake_nvml(0x4 | 0x40, calls))
     monkeypatch.syspath_prepend(ROOT)
     bench = importlib.import_module("bench")
-    with bench.ClockSampler(0) as clk:
+    with bench.ClockSampler(0, period_s=0.01) as clk:
         time.sleep(0.1)
     s = clk.summary()
     assert s["source"] == "nvml"
@@ -53,7 +53,7 @@ def test_clock_sampler_without_reasons(monkeypatch):
     monkeypatch.setitem(sys.modules, "pynvml", _fake_nvml(0, calls))
     monkeypatch.syspath_prepend(ROOT)
     bench = importlib.import_module("bench")
-    with bench.ClockSampler(0) as clk:
+    with bench.ClockSampler(0, period_s=0.01) as clk:
         time.sleep(0.05)
     s = clk.summary()
     assert s["reasons"] == [] and s["samples"] >= 1
