@@ -615,6 +615,106 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def _time_ms(fn, iters=5, warmup=2):
+    for _ in range(warmup):
+        fn()
+    s = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    for _ in range(iters):
+        fn()
+    e1.record(s)
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / iters
+
+
+def reference_kernels(args):
+    """The reference's own kernels on this GPU, beside ours on the same inputs and
+    shapes (`--impl reference --kernels`): its SageAttention kernel alone
+    (attention_forward_sage_sm80_fp16io) at the Sage microbenchmark (C2) and the
+    C4 joint sequence; its INT8 linear on pre-quantized inputs (cuBLAS INT8 +
+    dequant / GELU, linear_forward_int8_prequantized) at the C4 block shapes;
+    its whole forward with the default materialised-softmax attention at C4;
+    and its own per-stage split of the Sage forward (the PROFILE_BLOCK hook,
+    transformer.cu:486-860, read from a child process's log)."""
+    rank, world, local = dist_env()
+    if rank != 0:
+        return
+    torch.cuda.set_device(local)
+    import qi_ref as R
+    import qib200 as Q
+    if not R.available():
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libqiref.so (reference build) missing"}))
+        return
+    res = {"impl": "reference", "mode": "kernels", "attention": {}, "linear_int8_preq": {}}
+    for name, S in (("c2", 4352), ("c4", S_JOINT)):
+        BH = 48
+        q, k, v = (R.synth((BH, S, 128), R.seed_for(110, f"{n}_{S}"), 1.0).half() for n in "qkv")
+        flops = 4.0 * BH * S * S * 128
+        ms_ref = _time_ms(lambda: R.sage_attention(q, k, v, 1.0 / 128 ** 0.5))
+        ms_our = _time_ms(lambda: Q.sage_attention(q, k, v))
+        res["attention"][name] = {"BH": BH, "S": S, "reference_ms": round(ms_ref, 4), "ours_ms": round(ms_our, 4),
+                                  "reference_tflops": round(flops / ms_ref / 1e9, 1),
+                                  "ours_tflops": round(flops / ms_our / 1e9, 1)}
+        del q, k, v
+    M = 2 * N_IMG + 2 * N_TXT
+    for name, N, K, gelu in (("qkv", 3 * DIM, DIM, False), ("out", DIM, DIM, False), ("fc1", MLP, DIM, True),
+                             ("fc2", DIM, MLP, False)):
+        a = torch.randint(-127, 128, (M, K), dtype=torch.int8, device="cuda")
+        w = torch.randint(-127, 128, (N, K), dtype=torch.int8, device="cuda")
+        sa = torch.rand(M, device="cuda") * 1e-3
+        sw = torch.rand(N, device="cuda") * 1e-3
+        b = torch.zeros(N, dtype=torch.bfloat16, device="cuda")
+        out = torch.empty(M, N, device="cuda")
+        ms_ref = _time_ms(lambda: R.linear_int8_preq(a, sa, w, sw, b, gelu))
+        ms_our = _time_ms(lambda: Q.linear_i8(a, sa, w, sw, b, Q.EPI_GELU if gelu else Q.EPI_STORE, out=out))
+        ops = 2.0 * M * N * K
+        res["linear_int8_preq"][name] = {"M": M, "N": N, "K": K, "reference_ms": round(ms_ref, 4),
+                                         "ours_ms": round(ms_our, 4), "reference_tops": round(ops / ms_ref / 1e9, 1),
+                                         "ours_tops": round(ops / ms_our / 1e9, 1)}
+        del a, w, out
+    g, blocks = R.make_table(BLOCKS, distinct=BLOCKS)
+    garr, _, bt = R.table_pointers(g, blocks)
+    x = R.synth((1, 16, H_LAT, W_LAT), R.seed_for(100, "noise"), 1.0).to(torch.bfloat16)
+    ctx0 = R.synth((1, N_TXT, 3584), R.seed_for(100, "context_0"), 1.0, dtype=torch.bfloat16)
+    pe = torch.from_numpy(R.rope_table(H_LAT, W_LAT, N_TXT)).cuda()
+    for sage in (True, False):
+        ms = _time_ms(lambda: R.transformer_forward(garr, bt, x, 500.0, ctx0, pe, H_LAT, W_LAT, sage=sage), 2, 1)
+        res["forward_sage" if sage else "forward_default_attention"] = {"ms_per_forward": round(ms, 2)}
+    del g, blocks
+    torch.cuda.empty_cache()
+    env = dict(os.environ, PROFILE_BLOCK="1", QWEN_VERBOSE="1")
+    r = subprocess.run([sys.executable, os.path.abspath(__file__), "--impl", "reference", "--profile-block"],
+                       env=env, capture_output=True, text=True, timeout=900)
+    split, on = {}, False
+    for line in r.stderr.splitlines():
+        if "Block Loop Profile" in line:
+            split, on = {}, True
+        elif on and line.strip().startswith("===="):
+            on = False
+        elif on and ":" in line and "ms" in line:
+            key, rest = line.split(":", 1)
+            split[key.strip()] = float(rest.split("ms")[0])
+    res["reference_stage_split_ms"] = split or {"unavailable": (r.stderr or "")[-300:]}
+    print(json.dumps(res), flush=True)
+
+
+def reference_profile_child():
+    """One Sage forward of the reference at the bench workload, run with the
+    reference's PROFILE_BLOCK hook on (per-stage events, each synchronised);
+    the parent reads the printed split."""
+    torch.cuda.set_device(0)
+    import qi_ref as R
+    g, blocks = R.make_table(BLOCKS, distinct=BLOCKS)
+    garr, _, bt = R.table_pointers(g, blocks)
+    x = R.synth((1, 16, H_LAT, W_LAT), R.seed_for(100, "noise"), 1.0).to(torch.bfloat16)
+    ctx0 = R.synth((1, N_TXT, 3584), R.seed_for(100, "context_0"), 1.0, dtype=torch.bfloat16)
+    pe = torch.from_numpy(R.rope_table(H_LAT, W_LAT, N_TXT)).cuda()
+    for _ in range(2):  # the second forward's split is the one kept
+        R.transformer_forward(garr, bt, x, 500.0, ctx0, pe, H_LAT, W_LAT, sage=True)
+    torch.cuda.synchronize()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -625,6 +725,10 @@ def main():
     ap.add_argument("--loader", action="store_true",
                     help="time the checkpoint loader against the reference's instead of the step")
     ap.add_argument("--loader-blocks", type=int, default=8, help="blocks in the --loader checkpoint")
+    ap.add_argument("--kernels", action="store_true",
+                    help="with --impl reference: the reference's kernels beside ours (attention, INT8 linear, "
+                         "default-attention forward, the reference's per-stage split)")
+    ap.add_argument("--profile-block", action="store_true", help=argparse.SUPPRESS)
     ap.add_argument("--workload", default="c4", choices=["c4", "c5"],
                     help="c4: 1328x1328 (the headline metric); c5: 2048x2048, 20 steps (scaling study)")
     args = ap.parse_args()
@@ -637,8 +741,12 @@ def main():
     if args.warmup < 3:
         print("warmup < 3 is not a valid measurement; using 3", file=sys.stderr)
         args.warmup = 3
-    if args.loader:
+    if args.profile_block:
+        reference_profile_child()
+    elif args.loader:
         run_loader(args)
+    elif args.impl == "reference" and args.kernels:
+        reference_kernels(args)
     elif args.impl == "reference":
         run_reference(args)
     else:
