@@ -190,7 +190,8 @@ __global__ void __launch_bounds__(attn::THREADS, 1) sage_attn_kernel(const __gri
   uint64_t* s_full = v_empty + STAGES;        // [NT] QK of the tile's current block complete
   uint64_t* p_half = s_full + NT;             // [NT][2] half h of the tile's P written to TMEM (4 warps)
   uint64_t* o_final = p_half + 2 * NT;        // [NT] the tile's last PV complete (single use)
-  uint64_t* drain = o_final + NT;             // MMA teardown
+  uint64_t* s_loaded = o_final + NT;          // [NT] the tile's S of the current block is in registers (4 warps)
+  uint64_t* drain = s_loaded + NT;            // MMA teardown
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(drain + 2);
 
@@ -213,6 +214,7 @@ __global__ void __launch_bounds__(attn::THREADS, 1) sage_attn_kernel(const __gri
       mbar_init(&p_half[2 * t], 4);
       mbar_init(&p_half[2 * t + 1], 4);
       mbar_init(&o_final[t], 1);
+      mbar_init(&s_loaded[t], 4);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -299,6 +301,18 @@ __global__ void __launch_bounds__(attn::THREADS, 1) sage_attn_kernel(const __gri
           for (int k = 0; k < D / 32; ++k) mma_i8_ss_elect(d, qa + 2 * k, kb + 2 * k, id_qk, k > 0 ? 1u : 0u);
           mma_commit_elect(&s_full[t]);
         };
+        // Keys 64 hh .. 64 hh + 63 of that product into S_t columns 64 hh ..: the
+        // upper half (columns 64-127) never holds P, so it is issued as soon as the
+        // softmax has read S_t of the previous block; only the lower half waits
+        // for P_t . V to have read P_t.
+        const uint32_t id_qk64 = idesc_i8(BQ, 64);
+        auto qk_half = [&](int t, int st, int hh) {
+          const uint64_t qa = qd0 + static_cast<uint64_t>(t * (Q_BYTES >> 4));
+          const uint64_t kb = kd0 + static_cast<uint64_t>((st * K_BYTES + hh * (K_BYTES / 2)) >> 4);
+          const uint32_t d = tmem + TM_S + 128 * t + 64 * hh;
+  #pragma unroll
+          for (int k = 0; k < D / 32; ++k) mma_i8_ss_elect(d, qa + 2 * k, kb + 2 * k, id_qk64, k > 0 ? 1u : 0u);
+        };
         // O_t += P_t . V over keys 64h .. 64h+63 of the block in stage st; P_t is read from TMEM
         auto pv_half = [&](int t, int st, int j, int h) {
           const uint64_t vb = vd0 + static_cast<uint64_t>((st * V_BYTES) >> 4);
@@ -329,6 +343,12 @@ __global__ void __launch_bounds__(attn::THREADS, 1) sage_attn_kernel(const __gri
           const uint32_t ph = (j / STAGES) & 1, nph = ((j + 1) / STAGES) & 1;
           const bool more = j + 1 < nkb;
           for (int t = 0; t < NT && ok; ++t) {
+            if (more) {  // upper half of S_t for block j + 1, once S_t of block j is read
+              if (!wait_all(&s_loaded[t], j & 1)) { ok = false; break; }
+              if (t == 0 && !wait_all(&k_full[nst], nph)) { ok = false; break; }
+              tc_fence_after();
+              qk_half(t, nst, 1);
+            }
             // each half of P_t . V starts as soon as that half of P_t is in TMEM
             if (!wait_all(&p_half[2 * t], j & 1)) { ok = false; break; }
             if (t == 0 && !wait_all(&v_full[st], ph)) { ok = false; break; }
@@ -340,12 +360,12 @@ __global__ void __launch_bounds__(attn::THREADS, 1) sage_attn_kernel(const __gri
             if (j == nkb - 1) mma_commit_elect(&o_final[t]);
             if (t == NT - 1) mma_commit_elect(&v_empty[st]);
             if (more) {
-              if (t == 0 && !wait_all(&k_full[nst], nph)) { ok = false; break; }
-              // QK(j+1) overwrites the S_t / P_t columns that P_t . V of block j
-              // reads; the tensor pipe runs one CTA's MMAs in issue order, so it
-              // is issued right behind it.
-              tc_fence_after();
-              qk(t, nst);
+              // the lower half of QK(j+1) overwrites the S_t / P_t columns that
+              // P_t . V of block j reads; the tensor pipe runs one CTA's MMAs in
+              // issue order, so it is issued right behind it.  The commit covers
+              // both halves.
+              qk_half(t, nst, 0);
+              mma_commit_elect(&s_full[t]);
               if (t == NT - 1) mma_commit_elect(&k_empty[nst]);
             }
           }
@@ -399,6 +419,10 @@ __global__ void __launch_bounds__(attn::THREADS, 1) sage_attn_kernel(const __gri
       tmem_ld_wait();
 #pragma unroll
       for (int q = 0; q < BKV / 32; ++q) tmem_reg_fence32(*reinterpret_cast<uint32_t(*)[32]>(r + 32 * q));
+      // S_t is in registers: the MMA warp may overwrite its columns 64-127
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s_loaded[t]);
       const bool tail = (j + 1) * BKV > S;  // last block reaches past the sequence end
       if (tail) {
 #pragma unroll
