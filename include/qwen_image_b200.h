@@ -169,6 +169,21 @@ int qi_layer_norm_modulate_quantize(const float* x, const float* shift, const fl
 int qi_qk_norm_rope(const float* qkv_img, const float* qkv_txt, const void* norms_bf16, const float* pe, int nb,
                     int n_img, int n_txt, void* qkv_f16, void* stream);
 
+/* The QKV projections of both streams with qi_qk_norm_rope's arithmetic in
+ * the GEMM epilogue (the forward's fused form): act_img [nb*n_img, 3072] and
+ * act_txt [nb*n_txt, 3072] INT8 codes with per-row scales (as
+ * qi_layer_norm_modulate_quantize gives them), w_img / w_txt [9216, 3072]
+ * INT8 [q | k | v] rows with per-row scales and BF16 biases (or NULL);
+ * norms_bf16, pe and the output as for qi_qk_norm_rope.  Bit-identical to
+ * qi_linear_i8 (epilogue 0) of each stream followed by qi_qk_norm_rope, with
+ * no FP32 projection in memory.  Needs at least 512 rows in all
+ * (QI_ERR_UNSUPPORTED below).  Replaces linear_forward_int8_prequantized x 6
+ * and the qkv_post chain of transformer.cu:568-671.                         */
+int qi_qkv_norm_rope_i8(const int8_t* act_img, const float* act_img_scales, const int8_t* act_txt,
+                        const float* act_txt_scales, const int8_t* w_img, const float* w_img_scales, const void* b_img,
+                        const int8_t* w_txt, const float* w_txt_scales, const void* b_txt, const void* norms_bf16,
+                        const float* pe, int nb, int n_img, int n_txt, void* qkv_f16, void* stream);
+
 /* ------------------------------------------------------------ model level */
 typedef struct qi_ctx qi_ctx;
 typedef struct qi_model qi_model;
@@ -186,6 +201,14 @@ int qi_ctx_check(qi_ctx* ctx);
  * reference launches (0, the default).  Off the reference's numerics: its
  * outputs are checked against exact attention, not against the reference.   */
 int qi_ctx_set_attention_fp8pv(qi_ctx* ctx, int enable);
+
+/* Where qi_forward / qi_forward_blocks apply the q/k RMSNorm, RoPE and FP16
+ * head-major layout of each block (transformer.cu:637-666): in the epilogue
+ * of the QKV projection, so the FP32 projection never reaches HBM
+ * (enable != 0, the default), or as a separate kernel after an FP32
+ * projection (0).  Both give the same bits; the fused form needs the CTA-pair
+ * GEMM (at least 512 rows), and shorter inputs take the separate kernel.    */
+int qi_ctx_set_fused_qkv_epilogue(qi_ctx* ctx, int enable);
 
 /* Head-parallel (Ulysses) group.  New: the reference runs on one GPU
  * (its main.cu:761-773 calls transformer_forward for cond and uncond in

@@ -109,6 +109,7 @@ struct qi_ctx {
   int urank = 0, usize = 1;
   bool comm_failed = false;   // the group's communicator was aborted; multi-GPU calls fail
   bool attn_fp8 = false;      // forward attention: FP8 P.V variant (qi_ctx_set_attention_fp8pv)
+  bool qkv_fused = true;      // q/k norm + RoPE in the QKV GEMM's epilogue (qi_ctx_set_fused_qkv_epilogue)
   int comm_timeout_ms = 60000;  // deadline of every collective step (qi_ctx_set_comm_timeout)
   // direct exchanges over peer memory: the group's buffers mapped here (CUDA
   // IPC), set up for one forward shape (peer_key) at a time
@@ -320,6 +321,12 @@ int qi_ctx_destroy(qi_ctx* c) {
 int qi_ctx_set_attention_fp8pv(qi_ctx* c, int enable) {
   if (!c) return QI_ERR_ARG;
   c->attn_fp8 = enable != 0;
+  return QI_OK;
+}
+
+int qi_ctx_set_fused_qkv_epilogue(qi_ctx* c, int enable) {
+  if (!c) return QI_ERR_ARG;
+  c->qkv_fused = enable != 0;
   return QI_OK;
 }
 
@@ -588,6 +595,27 @@ int qi_qk_norm_rope(const float* qkv_img, const float* qkv_txt, const void* norm
   QkvPostArgs a{qkv_img, qkv_txt, n, n + kHeadDim, n + 2 * kHeadDim, n + 3 * kHeadDim, pe, qkv_f16, nb, n_img, n_txt,
                 0, n_img, 0, n_txt, kHeads, 0};
   return qkv_post_launch(a, S_(stream));
+}
+
+int qi_qkv_norm_rope_i8(const int8_t* act_img, const float* act_img_scales, const int8_t* act_txt,
+                        const float* act_txt_scales, const int8_t* w_img, const float* w_img_scales, const void* b_img,
+                        const int8_t* w_txt, const float* w_txt_scales, const void* b_txt, const void* norms_bf16,
+                        const float* pe, int nb, int n_img, int n_txt, void* qkv_f16, void* stream) {
+  if (!act_img || !act_img_scales || !act_txt || !act_txt_scales || !w_img || !w_img_scales || !w_txt ||
+      !w_txt_scales || !norms_bf16 || !pe || !qkv_f16 || nb < 1 || n_img < 0 || n_txt < 0)
+    return QI_ERR_ARG;
+  if ((reinterpret_cast<uintptr_t>(pe) | reinterpret_cast<uintptr_t>(qkv_f16)) & 15) return QI_ERR_ALIGN;
+  qi_ctx* c = default_ctx();
+  if (!c) return QI_ERR_CUDA;
+  const __nv_bfloat16* n = static_cast<const __nv_bfloat16*>(norms_bf16);
+  QkvPostArgs a{nullptr, nullptr, n, n + kHeadDim, n + 2 * kHeadDim, n + 3 * kHeadDim, pe, qkv_f16, nb, n_img, n_txt,
+                0, n_img, 0, n_txt, kHeads, 0};
+  GemmDesc d[2] = {{act_img, act_img_scales, w_img, w_img_scales, b_img, nullptr, nullptr, nb * n_img, 3 * kDim, kDim,
+                    3 * kDim},
+                   {act_txt, act_txt_scales, w_txt, w_txt_scales, b_txt, nullptr, nullptr, nb * n_txt, 3 * kDim, kDim,
+                    3 * kDim}};
+  if (!gemm_qkv_fusable(d, 2, c->num_sms)) return QI_ERR_UNSUPPORTED;
+  return gemm_qkv_launch(d, 2, a, S_(stream), c->err, c->num_sms);
 }
 
 int qi_rope_table(int h, int w, int n_txt, float* pe_host) {
@@ -1072,7 +1100,6 @@ int fwd_blocks(Fwd& f, float* x_img, float* x_txt, const float* pe, int b0, int 
                        kDim, 3 * kDim},
                       {act + Mi * kDim, act_s + Mi, B.qkv[1].w, B.qkv[1].s, B.qkv[1].b, qkv + Mi * 3 * kDim, nullptr,
                        static_cast<int>(Mt), 3 * kDim, kDim, 3 * kDim}};
-    QI_LAUNCH(QI_PROF_GEMM_QKV, 1, gemm_i8_launch(gq, 2, kEpiStore, s, c->err, c->num_sms));
     const bool par = f.P > 1, direct = par && f.direct;
     __half* qkvh = c->p<__half>(B_QKVH);
     const size_t hs = static_cast<size_t>(BH) * S * kHeadDim;
@@ -1081,7 +1108,13 @@ int fwd_blocks(Fwd& f, float* x_img, float* x_txt, const float* pe, int b0, int 
                    f.txt_lo, f.n_txt_l, f.Hl, direct ? 1 : 0};
     if (direct)
       for (int q = 0; q < f.P; ++q) qa.peer_qkvh[q] = c->peers.qkvh[q];
-    QI_LAUNCH(QI_PROF_QKV_POST, 1, qkv_post_launch(qa, s));
+    if (c->qkv_fused && gemm_qkv_fusable(gq, 2, c->num_sms)) {
+      // q/k RMSNorm + RoPE + FP16 head-major store in the projection's epilogue
+      QI_LAUNCH(QI_PROF_GEMM_QKV, 1, gemm_qkv_launch(gq, 2, qa, s, c->err, c->num_sms));
+    } else {
+      QI_LAUNCH(QI_PROF_GEMM_QKV, 1, gemm_i8_launch(gq, 2, kEpiStore, s, c->err, c->num_sms));
+      QI_LAUNCH(QI_PROF_QKV_POST, 1, qkv_post_launch(qa, s));
+    }
     if (direct) {  // every rank has stored its rows of this rank's heads
       QI_LAUNCH(QI_PROF_EXCHANGE, 1, peer_barrier_launch(c->peers, 0, ++c->epoch, c->err, s));
     } else if (par) {  // every token of this rank's heads

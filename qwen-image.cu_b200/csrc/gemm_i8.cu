@@ -66,6 +66,8 @@ struct alignas(64) GemmArgsDev {
   // used once or by the tiles running at the same time), so the weight panels
   // that every row block re-reads stay in L2; 2 also the weights evict_last
   int l2;
+  QkvPostArgs qp;  // kEpiQkv: qkv_post's parameters (its qkv_img / qkv_txt unused)
+  CUtensorMap tmPE;  // kEpiQkv: the RoPE table [nb * S][256] FP32, 32 x 32 boxes, 128-byte swizzle
 };
 
 __device__ __forceinline__ float gelu_tanh_dev(float v) {
@@ -79,6 +81,10 @@ __device__ __forceinline__ float gelu_tanh_dev(float v) {
 struct EpiState {
   uint32_t xphase = 0;    // parity bit per staging buffer
   uint32_t xpending = 0;  // buffers with a residual load issued and not yet waited
+  // kEpiQkv's RoPE-row ring (the filling warp): parity of the next "slot
+  // empty" completion per slot, and the slots filled at least once
+  uint32_t ephase = 0;
+  uint32_t eused = 0;
 };
 
 // One accumulator tile: this warp's 32 rows (TMEM lane quarter) of the 128
@@ -224,10 +230,10 @@ __device__ __forceinline__ bool epilogue_tile(const GemmArgsDev& args, const Gem
 }
 
 // Stores finished and an abandoned residual load landed before the CTA exits.
-__device__ __forceinline__ void epilogue_drain(const EpiState& es, uint64_t* xb, int lane) {
+__device__ __forceinline__ void epilogue_drain(const EpiState& es, uint64_t* xb, int lane, int nbars = 2) {
   if (lane == 0) {
     bulk_wait<0>();
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < nbars; ++b) {
       if (!(es.xpending & (1u << b))) continue;
       const uint64_t t0 = global_timer_ns();
       while (!mbar_try_wait(&xb[b], (es.xphase >> b) & 1) && global_timer_ns() - t0 < kWaitLimitNs / 4) {
@@ -443,6 +449,238 @@ __global__ void __launch_bounds__(gemm::THREADS, 1) gemm_kernel(const __grid_con
   }
 }
 
+// ------------------------------------------------------------------ fused q/k/v post
+// kEpiQkv: one head of the QKV projection for this warp's 32 rows.  With
+// N = 3 x 3072 and 256-column tiles, tile columns [c0, c0 + 128) are head h
+// of Q, K or V.  The arithmetic is qkv_post_kernel's (glue.cu) applied to the
+// values epilogue_tile would have stored:
+//   * dequant + bias per 32-column chunk (epilogue_tile's expressions);
+//   * Q and K: the sum of squares in the order of rms_norm_fp32_kernel's
+//     reduction (cuda_kernels.cu:1656-1688: thread t = element t, each square
+//     rounded, shfl_down 16..1 within each warp of 32 elements, then warp 0
+//     over the 4 warp sums, i.e. (w0 + w2) + (w1 + w3)), then
+//     rsqrt(ss / 128 + eps), x * rms * w and RoPE on interleaved pairs
+//     (rope_apply_fp32_to_fp16_kernel, :1935-1963);
+//   * V: only rounded to FP16.
+// A first pass over TMEM gives the sum of squares. A second pass recomputes
+// the same dequantised values chunk by chunk, so at most one 32-column chunk
+// sits in registers.  The RoPE rows of the 32 rows (16 pairs x 16 bytes per
+// row and chunk) come by TMA, as two 32-row x 128-byte boxes with 128-byte
+// swizzle, into an NS-slot ring (8 KB per slot) shared by the two warps of
+// this TMEM lane quarter (the same 32 rows, the tile's two heads): full[s]
+// completes when a chunk has landed in slot s and empty[s] when both warps
+// have read it.  The half-0 warp fills chunks 0 .. NS - 1 before it waits for
+// the accumulator, and chunk c + NS once chunk c is read, so the copies run
+// under the first pass and the earlier chunks.  A slab whose rows straddle
+// a batch entry (its table rows are not consecutive) reads the rows per lane
+// instead; the values are the same.
+// Each chunk's FP16 output goes through a 2 KB per-warp staging buffer, so a
+// store instruction writes eight rows' 64 contiguous bytes, to this rank's
+// Q/K/V buffer or, direct, the head owner's (peer memory), addressed as in
+// qkv_post_kernel.
+template <int NS>
+__device__ __forceinline__ bool epilogue_qkv(const GemmArgsDev& args, const GemmProblemDev& P, int pi, int row0,
+                                             int c0, uint32_t tmem_col, int buf, uint32_t acc_phase,
+                                             uint32_t tmem_base, uint8_t* ring, uint64_t* full, uint64_t* empty,
+                                             bool filler, uint8_t* obuf, uint64_t* tfull, EpiState& es,
+                                             uint32_t tempty_addr, volatile int* abort_flag, int quarter, int lane) {
+  static_assert(NS >= 2 && NS <= 4, "ring slots");
+  const QkvPostArgs& q = args.qp;
+  const int r0 = row0 + quarter * 32;  // first output row of this warp
+  // the accumulator buffer is handed back as soon as it has been read
+  auto release = [&]() {
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive_cluster(tempty_addr);
+  };
+  const int which = c0 / kDim, h = (c0 % kDim) / kHeadDim;  // which: 0 Q, 1 K, 2 V
+  const int S = q.n_img + q.n_txt, L = q.n_img_l + q.n_txt_l;
+  const int n_l = pi == 0 ? q.n_img_l : q.n_txt_l;              // rows per batch entry
+  const int base = pi == 0 ? q.n_txt + q.img_lo : q.txt_lo;     // joint position of local row 0
+  // the RoPE rows of a slab in one batch entry are consecutive table rows
+  const int r_last = min(r0 + 31, P.M - 1);
+  const bool tma_pe = which < 2 && r0 < P.M && r0 / n_l == r_last / n_l;
+  const int pe_row0 = tma_pe ? (r0 / n_l) * S + base + r0 % n_l : 0;
+  const uint64_t pol_out = l2_policy_evict_first(), pol_pe = l2_policy_evict_last();
+  // chunk c's 16 pairs of the 32 rows (floats 64c .. 64c + 63) into slot c % NS,
+  // once both warps have read what the slot held (filler warp only)
+  auto fill = [&](int c) -> bool {
+    const int sl = c % NS;
+    if (es.eused & (1u << sl)) {
+      const bool ok_e = mbar_wait(&empty[sl], (es.ephase >> sl) & 1u, abort_flag);
+      if (!__all_sync(0xffffffffu, ok_e)) return false;
+      es.ephase ^= 1u << sl;
+    }
+    es.eused |= 1u << sl;
+    if (lane == 0) {
+      uint8_t* dstb = ring + sl * 8192;
+      fence_proxy_async_smem();  // the lanes' reads of the slot's previous chunk come first
+      mbar_expect_tx(&full[sl], 8192);
+      tma_load_2d_hint(dstb, &args.tmPE, 64 * c, pe_row0, &full[sl], pol_pe);
+      tma_load_2d_hint(dstb + 4096, &args.tmPE, 64 * c + 32, pe_row0, &full[sl], pol_pe);
+      es.xpending |= 1u << sl;
+    }
+    return true;
+  };
+  if (tma_pe && filler) {
+    for (int c = 0; c < NS; ++c)
+      if (!fill(c)) return false;
+  }
+  bool w = mbar_wait(&tfull[buf], acc_phase, abort_flag);
+  if (!__all_sync(0xffffffffu, w)) return false;
+  tc_fence_after();
+  if (r0 >= P.M) {  // the whole 32-row slab is past M (all lanes agree)
+    release();
+    return true;
+  }
+  const int grow = r0 + lane;
+  const bool valid = grow < P.M;
+  const float sa = valid ? __ldg(P.sa + grow) : 0.0f;
+  const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + tmem_col;
+  auto dequant = [&](const uint32_t (&acc)[32], int gcol, float (&v)[32]) {
+    const float4* sw4 = reinterpret_cast<const float4*>(P.sw + gcol);
+#pragma unroll
+    for (int j = 0; j < 32; j += 4) {
+      const float4 ws = __ldg(sw4 + j / 4);
+      v[j + 0] = static_cast<float>(static_cast<int32_t>(acc[j + 0])) * sa * ws.x;
+      v[j + 1] = static_cast<float>(static_cast<int32_t>(acc[j + 1])) * sa * ws.y;
+      v[j + 2] = static_cast<float>(static_cast<int32_t>(acc[j + 2])) * sa * ws.z;
+      v[j + 3] = static_cast<float>(static_cast<int32_t>(acc[j + 3])) * sa * ws.w;
+    }
+    if (P.bias) {
+      const __nv_bfloat162* b2 = reinterpret_cast<const __nv_bfloat162*>(P.bias + gcol);
+#pragma unroll
+      for (int j = 0; j < 32; j += 2) {
+        const float2 bb = __bfloat1622float2(b2[j / 2]);
+        v[j] += bb.x;
+        v[j + 1] += bb.y;
+      }
+    }
+  };
+  auto load_chunk = [&](int c, uint32_t (&acc)[32]) {
+    tmem_ld32(taddr + 32 * c, acc);
+    tmem_ld_wait();
+    tmem_reg_fence32(acc);
+  };
+  // this lane's row: batch entry, joint and local position, destination
+  int b = 0, pos = 0, lpos = 0;
+  if (valid) {
+    b = grow / n_l;
+    const int i = grow % n_l;
+    pos = base + i;
+    lpos = (pi == 0 ? q.n_txt_l : 0) + i;
+  }
+  const int dest = h / q.Hl, hh = h % q.Hl;
+  __half* dst = nullptr;
+  if (valid) {
+    if (q.direct) {
+      const size_t slab = static_cast<size_t>(q.nb) * q.Hl * S * kHeadDim;
+      dst = reinterpret_cast<__half*>(q.peer_qkvh[dest]) + which * slab +
+            ((static_cast<size_t>(b) * q.Hl + hh) * S + pos) * kHeadDim;
+    } else {
+      const size_t slab = static_cast<size_t>(q.nb) * q.Hl * L * kHeadDim;
+      dst = reinterpret_cast<__half*>(q.qkvh) + (static_cast<size_t>(dest) * 3 + which) * slab +
+            ((static_cast<size_t>(b) * q.Hl + hh) * L + lpos) * kHeadDim;
+    }
+  }
+  float rms = 0.0f;
+  const __nv_bfloat16* nw = nullptr;
+  if (which < 2) {
+    nw = reinterpret_cast<const __nv_bfloat16*>(pi == 0 ? (which == 0 ? q.nq_img : q.nk_img)
+                                                        : (which == 0 ? q.nq_txt : q.nk_txt));
+    float ws0 = 0.0f, ws1 = 0.0f, ws2 = 0.0f, ws3 = 0.0f;  // the 4 warp sums
+#pragma unroll 1
+    for (int c = 0; c < 4; ++c) {
+      uint32_t acc[32];
+      float v[32];
+      load_chunk(c, acc);
+      dequant(acc, c0 + 32 * c, v);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] = __fmul_rn(v[i], v[i]);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+#pragma unroll
+        for (int i = 0; i < o; ++i) v[i] = __fadd_rn(v[i], v[i + o]);
+      }
+      ws0 = c == 0 ? v[0] : ws0;
+      ws1 = c == 1 ? v[0] : ws1;
+      ws2 = c == 2 ? v[0] : ws2;
+      ws3 = c == 3 ? v[0] : ws3;
+    }
+    const float ss = __fadd_rn(__fadd_rn(ws0, ws2), __fadd_rn(ws1, ws3));
+    rms = rsqrtf(ss / q.norm_dim + q.eps);
+  }
+  const float* pe_lane = q.pe + (valid ? (static_cast<long long>(b) * S + pos) * 256 : 0);
+#pragma unroll 1
+  for (int c = 0; c < 4; ++c) {
+    uint32_t acc[32];
+    float v[32];
+    load_chunk(c, acc);
+    if (c == 3) release();
+    dequant(acc, c0 + 32 * c, v);
+    uint32_t pk[16];
+    if (which < 2) {
+      const int sl = c % NS;
+      const uint8_t* slot = ring + sl * 8192;
+      if (tma_pe) {
+        const bool ok_pe = mbar_wait(&full[sl], (es.xphase >> sl) & 1u, abort_flag);
+        if (!__all_sync(0xffffffffu, ok_pe)) return false;  // still pending: the exit drain waits for it
+        es.xphase ^= 1u << sl;
+        es.xpending &= ~(1u << sl);
+      }
+      // pairs 16c .. 16c + 15 of the head: RoPE rows [cos, -sin, sin, cos]
+      const __nv_bfloat162* w2 = reinterpret_cast<const __nv_bfloat162*>(nw + 32 * c);
+#pragma unroll
+      for (int p = 0; p < 16; ++p) {
+        // pair p: box p / 8, 16-byte piece p % 8 of this row at (p % 8) ^ (row % 8)
+        const float4 e = tma_pe ? *reinterpret_cast<const float4*>(slot + (p / 8) * 4096 + lane * 128 +
+                                                                    (((p % 8) ^ (lane & 7)) * 16))
+                                : __ldg(reinterpret_cast<const float4*>(pe_lane + 64 * c) + p);
+        const float2 wp = __bfloat1622float2(w2[p]);
+        const float x0 = v[2 * p] * rms * wp.x, x1 = v[2 * p + 1] * rms * wp.y;
+        const float o0 = x0 * e.x + x1 * e.y;
+        const float o1 = x0 * e.z + x1 * e.w;
+        __half2 h2 = __floats2half2_rn(o0, o1);
+        pk[p] = *reinterpret_cast<uint32_t*>(&h2);
+      }
+      if (tma_pe) {
+        __syncwarp();  // every lane has read chunk c's rows
+        if (lane == 0) mbar_arrive(&empty[sl]);
+        if (filler && c + NS < 4 && !fill(c + NS)) return false;
+      }
+    } else {
+#pragma unroll
+      for (int p = 0; p < 16; ++p) {
+        __half2 h2 = __floats2half2_rn(v[2 * p], v[2 * p + 1]);
+        pk[p] = *reinterpret_cast<uint32_t*>(&h2);
+      }
+    }
+    // FP16 elements 32c .. 32c + 31 of the 32 rows (64 bytes each) through the
+    // staging buffer: row r's 16-byte piece k at slot k ^ ((r / 2) % 4), then
+    // eight rows per store instruction (lanes 4i .. 4i + 3: row i's pieces)
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+      *reinterpret_cast<uint4*>(obuf + lane * 64 + ((k ^ ((lane >> 1) & 3)) * 16)) =
+          make_uint4(pk[4 * k], pk[4 * k + 1], pk[4 * k + 2], pk[4 * k + 3]);
+    __syncwarp();
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int r = 8 * i + (lane >> 2), k = lane & 3;
+      const unsigned long long d = __shfl_sync(0xffffffffu, reinterpret_cast<unsigned long long>(dst), r);
+      const uint4 val = *reinterpret_cast<const uint4*>(obuf + r * 64 + ((k ^ ((r >> 1) & 3)) * 16));
+      if (d) {
+        uint4* d4 = reinterpret_cast<uint4*>(reinterpret_cast<__half*>(d) + 32 * c) + k;
+        if (q.direct)  // peer memory: plain stores
+          *d4 = val;
+        else
+          st_global_v4_hint(d4, val, pol_out);
+      }
+    }
+    __syncwarp();  // the staging buffer is read before the next chunk writes it
+  }
+  return true;
+}
+
 // ------------------------------------------------------------------ CTA pairs
 // INT8 GEMM on CTA pairs (tcgen05 cta_group::2): a cluster of two CTAs owns a
 // 256 x 256 output tile; each CTA loads 128 rows of A and 128 rows (half) of
@@ -466,38 +704,51 @@ constexpr int BM = 256, BK = 128;
 constexpr int A_BYTES = 128 * BK;                // this CTA's 128 rows of A: 16 KB
 template <int BN>
 constexpr int b_bytes() { return (BN / 2) * BK; }  // this CTA's half of B: 16 / 8 KB
-template <int BN>
-constexpr int stages() { return BN == 128 ? 6 : 5; }
+// QKV: the fused QKV projection (kEpiQkv, BN = 256) gives one stage to its
+// epilogue's RoPE-row rings
+template <int BN, bool QKV = false>
+constexpr int stages() { return QKV ? 4 : (BN == 128 ? 6 : 5); }
 template <int BN>
 constexpr int stage_bytes() { return A_BYTES + b_bytes<BN>(); }
 constexpr int EPI_WARPS = 8;
 constexpr int THREADS = 64 + 32 * EPI_WARPS;     // producer, MMA issuer, 8 epilogue warps
 constexpr int EPI_BYTES = EPI_WARPS * 2 * gemm::EPI_BUF;  // double buffered per warp: 64 KB
-template <int BN>
-constexpr int smem_bytes() { return stages<BN>() * stage_bytes<BN>() + EPI_BYTES + 1024 + 256; }
+constexpr int QKV_SLOTS = 2;  // RoPE-row ring slots (8 KB: one chunk) per TMEM lane quarter
+constexpr int QKV_OUT = 2048;  // per-warp staging of one chunk's FP16 output (32 rows x 64 bytes)
+template <bool QKV>
+constexpr int epi_bytes() { return QKV ? 4 * QKV_SLOTS * 8192 + EPI_WARPS * QKV_OUT : EPI_BYTES; }
+template <bool QKV>
+constexpr int bar_bytes() { return QKV ? 512 : 256; }
+template <int BN, bool QKV = false>
+constexpr int smem_bytes() {
+  return stages<BN, QKV>() * stage_bytes<BN>() + epi_bytes<QKV>() + 1024 + bar_bytes<QKV>();
+}
+static_assert(smem_bytes<256, true>() <= 232448, "shared memory per CTA");
 static_assert(smem_bytes<256>() <= 232448 && smem_bytes<192>() <= 232448 && smem_bytes<128>() <= 232448,
               "shared memory per CTA");
 constexpr int TMEM_COLS = 512;  // two accumulator buffers, 256 columns apart (narrower tiles use part of each)
 }  // namespace gemm2
 
-template <int BN>
+template <int BN, bool QKV>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(gemm2::THREADS, 1)
     gemm_pair_kernel(const __grid_constant__ GemmArgsDev args) {
   static_assert(BN == 256 || BN == 192 || BN == 128, "pair tile width");
+  static_assert(!QKV || BN == 256, "the fused QKV epilogue takes one head per epilogue warp");
   using gemm2::A_BYTES;
   using gemm2::BK;
   using gemm2::BM;
   using gemm2::TMEM_COLS;
   constexpr int B_BYTES = gemm2::b_bytes<BN>();
   constexpr int STAGE_BYTES = gemm2::stage_bytes<BN>();
-  constexpr int STAGES = gemm2::stages<BN>();
+  constexpr int STAGES = gemm2::stages<BN, QKV>();
+  constexpr int NS = gemm2::QKV_SLOTS;
   constexpr int TMEM_BUF = 256;  // column stride of the two accumulator buffers
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * A_BYTES;
   uint8_t* sE = smem + STAGES * STAGE_BYTES;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sE + gemm2::EPI_BYTES);  // used in the even CTA
+  uint64_t* full = reinterpret_cast<uint64_t*>(sE + gemm2::epi_bytes<QKV>());  // used in the even CTA
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;  // used in the even CTA: 8 epilogue warps x 2 CTAs
@@ -505,6 +756,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(gemm2::THREADS, 1)
   uint64_t* drain = xfull + 2 * gemm2::EPI_WARPS;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  // QKV: per TMEM lane quarter, NS "RoPE rows landed" and NS "slot read by both warps" barriers
+  uint64_t* ring_full = drain + 2;
+  uint64_t* ring_empty = ring_full + 4 * NS;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -522,14 +776,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(gemm2::THREADS, 1)
       mbar_init(&tempty[b], 2 * gemm2::EPI_WARPS);
     }
     for (int b = 0; b < 2 * gemm2::EPI_WARPS; ++b) mbar_init(&xfull[b], 1);
+    if constexpr (QKV) {
+      for (int b = 0; b < 4 * NS; ++b) {
+        mbar_init(&ring_full[b], 1);
+        mbar_init(&ring_empty[b], 2);
+      }
+    }
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
     for (int i = 0; i < args.nprob; ++i) {
       tma_prefetch_desc(&args.p[i].tmA);
       tma_prefetch_desc(&args.p[i].tmB);
-      tma_prefetch_desc(&args.p[i].tmO);
+      if constexpr (!QKV) tma_prefetch_desc(&args.p[i].tmO);  // no FP32 output tiles when fused
     }
+    if constexpr (QKV) tma_prefetch_desc(&args.tmPE);
   }
   if (warp == 1) {
     tmem_alloc_pair(tmem_slot, TMEM_COLS);
@@ -669,15 +930,32 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(gemm2::THREADS, 1)
       int pi, m0, n0;
       locate(t, pi, m0, n0);
       const int buf = local & 1;
-      ok = epilogue_tile<false>(args, args.p[pi], m0 + 128 * static_cast<int>(cr), n0, buf, (local >> 1) & 1,
-                                tmem_base, ebuf, xb, tfull, es, abort_flag, quarter, lane, HCH * half,
-                                HCH * half + HCH);
+      bool released = false;  // the fused epilogue hands the accumulator back itself
+      if constexpr (QKV) {
+        // the ring of this TMEM lane quarter (its half-0 and half-1 warps)
+        const int e0 = ew & 3;
+        ok = epilogue_qkv<NS>(args, args.p[pi], pi, m0 + 128 * static_cast<int>(cr), n0 + 128 * half,
+                              static_cast<uint32_t>(buf * TMEM_BUF + 128 * half), buf, (local >> 1) & 1, tmem_base,
+                              sE + e0 * NS * 8192, ring_full + e0 * NS, ring_empty + e0 * NS, half == 0,
+                              sE + 4 * NS * 8192 + ew * gemm2::QKV_OUT, tfull, es, tempty0 + buf * 8, abort_flag,
+                              quarter, lane);
+        released = true;
+      } else {
+        ok = epilogue_tile<false>(args, args.p[pi], m0 + 128 * static_cast<int>(cr), n0, buf, (local >> 1) & 1,
+                                  tmem_base, ebuf, xb, tfull, es, abort_flag, quarter, lane, HCH * half,
+                                  HCH * half + HCH);
+      }
       if (!ok) break;
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive_cluster(tempty0 + buf * 8);
+      if (!released) {
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(tempty0 + buf * 8);
+      }
     }
-    epilogue_drain(es, xb, lane);
+    if constexpr (QKV)  // RoPE-row copies this warp issued (the filling warps)
+      epilogue_drain(es, ring_full + (ew & 3) * NS, lane, NS);
+    else
+      epilogue_drain(es, xb, lane);
     __syncwarp();
     if (!ok && lane == 0) {
       *abort_flag = 1;
@@ -744,13 +1022,14 @@ static void fill_problem(GemmProblemDev& P, int M, int N, int K, int ldo, int& t
   P.tile_end = tiles;
 }
 
-template <int BN>
+template <int BN, bool QKV = false>
 static int launch_pair(GemmArgsDev& args, cudaStream_t stream, int num_sms) {
   static unsigned long long attr_done = 0;
-  if (smem_optin(reinterpret_cast<const void*>(gemm_pair_kernel<BN>), gemm2::smem_bytes<BN>(), &attr_done) != QI_OK)
+  constexpr int smem = gemm2::smem_bytes<BN, QKV>();
+  if (smem_optin(reinterpret_cast<const void*>(gemm_pair_kernel<BN, QKV>), smem, &attr_done) != QI_OK)
     return QI_ERR_CUDA;
   const int clusters = args.total_tiles < num_sms / 2 ? args.total_tiles : num_sms / 2;
-  gemm_pair_kernel<BN><<<2 * clusters, gemm2::THREADS, gemm2::smem_bytes<BN>(), stream>>>(args);
+  gemm_pair_kernel<BN, QKV><<<2 * clusters, gemm2::THREADS, smem, stream>>>(args);
   return cudaGetLastError() == cudaSuccess ? QI_OK : QI_ERR_CUDA;
 }
 
@@ -789,28 +1068,44 @@ static int pair_tile_width(const GemmDesc* descs, int n, int clusters) {
   return best;
 }
 
-int gemm_i8_launch(const GemmDesc* descs, int n, int epi, cudaStream_t stream, int* err_dev, int num_sms) {
-  if (n < 1 || n > 2) return QI_ERR_ARG;
-  GemmArgsDev args;
-  memset(&args, 0, sizeof(args));
-  int tiles = 0;
-  // CTA pairs (256-row tiles, eight epilogue warps) whenever there are rows
-  // enough to fill them; the one-CTA kernel for short problems
+// CTA pairs (256-row tiles, eight epilogue warps) whenever there are rows
+// enough to fill them; the one-CTA kernel for short problems.
+static bool use_pairs(const GemmDesc* descs, int n, int num_sms) {
   long long rows = 0;
   int kmin = 1 << 30;
   for (int i = 0; i < n; ++i) {
     rows += descs[i].M;
     if (descs[i].M > 0 && descs[i].K < kmin) kmin = descs[i].K;
   }
-  const bool pair = rows >= 512 && kmin >= QI_GEMM_PAIR_MIN_K && num_sms >= 2;
+  return rows >= 512 && kmin >= QI_GEMM_PAIR_MIN_K && num_sms >= 2;
+}
+
+bool gemm_qkv_fusable(const GemmDesc* descs, int n, int num_sms) {
+  if (n < 1 || n > 2) return false;
+  for (int i = 0; i < n; ++i)
+    if (descs[i].N != 3 * kDim) return false;
+  return use_pairs(descs, n, num_sms);
+}
+
+// qp: kEpiQkv's parameters (null otherwise).
+static int gemm_i8_run(const GemmDesc* descs, int n, int epi, const QkvPostArgs* qp, cudaStream_t stream,
+                       int* err_dev, int num_sms) {
+  if (n < 1 || n > 2) return QI_ERR_ARG;
+  GemmArgsDev args;
+  memset(&args, 0, sizeof(args));
+  int tiles = 0;
+  const bool fused = epi == kEpiQkv;
+  const bool pair = use_pairs(descs, n, num_sms);
+  if (fused && (!qp || !gemm_qkv_fusable(descs, n, num_sms))) return QI_ERR_UNSUPPORTED;
   const int bm = pair ? gemm2::BM : gemm::BM;
-  const int bn = pair ? pair_tile_width(descs, n, num_sms / 2) : gemm::BN;
+  // the fused epilogue needs whole heads per epilogue warp: 256-column tiles
+  const int bn = fused ? 256 : (pair ? pair_tile_width(descs, n, num_sms / 2) : gemm::BN);
   for (int i = 0; i < n; ++i) {
     const GemmDesc& d = descs[i];
     if (d.M < 0 || d.N <= 0 || d.K <= 0) return QI_ERR_ARG;
     if (d.K % 16 != 0 || d.N % 32 != 0 || d.ldo % 4 != 0) return QI_ERR_ARG;
     if ((reinterpret_cast<uintptr_t>(d.a) & 15) || (reinterpret_cast<uintptr_t>(d.w) & 15) ||
-        (reinterpret_cast<uintptr_t>(d.out) & 15) || (reinterpret_cast<uintptr_t>(d.sw) & 15))
+        (!fused && (reinterpret_cast<uintptr_t>(d.out) & 15)) || (reinterpret_cast<uintptr_t>(d.sw) & 15))
       return QI_ERR_ALIGN;
     if (epi == kEpiResidual && (d.gate == nullptr || (reinterpret_cast<uintptr_t>(d.gate) & 15)))
       return QI_ERR_ARG;
@@ -818,7 +1113,7 @@ int gemm_i8_launch(const GemmDesc* descs, int n, int epi, cudaStream_t stream, i
     if (d.M > 0) {
       if (encode_kmajor(&P.tmA, d.a, d.M, d.K, 128, false) != QI_OK) return QI_ERR_CUDA;
       if (encode_kmajor(&P.tmB, d.w, d.N, d.K, pair ? bn / 2 : gemm::BN, false) != QI_OK) return QI_ERR_CUDA;
-      if (encode_out(&P.tmO, d.out, d.M, d.N, d.ldo) != QI_OK) return QI_ERR_CUDA;
+      if (!fused && encode_out(&P.tmO, d.out, d.M, d.N, d.ldo) != QI_OK) return QI_ERR_CUDA;
     }
     P.sa = d.sa;
     P.sw = d.sw;
@@ -839,10 +1134,37 @@ int gemm_i8_launch(const GemmDesc* descs, int n, int epi, cudaStream_t stream, i
     if (l2_mode < 0 || l2_mode > 2) l2_mode = 2;
   }
   args.l2 = pair ? l2_mode : 0;
+  if (fused) {
+    if (qp->Hl <= 0 || kHeads % qp->Hl || !qp->pe || (reinterpret_cast<uintptr_t>(qp->pe) & 15)) return QI_ERR_ARG;
+    // the RoPE table, nb x [S][64][2][2] FP32: rows of 256 floats, boxes of
+    // 32 rows x 32 floats (128 bytes) in the 128-byte swizzle
+    cuuint64_t dims[2] = {256, static_cast<cuuint64_t>(qp->nb) * (qp->n_img + qp->n_txt)};
+    cuuint64_t strides[1] = {1024};
+    cuuint32_t box[2] = {32, 32};
+    cuuint32_t estr[2] = {1, 1};
+    if (qi_encode_tiled(&args.tmPE, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(qp->pe), dims, strides, box,
+                        estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return QI_ERR_CUDA;
+    args.qp = *qp;
+    args.qp.norm_dim = kHeadDim;  // run-time operands, as in qkv_post_launch
+    args.qp.eps = 1e-6f;
+    return launch_pair<256, true>(args, stream, num_sms);
+  }
   if (!pair) return launch_args<false>(args, stream, num_sms);
   if (bn == 128) return launch_pair<128>(args, stream, num_sms);
   if (bn == 192) return launch_pair<192>(args, stream, num_sms);
   return launch_pair<256>(args, stream, num_sms);
+}
+
+int gemm_i8_launch(const GemmDesc* descs, int n, int epi, cudaStream_t stream, int* err_dev, int num_sms) {
+  if (epi == kEpiQkv) return QI_ERR_ARG;  // gemm_qkv_launch
+  return gemm_i8_run(descs, n, epi, nullptr, stream, err_dev, num_sms);
+}
+
+int gemm_qkv_launch(const GemmDesc* descs, int n, const QkvPostArgs& a, cudaStream_t stream, int* err_dev,
+                    int num_sms) {
+  return gemm_i8_run(descs, n, kEpiQkv, &a, stream, err_dev, num_sms);
 }
 
 int gemm_bf16_launch(const GemmBf16Desc& d, cudaStream_t stream, int* err_dev, int num_sms) {

@@ -18,7 +18,9 @@ constexpr int kTxtDim = 3584;   // text-encoder hidden size
 constexpr int kPatchDim = 64;   // 16 channels x 2 x 2 patch
 constexpr int kOutCh = 16;
 
-enum Epilogue { kEpiStore = 0, kEpiGelu = 1, kEpiResidual = 2 };
+// kEpiQkv: the q/k RMSNorm + RoPE + FP16 head-major store of qkv_post_kernel,
+// applied to the QKV projection's accumulators (gemm_qkv_launch)
+enum Epilogue { kEpiStore = 0, kEpiGelu = 1, kEpiResidual = 2, kEpiQkv = 3 };
 
 // Raises a kernel's dynamic shared-memory limit on the current device, once
 // per device: the attribute belongs to the device, so a process that drives
@@ -170,6 +172,15 @@ struct QkvPostArgs {
   float eps;
 };
 int qkv_post_launch(const QkvPostArgs& a, cudaStream_t stream);
+// The QKV projection (descs: the image and text problems, N = 3 x 3072) with
+// qkv_post's arithmetic in its epilogue: the FP32 projection never reaches
+// HBM (a.qkv_img / a.qkv_txt are unused).  Outputs are bit-identical to
+// gemm_i8_launch(kEpiStore) followed by qkv_post_launch.  Needs the CTA-pair
+// kernel at 256-column tiles (one head per epilogue warp): gemm_qkv_fusable
+// says whether the shapes get it; otherwise use the two launches.
+bool gemm_qkv_fusable(const GemmDesc* descs, int n, int num_sms);
+int gemm_qkv_launch(const GemmDesc* descs, int n, const QkvPostArgs& a, cudaStream_t stream, int* err_dev,
+                    int num_sms);
 
 // ---------------------------------------------------------------- attention
 // Longest joint sequence the attention kernel takes (its K scales of up to

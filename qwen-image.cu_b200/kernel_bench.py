@@ -2,7 +2,7 @@
 CUDA events on the launching stream).  Also the target of the ncu captures
 summarised in profiles/.
 
-    python qwen-image.cu_b200/kernel_bench.py [--which gemm,attn,quant,spectrum,peaks] [--iters N] [--config c4|c2]
+    python qwen-image.cu_b200/kernel_bench.py [--which gemm,attn,quant,spectrum,qkv,peaks] [--iters N] [--config c4|c2]
                                               [--gpus 1|2|4|8]
 
 GEMM shapes are those of one CFG-batched C4 forward (M = 2 x 6889 image +
@@ -15,6 +15,8 @@ Quantizers: LayerNorm-modulate + FWHT-1024 (K 3072), the attention output
 (FP16, K 3072) and the MLP hidden (FWHT-4096, K 12288) at the C4 rows.
 `spectrum`: a skipped Spectrum step at C4 (prediction from 28 stored states,
 then the output head).
+`qkv`: the fused QKV projection (q/k RMSNorm + RoPE in the GEMM epilogue)
+against the FP32 projection followed by qk_norm_rope, at C4 rows.
 `peaks`: the dense tensor-core rates of this GPU through the libraries
 (torch._int_mm INT8 -> INT32, torch.matmul FP16 and BF16 at 8192^3), as a
 burst (best of 10) and sustained (back to back for 4 s); the roofline
@@ -140,6 +142,42 @@ def bench_spectrum(iters, res, K=28):
     ctx.close()
 
 
+def bench_qkv(iters, res, n_gpus=1):
+    """The block's QKV stage at C4: the fused projection (q/k RMSNorm + RoPE
+    + FP16 head-major store in the GEMM epilogue) against the two-launch form
+    (FP32 projection, then qk_norm_rope), and the projection alone.  The
+    fused launches come first (an ncu capture of the first CTA-pair GEMM
+    launches sees them)."""
+    nb, P = shard(n_gpus)
+    n_img, n_txt = 6889 // P, 256 // P
+    rows_i, rows_t = nb * n_img, nb * n_txt
+
+    def stream(rows, tag):
+        x = Q.synth((rows, 3072), 50 + len(tag), 1.0)
+        w = Q.synth((9216, 3072), 60 + len(tag), 0.02, dtype=torch.bfloat16)
+        b = Q.synth((9216,), 70 + len(tag), 0.02, dtype=torch.bfloat16)
+        return Q.fwht_quantize(x), Q.quantize_weight(w) + (b,)
+
+    act_i, w_i = stream(rows_i, "img")
+    act_t, w_t = stream(rows_t, "tx")
+    norms = Q.synth((4, 128), 80, 0.1, 1.0, dtype=torch.bfloat16)
+    pe = torch.from_numpy(Q.rope_table(166, 166, 256)).cuda()
+    pe = torch.stack([pe[: n_img + n_txt]] * nb).contiguous()
+    ms_f = time_it(lambda: Q.qkv_norm_rope_i8(act_i, act_t, w_i, w_t, norms, pe, nb), iters)
+    qi = torch.empty(rows_i, 9216, device="cuda")
+    qt = torch.empty(rows_t, 9216, device="cuda")
+
+    def proj():
+        Q.linear_i8(act_i[0], act_i[1], w_i[0], w_i[1], w_i[2], out=qi)
+        Q.linear_i8(act_t[0], act_t[1], w_t[0], w_t[1], w_t[2], out=qt)
+
+    ms_p = time_it(proj, iters)
+    ms_s = time_it(lambda: (proj(), Q.qk_norm_rope(qi, qt, norms, pe, nb)), iters)
+    flops = 2.0 * (rows_i + rows_t) * 9216 * 3072
+    res["qkv"] = {"rows": rows_i + rows_t, "fused_ms": round(ms_f, 4), "projection_ms": round(ms_p, 4),
+                  "two_launch_ms": round(ms_s, 4), "fused_tops": round(flops / (ms_f * 1e-3) / 1e12, 1)}
+
+
 def bench_peaks(res, seconds=4.0):
     n = 8192
     flops = 2.0 * n ** 3
@@ -188,6 +226,8 @@ def main():
         bench_quant(a.iters, res)
     if "spectrum" in w:
         bench_spectrum(a.iters, res)
+    if "qkv" in w:
+        bench_qkv(a.iters, res, a.gpus)
     if "peaks" in w:
         bench_peaks(res)
     print(json.dumps(res))

@@ -87,6 +87,7 @@ def lib():
             "qi_rms_norm": ([vp, vp, vp, i, i, f, vp], i),
             "qi_layer_norm_modulate_quantize": ([vp, vp, vp, i, i, f, vp, vp, vp], i),
             "qi_qk_norm_rope": ([vp, vp, vp, vp, i, i, i, vp, vp], i),
+            "qi_qkv_norm_rope_i8": ([vp] * 12 + [i, i, i, vp, vp], i),
             "qi_ctx_create": ([i, ctypes.POINTER(vp)], i),
             "qi_ctx_destroy": ([vp], i),
             "qi_ctx_check": ([vp], i),
@@ -105,6 +106,7 @@ def lib():
             "qi_ctx_set_comm": ([vp, vp, i, i], i),
             "qi_ctx_set_comm_timeout": ([vp, i], i),
             "qi_ctx_set_attention_fp8pv": ([vp, i], i),
+            "qi_ctx_set_fused_qkv_epilogue": ([vp, i], i),
             "qi_ctx_sync": ([vp, vp, i], i),
             "qi_exchange_plan": ([i, i, i, i, i, i, vp, vp, vp, vp], i),
             "qi_rope_table": ([i, i, i, vp], i),
@@ -236,6 +238,22 @@ def qk_norm_rope(qkv_img, qkv_txt, norms, pe, nb=1):
     n_txt = qkv_txt.shape[0] // nb
     out = torch.empty(3, nb * HEADS, n_img + n_txt, HEAD_DIM, dtype=torch.float16, device=qkv_img.device)
     check(lib().qi_qk_norm_rope(_p(qkv_img), _p(qkv_txt), _p(norms), _p(pe), nb, n_img, n_txt, _p(out), _stream()))
+    return out
+
+
+def qkv_norm_rope_i8(act_img, act_txt, w_img, w_txt, norms, pe, nb=1):
+    """The fused QKV projection: act_* = (codes [nb*n, 3072] INT8, scales
+    [nb*n]); w_* = (codes [9216, 3072], scales [9216], BF16 bias or None).
+    Returns FP16 [3, nb*24, S, 128] (q, k, v), the bits of linear_i8 +
+    qk_norm_rope."""
+    n_img = act_img[0].shape[0] // nb
+    n_txt = act_txt[0].shape[0] // nb
+    out = torch.empty(3, nb * HEADS, n_img + n_txt, HEAD_DIM, dtype=torch.float16, device=act_img[0].device)
+    bi = _p(w_img[2]) if w_img[2] is not None else None
+    bt = _p(w_txt[2]) if w_txt[2] is not None else None
+    check(lib().qi_qkv_norm_rope_i8(_p(act_img[0]), _p(act_img[1]), _p(act_txt[0]), _p(act_txt[1]), _p(w_img[0]),
+                                    _p(w_img[1]), bi, _p(w_txt[0]), _p(w_txt[1]), bt, _p(norms), _p(pe), nb, n_img,
+                                    n_txt, _p(out), _stream()))
     return out
 
 
@@ -371,6 +389,11 @@ class Context:
         """Every forward copies its final image hidden state [nb*n_img, 3072]
         FP32 into `hidden` (a device tensor; None stops)."""
         check(lib().qi_ctx_set_hidden_capture(self.h, _p(hidden) if hidden is not None else None))
+
+    def set_fused_qkv_epilogue(self, enable):
+        """q/k RMSNorm + RoPE in the QKV GEMM's epilogue (True, the default)
+        or as a separate kernel after an FP32 projection; same bits."""
+        check(lib().qi_ctx_set_fused_qkv_epilogue(self.h, int(bool(enable))))
 
     def close(self):
         if self.h:

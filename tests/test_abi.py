@@ -92,6 +92,8 @@ def test_null_handles_and_buffers_are_rejected_without_device():
     assert L.qi_cfg_euler_step(null, null, null, 4.0, 0.5, 0.4, 8, 8, null, null) == 1
     assert L.qi_layer_norm_modulate_quantize(null, null, null, 4, 3072, 1e-6, null, null, null) == 1
     assert L.qi_qk_norm_rope(null, null, null, null, 1, 16, 8, null, null) == 1
+    assert L.qi_qkv_norm_rope_i8(*([null] * 12), 1, 16, 8, null, null) == 1
+    assert L.qi_ctx_set_fused_qkv_epilogue(null, 1) == 1
     assert L.qi_alloc_count() >= 0
 
 
