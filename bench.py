@@ -79,11 +79,13 @@ def flops_per_forward(n_img, n_txt, blocks=BLOCKS):
 class ClockSampler:
     """SM clocks and clock-event (throttle) reasons of this rank's GPU, sampled
     every 50 ms through NVML on a host thread while the timed region runs
-    (read-only: nothing is set).  Sampling every 10 ms slowed the 8-GPU step,
-    whose host enqueue has the least slack (55.2 ms/step timed with sampling
-    against 44.3 ms for the same step timed without).  The device is found by UUID, so the index
-    under CUDA_VISIBLE_DEVICES does not matter.  Falls back to `nvidia-smi -lms
-    200` if NVML is unavailable."""
+    (read-only: nothing is set).  NVML is initialised on entry, which takes a
+    different time on each rank: the ranks' barrier that opens the timed
+    region comes after it (with NVML started after the barrier, a 2-GPU step
+    timed 0.120 s against 0.099 s for the same step untimed by it, the start-up
+    skew showing up in the max over ranks).  The device is found by UUID, so
+    the index under CUDA_VISIBLE_DEVICES does not matter.  Falls back to
+    `nvidia-smi -lms 200` if NVML is unavailable."""
 
     NAMES = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
 
@@ -269,9 +271,11 @@ def run_ours(args):
     for i in range(args.warmup):
         step(i)
     ctx.check()
-    barrier(world)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clk:
+        # NVML starts up before the barrier, so the ranks enter the timed
+        # region together (its start-up time differs between ranks)
+        barrier(world)
         e0.record(stream)
         for i in range(args.steps):
             step(args.warmup + i, keep=(i == 0))
