@@ -807,7 +807,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(gemm2::THREADS, 1)
     const GemmProblemDev& P = args.p[pi];
     int lt = t - P.tile_begin;
     m0 = (lt / P.tiles_n) * BM;
-    n0 = (lt % P.tiles_n) * BN;
+    int nt = lt % P.tiles_n;
+    // QKV: a row block's column tiles in the order Q, K, V, Q, K, V, ...  A
+    // cluster takes every (clusters)-th tile, so its tiles then mix the q/k
+    // heads' longer epilogue with the V heads' shorter one instead of running
+    // a dozen q/k tiles back to back; each tile's work is unchanged.
+    if constexpr (QKV) nt = (nt % 3) * (P.tiles_n / 3) + nt / 3;
+    n0 = nt * BN;
   };
 
   if (warp == 0) {
