@@ -1,8 +1,8 @@
 """Model-level parity: the product's forward (qi_forward through the C ABI)
 against the reference's own transformer_forward (Sage path) on identical
 weights and inputs, against the CPU oracle, and CFG batching against two
-single forwards.  Tolerance: cosine >= 0.999 and
-normwise max relative error max|a-b| / max|b| <= 2e-2."""
+single forwards.  Tolerance: cosine >= 0.999 and normwise max relative
+error max|a-b| / max|b| <= 2e-2."""
 import json
 import os
 import struct

@@ -163,7 +163,7 @@ def test_sage_quantizers_bitexact(BH, S):
             assert torch.equal(a, b), n
 
 
-# (2, 16896): the joint sequence of BASELINE config 5 (2048x2048)
+# (2, 16896): the joint sequence of a 2048x2048 image (16384 image + 512 text tokens)
 @pytest.mark.parametrize("BH,S", [(2, 200), (1, 77), (2, 384), (4, 1088), (2, 4352), (1, 129), (1, 1), (2, 16896)])
 def test_sage_attention_matches_reference_and_exact(BH, S):
     q = Q.synth((BH, S, 128), Q.seed_for(14, f"q_{BH}_{S}"), 1.0).half()
