@@ -932,25 +932,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(gemm2::THREADS, 1)
     EpiState es;
     int local = 0;
     bool ok = true;
-    // Residual epilogue: this warp's 32 rows x (BN / 2) columns of a tile's
-    // residual are brought into L2 one tile ahead, so the per-chunk TMA loads
-    // of x find them there instead of waiting on HBM.
-    auto prefetch_residual = [&](int t) {
-      if (args.epi != kEpiResidual || lane != 0 || t >= args.total_tiles) return;
-      int pi, m0, n0;
-      locate(t, pi, m0, n0);
-      const GemmProblemDev& P = args.p[pi];
-      const int r0 = m0 + 128 * static_cast<int>(cr) + 32 * quarter;
-      if (r0 >= P.M) return;
-      for (int c = HCH * half; c < HCH * half + HCH && n0 + 32 * c < P.N; ++c)
-        tma_prefetch_l2_2d(&P.tmO, n0 + 32 * c, r0);
-    };
-    if constexpr (!QKV) prefetch_residual(cluster);
     for (int t = cluster; t < args.total_tiles && ok; t += nclusters, ++local) {
       int pi, m0, n0;
       locate(t, pi, m0, n0);
       const int buf = local & 1;
-      if constexpr (!QKV) prefetch_residual(t + nclusters);
       bool released = false;  // the fused epilogue hands the accumulator back itself
       if constexpr (QKV) {
         // the ring of this TMEM lane quarter (its half-0 and half-1 warps)
