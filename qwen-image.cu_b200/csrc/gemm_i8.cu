@@ -462,9 +462,9 @@ __global__ void __launch_bounds__(gemm::THREADS, 1) gemm_kernel(const __grid_con
 //     rsqrt(ss / 128 + eps), x * rms * w and RoPE on interleaved pairs
 //     (rope_apply_fp32_to_fp16_kernel, :1935-1963);
 //   * V: only rounded to FP16.
-// A first pass over TMEM gives the sum of squares. A second pass recomputes
-// the same dequantised values chunk by chunk, so at most one 32-column chunk
-// sits in registers.  The RoPE rows of the 32 rows (16 pairs x 16 bytes per
+// A first pass over TMEM dequantises each 32-column chunk, writes the FP32
+// values back over its accumulators and sums their squares; a second pass
+// reads them back chunk by chunk, so at most one chunk sits in registers.  The RoPE rows of the 32 rows (16 pairs x 16 bytes per
 // row and chunk) come by TMA, as two 32-row x 128-byte boxes with 128-byte
 // swizzle, into an NS-slot ring (8 KB per slot) shared by the two warps of
 // this TMEM lane quarter (the same 32 rows, the tile's two heads): full[s]
@@ -595,6 +595,10 @@ __device__ __forceinline__ bool epilogue_qkv(const GemmArgsDev& args, const Gemm
       float v[32];
       load_chunk(c, acc);
       dequant(acc, c0 + 32 * c, v);
+      // the dequantised values replace the chunk's accumulators, for pass 2
+#pragma unroll
+      for (int i = 0; i < 32; ++i) acc[i] = __float_as_uint(v[i]);
+      tmem_st32(taddr + 32 * c, acc);
 #pragma unroll
       for (int i = 0; i < 32; ++i) v[i] = __fmul_rn(v[i], v[i]);
 #pragma unroll
@@ -609,6 +613,7 @@ __device__ __forceinline__ bool epilogue_qkv(const GemmArgsDev& args, const Gemm
     }
     const float ss = __fadd_rn(__fadd_rn(ws0, ws2), __fadd_rn(ws1, ws3));
     rms = rsqrtf(ss / q.norm_dim + q.eps);
+    tmem_st_wait();  // pass 2 reads the stored values back
   }
   const float* pe_lane = q.pe + (valid ? (static_cast<long long>(b) * S + pos) * 256 : 0);
 #pragma unroll 1
@@ -617,7 +622,12 @@ __device__ __forceinline__ bool epilogue_qkv(const GemmArgsDev& args, const Gemm
     float v[32];
     load_chunk(c, acc);
     if (c == 3) release();
-    dequant(acc, c0 + 32 * c, v);
+    if (which < 2) {  // dequantised by pass 1
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(acc[i]);
+    } else {
+      dequant(acc, c0 + 32 * c, v);
+    }
     uint32_t pk[16];
     if (which < 2) {
       const int sl = c % NS;
