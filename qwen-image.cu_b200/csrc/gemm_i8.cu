@@ -667,7 +667,8 @@ __device__ __forceinline__ bool epilogue_qkv(const GemmArgsDev& args, const Gemm
     }
     // FP16 elements 32c .. 32c + 31 of the 32 rows (64 bytes each) through the
     // staging buffer: row r's 16-byte piece k at slot k ^ ((r / 2) % 4), then
-    // eight rows per store instruction (lanes 4i .. 4i + 3: row i's pieces)
+    // eight rows per store instruction (in instruction i, lanes 4j .. 4j + 3
+    // write the four pieces of row 8i + j)
 #pragma unroll
     for (int k = 0; k < 4; ++k)
       *reinterpret_cast<uint4*>(obuf + lane * 64 + ((k ^ ((lane >> 1) & 3)) * 16)) =
